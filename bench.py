@@ -1,0 +1,414 @@
+"""Benchmark of the B200 donor-reuse hot path (one JSON line on rank 0).
+
+Workload (``configs[1]`` of the baseline): RoPE-corrected donor-KV inject for
+8 requests × 16384-token donors, 28 layers × 4 KV heads × 128 dims, bf16, 85 %
+of tokens reused through 256-token chunks shifted by per-chunk deltas
+U[-4096, 4096] (clamped so donor rows exist), 15 % recompute positions left
+untouched, paged cache with block size 16 and a seeded random block table.
+One step = one launch injecting every layer, head and request.
+
+Metric: GB/s of algorithmic bytes (K and V rows read and written, positions and
+block tables read once).  Multi-GPU: one process per GPU, each owning 4 KV
+heads of its own tensor-parallel shard (weak scaling, no collective on the
+inject path); value = all ranks' bytes ÷ the slowest rank's time.
+
+``--impl reference`` times the CPU restatement of the reference's inject
+(``oracle/``) on a bounded sample of the same workload on the host cores.
+
+Usage: python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+# c2 geometry
+N_REQ, SEQ, N_LAYERS, N_KV_HEADS, HEAD_DIM, BLOCK = 8, 16384, 28, 4, 128, 16
+CHUNK, MAX_DELTA, RECOMPUTE_FRAC, ROPE_THETA = 256, 4096, 0.15, 1e6
+SEED = 20261201
+
+
+def peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]),
+                "bf16_tflops_sustained": float(d.get("bf16_tflops_sustained", d["bf16_tflops"])),
+                "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+# ---------------------------------------------------------------------------
+# Workload generation (seeded, host side: pair lists and block tables)
+# ---------------------------------------------------------------------------
+def make_request_plan(rng: np.random.Generator, seq: int = SEQ):
+    """Donor/target positions of one request: 256-token chunks shifted by a
+    per-chunk delta, 15 % of target positions marked for recompute."""
+    n_chunks = seq // CHUNK
+    tgt_all, don_all = [], []
+    for c in range(n_chunks):
+        t0 = c * CHUNK
+        delta = int(rng.integers(-MAX_DELTA, MAX_DELTA + 1))
+        delta = min(max(delta, t0 - (seq - CHUNK)), t0)  # donor chunk inside [0, seq)
+        t = np.arange(t0, t0 + CHUNK)
+        tgt_all.append(t)
+        don_all.append(t - delta)
+    tgt = np.concatenate(tgt_all)
+    don = np.concatenate(don_all)
+    recompute = rng.permutation(seq)[: int(round(RECOMPUTE_FRAC * seq))]
+    keep = np.ones(seq, bool)
+    keep[recompute] = False
+    return don[keep].astype(np.int32), tgt[keep].astype(np.int32), np.sort(recompute)
+
+
+def make_block_tables(rng: np.random.Generator, n_req: int, seq: int, pool: int):
+    per = seq // BLOCK
+    perm = rng.permutation(pool)[: n_req * per]
+    return [perm[r * per : (r + 1) * per].astype(np.int32) for r in range(n_req)]
+
+
+def algorithmic_bytes(n_pairs: int, n_layers: int, n_heads: int, head_dim: int, elt: int, n_blocks: int) -> int:
+    """K and V rows read once and written once, positions (2 × int32) and
+    block-table entries (int32) read once."""
+    return n_pairs * n_layers * n_heads * head_dim * elt * 4 + 8 * n_pairs + 4 * n_blocks
+
+
+# ---------------------------------------------------------------------------
+# Clock sampling during the timed region
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu_index = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+        self._t = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100",
+                 "-i", str(self.gpu_index)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (OSError, ValueError):
+            self.proc = None
+            return
+        self._t = threading.Thread(target=self._read, daemon=True)
+        self._t.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self._t.join(timeout=2)
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# Distributed plumbing
+# ---------------------------------------------------------------------------
+def dist_setup(n_gpus: int):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(local)
+    return world, rank, local
+
+
+def barrier(world: int):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ---------------------------------------------------------------------------
+# Our implementation
+# ---------------------------------------------------------------------------
+def run_ours(args, world, rank, local) -> dict | None:
+    from semblend_b200 import _lib
+    from semblend_b200 import rope_correction as rc
+
+    dev = torch.device("cuda", local)
+    rng = np.random.default_rng(SEED + rank)
+    pool = int(N_REQ * (SEQ // BLOCK) * 1.25)
+    plans = [make_request_plan(rng) for _ in range(N_REQ)]
+    tables = make_block_tables(rng, N_REQ, SEQ, pool)
+    n_pairs = sum(p[0].shape[0] for p in plans)
+
+    gen = torch.Generator(device=dev).manual_seed(SEED + rank)
+    cache = torch.empty(N_LAYERS, pool, 2, N_KV_HEADS, BLOCK, HEAD_DIM, dtype=torch.bfloat16, device=dev)
+    cache.normal_(generator=gen)
+    donors = []
+    for _ in range(N_REQ):
+        dk = torch.empty(N_LAYERS, 2, N_KV_HEADS, SEQ, HEAD_DIM, dtype=torch.bfloat16, device=dev)
+        dk.normal_(generator=gen)
+        donors.append(dk)
+
+    # host-side (pinned) step inputs: positions and block tables
+    host_pos = [torch.from_numpy(np.stack([d, t])).pin_memory() for d, t, _ in plans]
+    host_bt = [torch.from_numpy(b).pin_memory() for b in tables]
+    dev_pos = [h.to(dev) for h in host_pos]
+    dev_bt = [h.to(dev) for h in host_bt]
+    injections = [rc.DonorInjection(donors[r], dev_bt[r], dev_pos[r][0], dev_pos[r][1]) for r in range(N_REQ)]
+    err = _lib.err_counter(dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        rc.inject_donors(cache, injections, rope_base=ROPE_THETA, rotary_style="neox")
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+
+    # --- device-resident timed region ---
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    clocks = ClockSampler(local)
+    clocks.start()
+    barrier(world)
+    torch.cuda.synchronize(dev)
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for i in range(args.steps):
+        starts[i].record(stream)
+        step()
+        ends[i].record(stream)
+    t1.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    clk = clocks.stop()
+    total_ms = t0.elapsed_time(t1)
+    kernel_ms = statistics.mean(s.elapsed_time(e) for s, e in zip(starts, ends))
+    total_ms = max_over_ranks(total_ms, world)
+    kernel_ms_max = max_over_ranks(kernel_ms, world)
+
+    # --- end to end through the public API with host buffers ---
+    h2d = sum(h.numel() * h.element_size() for h in host_pos) + sum(h.numel() * h.element_size() for h in host_bt)
+    status = torch.empty(1, dtype=torch.int64).pin_memory()
+
+    def e2e_step():
+        for r in range(N_REQ):
+            dev_pos[r].copy_(host_pos[r], non_blocking=True)
+            dev_bt[r].copy_(host_bt[r], non_blocking=True)
+        rc.inject_donors(cache, injections, rope_base=ROPE_THETA, rotary_style="neox")
+        status.copy_(err, non_blocking=True)
+
+    for _ in range(max(3, args.warmup // 2)):
+        e2e_step()
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1), world)
+    skipped = int(status.item())
+
+    elt = 2
+    per_rank_bytes = algorithmic_bytes(n_pairs, N_LAYERS, N_KV_HEADS, HEAD_DIM, elt, N_REQ * (SEQ // BLOCK))
+    total_bytes = per_rank_bytes * world  # every rank moves the same amount (weak scaling)
+    ms_per_step = total_ms / args.steps
+    value = total_bytes / (ms_per_step * 1e-3) / 1e9
+    e2e_value = total_bytes / (e2e_ms / args.steps * 1e-3) / 1e9
+    pk = peaks()
+    achieved = per_rank_bytes / (kernel_ms_max * 1e-3) / 1e9
+    del cache, donors
+    torch.cuda.empty_cache()
+    if rank != 0:
+        return None
+    traffic = None
+    tf = ROOT / "profiles" / "inject_c2_traffic.json"
+    if tf.exists():
+        traffic = json.loads(tf.read_text()).get("bytes_per_launch")
+    return {
+        "metric": "RoPE-corrected KV inject GB/s",
+        "value": round(value, 2),
+        "unit": "GB/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms_per_step, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) K/V, seeded chunk deltas, recompute set and block tables)",
+        "config": {
+            "workload": "c2: 8 req x 16384 tok donors, 28 L x 4 KV heads x 128, bf16, 85% reuse via 256-tok "
+                        "chunks (delta U[-4096,4096]), 15% recompute untouched, block 16, neox RoPE theta 1e6",
+            "pairs_per_rank": n_pairs,
+            "parallelism": f"tp{world} by kv-heads (4 kv-heads per rank, weak scaling, no collective)",
+            "l2": "inputs larger than L2 (7.3 GB donors + 9.2 GB cache per rank)",
+            "seed": SEED,
+        },
+        "roofline": {
+            "bound": "hbm",
+            "achieved": round(achieved, 1),
+            "peak": pk["hbm_gbs"],
+            "unit": "GB/s",
+            "frac": round(achieved / pk["hbm_gbs"], 4),
+            "peak_source": pk["source"],
+            "traffic": traffic,
+            "algorithmic_bytes_per_launch": per_rank_bytes,
+            "kernel": "inject_kernel<bf16, 8>",
+        },
+        "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": 8, "api": "semblend_b200.rope_correction.inject_donors",
+                "skipped_pairs": skipped},
+        "gpu_launches": args.steps,
+        "clocks": clk,
+    }
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline (oracle port of the reference's inject) — bounded sample
+# ---------------------------------------------------------------------------
+def cpu_baseline(steps: int = 1) -> dict:
+    from oracle import rope as orope
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    rng = np.random.default_rng(SEED)
+    d, t, _ = make_request_plan(rng)
+    bt = make_block_tables(rng, 1, SEQ, SEQ // BLOCK)[0]
+    g = torch.Generator().manual_seed(SEED)
+    donor = torch.randn(2, N_KV_HEADS, SEQ, HEAD_DIM, generator=g).to(torch.bfloat16)
+    cache = torch.randn(SEQ // BLOCK, 2, N_KV_HEADS, BLOCK, HEAD_DIM, generator=g).to(torch.bfloat16)
+    dt, tt, btt = torch.from_numpy(d), torch.from_numpy(t), torch.from_numpy(bt)
+    orope.rope_correct_scatter_paged(cache, donor, btt, dt[:64], tt[:64], ROPE_THETA, "neox")  # warm-up
+    times = []
+    for _ in range(steps):
+        s = time.perf_counter()
+        orope.rope_correct_scatter_paged(cache, donor, btt, dt, tt, ROPE_THETA, "neox")
+        times.append(time.perf_counter() - s)
+    sec = statistics.median(times)
+    nbytes = algorithmic_bytes(d.shape[0], 1, N_KV_HEADS, HEAD_DIM, 2, SEQ // BLOCK)
+    return {"value": round(nbytes / sec / 1e9, 4), "unit": "GB/s", "cores": torch.get_num_threads(),
+            "kind": "port",
+            "sample": f"1 request x 1 layer of c2 ({d.shape[0]} pairs x 4 heads, bf16), "
+                      f"oracle.rope.rope_correct_scatter_paged, median of {steps}; GB/s scales to the full step "
+                      "by bytes (28 layers x 8 requests)",
+            "seconds_per_sample": round(sec, 4)}
+
+
+def run_reference(args, world, rank) -> dict | None:
+    if rank != 0:
+        return None
+    steps = max(1, min(args.steps, 5))
+    cb = cpu_baseline(steps)
+    return {
+        "impl": "reference",
+        "metric": "RoPE-corrected KV inject GB/s",
+        "value": cb["value"],
+        "unit": "GB/s",
+        "n_gpus": world,
+        "steps": steps,
+        "warmup": 1,
+        "ms_per_step": round(cb["seconds_per_sample"] * 1e3, 3),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (seeded)",
+        "config": {"workload": "c2 bounded sample on host cores (see cpu_baseline.sample)"},
+        "cpu_baseline": cb,
+        "e2e": {"value": cb["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def main() -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=300)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    if args.impl == "reference":
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        rank = int(os.environ.get("RANK", "0"))
+        line = run_reference(args, world, rank)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+        return 0
+    world, rank, local = dist_setup(args.gpus)
+    line = run_ours(args, world, rank, local)
+    if line is not None:
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(steps=3)
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,186 @@
+/*
+ * semblend_b200 — C ABI of the B200-native donor-reuse hot path.
+ *
+ * Every entry point takes plain device pointers, element strides and sizes,
+ * and an opaque CUDA stream handle (a cudaStream_t passed as void*).  Nothing
+ * here allocates device memory: scratch space is passed in by the caller and
+ * sized by the matching *_workspace_bytes() query.  Calls are asynchronous on
+ * the given stream.  A return value of SB_OK means the work was enqueued;
+ * negative values mean the arguments were rejected and nothing was launched.
+ *
+ * The reference implementation (SemBlend 0.3.2) is pure Python + Triton; the
+ * interfaces each entry point replaces are cited by file:line of that project.
+ */
+#ifndef SEMBLEND_B200_H
+#define SEMBLEND_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SB_API __attribute__((visibility("default")))
+
+/* ------------------------------------------------------------------------ */
+/* Status codes                                                              */
+/* ------------------------------------------------------------------------ */
+#define SB_OK 0
+#define SB_ERR_INVALID_ARGUMENT (-1)
+#define SB_ERR_UNSUPPORTED (-2)
+#define SB_ERR_CUDA (-3)
+#define SB_ERR_WORKSPACE_TOO_SMALL (-4)
+#define SB_ERR_TOO_LARGE (-5)
+
+/* Element types. */
+#define SB_DTYPE_F32 0
+#define SB_DTYPE_F16 1
+#define SB_DTYPE_BF16 2
+
+/* Index types (positions, block tables). */
+#define SB_INDEX_I32 0
+#define SB_INDEX_I64 1
+
+/* RoPE pairing: interleaved pairs (2i, 2i+1) as the reference rotates them,
+ * or neox half-rotation pairs (i, i + D/2). */
+#define SB_ROTARY_INTERLEAVED 0
+#define SB_ROTARY_NEOX 1
+
+/* Angle applied to K rows. */
+#define SB_ANGLE_NONE 0  /* plain copy                                     */
+#define SB_ANGLE_DELTA 1 /* rotate by (dst_pos - src_pos) * inv_freq          */
+#define SB_ANGLE_NOPE 2  /* rotate by -src_pos, then by +dst_pos (two steps)  */
+#define SB_ANGLE_CONST 3 /* rotate by const_delta * inv_freq                  */
+
+/* Which position selects a source / destination row. */
+#define SB_ROW_AT_SRC_POS 0
+#define SB_ROW_AT_DST_POS 1
+#define SB_ROW_AT_PAIR 2 /* row index = pair index (a per-pair snapshot)     */
+
+/* Row selection: bit 0 = K rows (kv index 0), bit 1 = V rows (kv index 1). */
+#define SB_KV_K 1
+#define SB_KV_V 2
+#define SB_KV_BOTH 3
+
+/* Maximum descriptors a single sb_inject call accepts. */
+#define SB_MAX_INJECT_DESC 64
+
+/* ------------------------------------------------------------------------ */
+/* Row addressing                                                           */
+/* ------------------------------------------------------------------------ */
+/* A set of KV rows of head_dim elements.  The element (layer l, kv, head h,
+ * position p, dim d) lives at
+ *     layer_base(l) + kv*stride_kv + h*stride_head + row_offset(p) + d*stride_dim
+ * (element units), where layer_base(l) = layer_ptrs[l] if layer_ptrs != NULL
+ * (a DEVICE array of n_layers byte addresses, each 16-byte aligned) else
+ * base + l*stride_layer.
+ *
+ * Flat rows (block_table == NULL): row_offset(p) = p*stride_pos and positions
+ * p outside [0, n_logical) are out of range.
+ * Paged rows: lb = p / block_size must lie in [0, n_logical) (the block-table
+ * length), phys = block_table[lb] must lie in [0, n_physical), and
+ * row_offset(p) = phys*stride_block + (p % block_size)*stride_pos.
+ * These strides cover the reference layout [nb, 2, H, bs, D], vLLM's
+ * FlashAttention layout [2, nb, bs, H, D] and TRT-LLM's [nb, 2, bs, H, D]. */
+typedef struct sb_rows {
+  void *base;
+  const uint64_t *layer_ptrs;
+  int64_t stride_layer, stride_block, stride_kv, stride_head, stride_pos,
+      stride_dim;
+  const void *block_table;
+  int64_t n_logical;
+  int64_t n_physical;
+  int32_t block_size;
+  int32_t block_table_dtype; /* SB_INDEX_I32 or SB_INDEX_I64 */
+} sb_rows;
+
+/* One independent inject job: a pair list moving rows from src to dst. */
+typedef struct sb_inject_desc {
+  sb_rows src;
+  sb_rows dst;
+  const void *src_pos; /* device, n_pairs entries */
+  const void *dst_pos; /* device, n_pairs entries */
+  int64_t n_pairs;
+  int32_t pos_dtype; /* SB_INDEX_I32 or SB_INDEX_I64 */
+  int32_t src_row;   /* SB_ROW_AT_SRC_POS or SB_ROW_AT_PAIR */
+  int32_t dst_row;   /* SB_ROW_AT_DST_POS, SB_ROW_AT_SRC_POS or SB_ROW_AT_PAIR */
+  int32_t flags;     /* SB_DESC_* bits */
+} sb_inject_desc;
+
+/* Also require src_pos to address a valid row of dst (used when the source
+ * rows were snapshotted out of dst and are read back by pair index). */
+#define SB_DESC_CHECK_SRC_IN_DST 1
+
+/* Parameters shared by every descriptor of one call. */
+typedef struct sb_inject_params {
+  int32_t n_layers;
+  int32_t n_heads;
+  int32_t head_dim;     /* even, <= 512 */
+  int32_t dtype;        /* element type of both src and dst rows */
+  int32_t rotary_style; /* SB_ROTARY_* */
+  int32_t k_angle;      /* SB_ANGLE_* for K rows; V rows are always copied */
+  int32_t kv_select;    /* SB_KV_* */
+  int32_t reserved;
+  int64_t const_delta;    /* for SB_ANGLE_CONST */
+  const float *inv_freq;  /* device, head_dim/2 floats; unused for SB_ANGLE_NONE */
+} sb_inject_params;
+
+/* Fused donor-KV gather + RoPE correction of K + scatter (paged or flat).
+ *
+ * For each descriptor, pair i and every (layer, kv, head) row selected by
+ * kv_select: read the source row, rotate it in fp32 when it is a K row and
+ * k_angle != SB_ANGLE_NONE (rounding each product and sum separately, as the
+ * reference's torch expressions do), and store it in the element type at the
+ * destination row.  A pair whose source or destination row is out of range is
+ * skipped and counted once in *err_counter (a device uint64, may be NULL),
+ * the way the reference's GPU kernels skip them.  Pairs of one call must not
+ * write the same destination row twice, and destination rows must not be the
+ * source rows of other pairs (use sb_permute_paged for in-place permutations).
+ *
+ * Replaces:
+ *   rope_correct_scatter_paged   semblend_core/rope_correction.py:193-282
+ *   scatter_donor_kv             semblend_core/triton_kernels.py:132-191
+ *   scatter_donor_kv_paged       semblend_core/triton_kernels.py:279-356
+ *   rope_correct_k               semblend_core/rope_correction.py:336-399
+ *   apply_rope_delta_inplace     semblend_core/rope_correction.py:699-783
+ * (the Triton kernels at triton_kernels.py:60-129, :201-276 and
+ *  rope_correction.py:69-190). */
+SB_API int sb_inject(const sb_inject_desc *descs, int32_t n_desc,
+                     const sb_inject_params *params, uint64_t *err_counter,
+                     void *stream);
+
+/* Bytes of workspace sb_permute_paged needs for n_pairs pairs. */
+SB_API int64_t sb_permute_workspace_bytes(int64_t n_pairs, int32_t n_layers,
+                                          int32_t n_heads, int32_t head_dim,
+                                          int32_t dtype);
+
+/* In-place permutation of rows inside one (paged or flat) cache: every source
+ * row (K and V, all layers and heads) is first copied into the workspace, then
+ * written to its destination with K rotated by k_angle (SB_ANGLE_DELTA or
+ * SB_ANGLE_NOPE; SB_ANGLE_NONE copies).  Sources may overlap destinations.
+ *
+ * Replaces:
+ *   permute_paged_kv_with_rope   semblend_core/rope_correction.py:407-476
+ *   nope_permute_paged_kv        semblend_core/rope_correction.py:599-696
+ *   (and _nope_permute_paged_kernel, rope_correction.py:499-596) */
+SB_API int sb_permute_paged(const sb_rows *cache, const void *src_pos,
+                            const void *dst_pos, int64_t n_pairs,
+                            int32_t pos_dtype, const sb_inject_params *params,
+                            void *workspace, int64_t workspace_bytes,
+                            uint64_t *err_counter, void *stream);
+
+/* ------------------------------------------------------------------------ */
+/* Miscellaneous                                                            */
+/* ------------------------------------------------------------------------ */
+SB_API const char *sb_status_string(int status);
+SB_API int sb_version(void);
+/* The last CUDA error code seen by this library on the calling thread (0 if
+ * none), for diagnosing SB_ERR_CUDA. */
+SB_API int sb_last_cuda_error(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SEMBLEND_B200_H */

@@ -1,0 +1,457 @@
+// Fused donor-KV gather + RoPE correction + paged / flat scatter (sm_100a).
+//
+// One launch covers every descriptor (request) of a call and every
+// (layer, kv, head) row of each pair.  A CTA owns a tile of pairs and a chunk
+// of (layer, kv, head) units: its threads compute cos/sin of their pair's
+// angles once and reuse them for every K row of the chunk, so the
+// transcendental cost is amortised over layers and heads and the kernel stays
+// bound by HBM traffic.  Each thread moves two vectors of up to 16 bytes per
+// row (the two halves of its RoPE pairs), with streaming loads and stores.
+//
+// Arithmetic follows the reference's CPU path term by term
+// (semblend_core/rope_correction.py:304-328 for delta correction,
+// :806-823 for the NoPE two-step, :753-779 for a constant delta):
+// theta = fp32(position difference) * inv_freq[i] as one fp32 multiply, and
+// every product and sum of the rotation rounded separately (no FMA
+// contraction), so results differ from the reference only where the cos/sin
+// values themselves differ in their last bit.  Out-of-range pairs are skipped
+// the way the reference's Triton kernels skip them
+// (rope_correction.py:117-129, triton_kernels.py:106-108, :246-260) and are
+// counted in a device error counter.
+#include <algorithm>
+
+#include "common.cuh"
+
+namespace sb {
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kUnroll = 4;
+
+template <int MAXD> struct InjectLaunch {
+  sb_inject_params p;
+  unsigned long long *err;
+  int32_t n_desc;
+  int32_t pairs_per_tile;
+  int32_t tpr;  // threads per row
+  int32_t n_kv_sel;
+  int32_t kv_first;
+  int32_t units_per_chunk;
+  int64_t n_units;
+  int64_t tile_start[MAXD + 1];
+  sb_inject_desc desc[MAXD];
+};
+
+__device__ __forceinline__ bool resolve_row(const sb_rows &r, int64_t pos, int64_t &off) {
+  if (pos < 0) return false;
+  if (r.block_table == nullptr) {
+    if (pos >= r.n_logical) return false;
+    off = pos * r.stride_pos;
+    return true;
+  }
+  const int64_t lb = pos / r.block_size;
+  if (lb >= r.n_logical) return false;
+  const int64_t phys = load_index(r.block_table, lb, r.block_table_dtype);
+  if (phys < 0 || phys >= r.n_physical) return false;
+  off = phys * r.stride_block + (pos - lb * r.block_size) * r.stride_pos;
+  return true;
+}
+
+template <typename T>
+__device__ __forceinline__ T *layer_base(const sb_rows &r, int l) {
+  if (r.layer_ptrs != nullptr) return reinterpret_cast<T *>(r.layer_ptrs[l]);
+  return reinterpret_cast<T *>(r.base) + (int64_t)l * r.stride_layer;
+}
+
+// cos / sin of an fp32 angle: evaluated in double precision and rounded once,
+// which gives the correctly rounded fp32 value in all but rare cases.
+__device__ __forceinline__ void sincos_f32(float theta, float &s, float &c) {
+  double sd, cd;
+  sincos((double)theta, &sd, &cd);
+  s = (float)sd;
+  c = (float)cd;
+}
+
+// (x, y) <- (x*c - y*s, x*s + y*c); every product and sum rounded on its own.
+__device__ __forceinline__ void rotate_fwd(float &x, float &y, float c, float s) {
+  const float nx = __fsub_rn(__fmul_rn(x, c), __fmul_rn(y, s));
+  const float ny = __fadd_rn(__fmul_rn(x, s), __fmul_rn(y, c));
+  x = nx;
+  y = ny;
+}
+// (x, y) <- (x*c + y*s, (-x)*s + y*c): rotation by the negated angle.
+__device__ __forceinline__ void rotate_inv(float &x, float &y, float c, float s) {
+  const float nx = __fadd_rn(__fmul_rn(x, c), __fmul_rn(y, s));
+  const float ny = __fadd_rn(__fmul_rn(-x, s), __fmul_rn(y, c));
+  x = nx;
+  y = ny;
+}
+
+template <typename T, bool NOPE>
+__device__ __forceinline__ void rotate_pair(T &a, T &b, float c1, float s1, float c2, float s2) {
+  float x = Elem<T>::to_f32(a), y = Elem<T>::to_f32(b);
+  if (NOPE) {
+    rotate_inv(x, y, c1, s1);
+    rotate_fwd(x, y, c2, s2);
+  } else {
+    rotate_fwd(x, y, c1, s1);
+  }
+  a = Elem<T>::from_f32(x);
+  b = Elem<T>::from_f32(y);
+}
+
+template <typename T, int VEC, bool NOPE>
+__device__ __forceinline__ void rotate_vectors(Vec<T, VEC> &va, Vec<T, VEC> &vb, bool neox,
+                                               const float *c1, const float *s1,
+                                               const float *c2, const float *s2) {
+  if (neox || VEC == 1) {
+    // element e of va pairs with element e of vb (frequency slot e)
+#pragma unroll
+    for (int e = 0; e < VEC; ++e)
+      rotate_pair<T, NOPE>(va.e[e], vb.e[e], c1[e], s1[e], c2[e], s2[e]);
+  } else {
+    // interleaved: adjacent elements pair up; va holds slots [0, VEC/2),
+    // vb holds slots [VEC/2, VEC)
+#pragma unroll
+    for (int m = 0; m < VEC / 2; ++m) {
+      rotate_pair<T, NOPE>(va.e[2 * m], va.e[2 * m + 1], c1[m], s1[m], c2[m], s2[m]);
+      rotate_pair<T, NOPE>(vb.e[2 * m], vb.e[2 * m + 1], c1[VEC / 2 + m], s1[VEC / 2 + m],
+                           c2[VEC / 2 + m], s2[VEC / 2 + m]);
+    }
+  }
+}
+
+template <typename T, int VEC, int MAXD>
+__global__ void __launch_bounds__(kThreads)
+    inject_kernel(const __grid_constant__ InjectLaunch<MAXD> L) {
+  const int tpr = L.tpr;
+  const int pl = threadIdx.x / tpr;
+  const int slice = threadIdx.x - pl * tpr;
+  if (pl >= L.pairs_per_tile) return;
+
+  const int64_t tile = blockIdx.x;
+  int di = 0;
+#pragma unroll 1
+  while (di + 1 < L.n_desc && tile >= L.tile_start[di + 1]) ++di;
+  const sb_inject_desc &d = L.desc[di];
+  const int64_t pair = (tile - L.tile_start[di]) * L.pairs_per_tile + pl;
+  if (pair >= d.n_pairs) return;
+
+  const int64_t sp = load_index(d.src_pos, pair, d.pos_dtype);
+  const int64_t tp = load_index(d.dst_pos, pair, d.pos_dtype);
+  const int64_t srow =
+      d.src_row == SB_ROW_AT_PAIR ? pair : (d.src_row == SB_ROW_AT_DST_POS ? tp : sp);
+  const int64_t drow =
+      d.dst_row == SB_ROW_AT_PAIR ? pair : (d.dst_row == SB_ROW_AT_SRC_POS ? sp : tp);
+  int64_t soff = 0, doff = 0, chk = 0;
+  bool ok = resolve_row(d.src, srow, soff) && resolve_row(d.dst, drow, doff);
+  if (ok && (d.flags & SB_DESC_CHECK_SRC_IN_DST)) ok = resolve_row(d.dst, sp, chk);
+  if (!ok) {
+    if (blockIdx.y == 0 && slice == 0 && L.err != nullptr) atomicAdd(L.err, 1ull);
+    return;
+  }
+
+  const sb_inject_params &P = L.p;
+  const int D = P.head_dim;
+  const bool neox = P.rotary_style == SB_ROTARY_NEOX;
+  int oa, ob;
+  if (neox) {
+    oa = slice * VEC;
+    ob = D / 2 + slice * VEC;
+  } else if (VEC == 1) {
+    oa = 2 * slice;
+    ob = 2 * slice + 1;
+  } else {
+    oa = 2 * slice * VEC;
+    ob = oa + VEC;
+  }
+
+  const bool rot = P.k_angle != SB_ANGLE_NONE && (P.kv_select & SB_KV_K);
+  const bool nope = P.k_angle == SB_ANGLE_NOPE;
+  float c1[VEC], s1[VEC], c2[VEC], s2[VEC];
+#pragma unroll
+  for (int e = 0; e < VEC; ++e) c1[e] = 1.f, s1[e] = 0.f, c2[e] = 1.f, s2[e] = 0.f;
+  if (rot) {
+    float m1, m2 = 0.f;
+    if (P.k_angle == SB_ANGLE_DELTA) {
+      m1 = (float)(tp - sp);
+    } else if (P.k_angle == SB_ANGLE_CONST) {
+      m1 = (float)P.const_delta;
+    } else {
+      m1 = (float)sp;
+      m2 = (float)tp;
+    }
+    const int f0 = slice * VEC;
+#pragma unroll
+    for (int e = 0; e < VEC; ++e) {
+      const float f = P.inv_freq[f0 + e];
+      sincos_f32(__fmul_rn(m1, f), s1[e], c1[e]);
+      if (nope) sincos_f32(__fmul_rn(m2, f), s2[e], c2[e]);
+    }
+  }
+
+  const int H = P.n_heads;
+  const int64_t ua = (int64_t)blockIdx.y * L.units_per_chunk;
+  const int64_t ub = min(ua + (int64_t)L.units_per_chunk, L.n_units);
+  const int64_t sdim = d.src.stride_dim, ddim = d.dst.stride_dim;
+
+#pragma unroll 1
+  for (int64_t u0 = ua; u0 < ub; u0 += kUnroll) {
+    Vec<T, VEC> va[kUnroll], vb[kUnroll];
+    T *dptr[kUnroll];
+    bool krow[kUnroll];
+#pragma unroll
+    for (int r = 0; r < kUnroll; ++r) {
+      const int64_t u = u0 + r;
+      dptr[r] = nullptr;
+      krow[r] = false;
+      if (u < ub) {
+        const int h = (int)(u % H);
+        const int64_t rest = u / H;
+        const int kv = L.kv_first + (int)(rest % L.n_kv_sel);
+        const int l = (int)(rest / L.n_kv_sel);
+        const T *s = layer_base<T>(d.src, l) + kv * d.src.stride_kv + h * d.src.stride_head + soff;
+        T *t = layer_base<T>(d.dst, l) + kv * d.dst.stride_kv + h * d.dst.stride_head + doff;
+        if (VEC == 1) {
+          va[r].e[0] = s[oa * sdim];
+          vb[r].e[0] = s[ob * sdim];
+        } else {
+          load_vec(va[r], s + oa);
+          load_vec(vb[r], s + ob);
+        }
+        dptr[r] = t;
+        krow[r] = kv == 0;
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < kUnroll; ++r) {
+      if (dptr[r] == nullptr) continue;
+      if (rot && krow[r]) {
+        if (nope)
+          rotate_vectors<T, VEC, true>(va[r], vb[r], neox, c1, s1, c2, s2);
+        else
+          rotate_vectors<T, VEC, false>(va[r], vb[r], neox, c1, s1, c2, s2);
+      }
+      if (VEC == 1) {
+        dptr[r][oa * ddim] = va[r].e[0];
+        dptr[r][ob * ddim] = vb[r].e[0];
+      } else {
+        store_vec(dptr[r] + oa, va[r]);
+        store_vec(dptr[r] + ob, vb[r]);
+      }
+    }
+  }
+}
+
+int sm_count() {
+  int dev = 0, n = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 148;
+  return n > 0 ? n : 148;
+}
+
+bool rows_valid(const sb_rows &r) {
+  if (r.base == nullptr && r.layer_ptrs == nullptr) return false;
+  if (r.n_logical < 0) return false;
+  if (r.block_table != nullptr) {
+    if (r.block_size <= 0 || r.n_physical < 0) return false;
+    if (r.block_table_dtype != SB_INDEX_I32 && r.block_table_dtype != SB_INDEX_I64) return false;
+  }
+  return true;
+}
+
+// Largest vector width (elements) usable for every descriptor.
+int pick_vec(const sb_inject_desc *descs, int n, int D, int es) {
+  for (int vec = 16 / es; vec >= 2; vec /= 2) {
+    if (D % (2 * vec) != 0) continue;
+    bool ok = true;
+    const int64_t vb = (int64_t)vec * es;
+    for (int i = 0; i < n && ok; ++i) {
+      if (descs[i].n_pairs == 0) continue;
+      for (const sb_rows *r : {&descs[i].src, &descs[i].dst}) {
+        if (r->stride_dim != 1) ok = false;
+        if (r->layer_ptrs == nullptr && r->stride_layer % vec) ok = false;
+        if (r->block_table != nullptr && r->stride_block % vec) ok = false;
+        if (r->stride_kv % vec || r->stride_head % vec || r->stride_pos % vec) ok = false;
+        if (r->base != nullptr && (reinterpret_cast<uintptr_t>(r->base) % vb)) ok = false;
+      }
+    }
+    if (ok) return vec;
+  }
+  return 1;
+}
+
+template <typename T, int VEC, int MAXD>
+int launch_typed(const InjectLaunch<MAXD> &L, dim3 grid, cudaStream_t st) {
+  inject_kernel<T, VEC, MAXD><<<grid, kThreads, 0, st>>>(L);
+  return launch_status();
+}
+
+template <int MAXD>
+int launch(const InjectLaunch<MAXD> &L, int vec, dim3 grid, cudaStream_t st) {
+  switch (L.p.dtype) {
+    case SB_DTYPE_F32:
+      if (vec == 4) return launch_typed<float, 4, MAXD>(L, grid, st);
+      if (vec == 2) return launch_typed<float, 2, MAXD>(L, grid, st);
+      return launch_typed<float, 1, MAXD>(L, grid, st);
+    case SB_DTYPE_F16:
+      if (vec == 8) return launch_typed<__half, 8, MAXD>(L, grid, st);
+      if (vec == 4) return launch_typed<__half, 4, MAXD>(L, grid, st);
+      if (vec == 2) return launch_typed<__half, 2, MAXD>(L, grid, st);
+      return launch_typed<__half, 1, MAXD>(L, grid, st);
+    case SB_DTYPE_BF16:
+      if (vec == 8) return launch_typed<__nv_bfloat16, 8, MAXD>(L, grid, st);
+      if (vec == 4) return launch_typed<__nv_bfloat16, 4, MAXD>(L, grid, st);
+      if (vec == 2) return launch_typed<__nv_bfloat16, 2, MAXD>(L, grid, st);
+      return launch_typed<__nv_bfloat16, 1, MAXD>(L, grid, st);
+  }
+  return SB_ERR_UNSUPPORTED;
+}
+
+int validate_params(const sb_inject_params *p) {
+  if (p == nullptr) return SB_ERR_INVALID_ARGUMENT;
+  if (p->n_layers <= 0 || p->n_heads <= 0) return SB_ERR_INVALID_ARGUMENT;
+  if (p->head_dim < 2 || p->head_dim % 2 || p->head_dim > 512) return SB_ERR_UNSUPPORTED;
+  if (elem_bytes(p->dtype) == 0) return SB_ERR_UNSUPPORTED;
+  if (p->rotary_style != SB_ROTARY_INTERLEAVED && p->rotary_style != SB_ROTARY_NEOX)
+    return SB_ERR_INVALID_ARGUMENT;
+  if (p->k_angle < SB_ANGLE_NONE || p->k_angle > SB_ANGLE_CONST) return SB_ERR_INVALID_ARGUMENT;
+  if (p->kv_select < 1 || p->kv_select > 3) return SB_ERR_INVALID_ARGUMENT;
+  if (p->k_angle != SB_ANGLE_NONE && (p->kv_select & SB_KV_K) && p->inv_freq == nullptr)
+    return SB_ERR_INVALID_ARGUMENT;
+  return SB_OK;
+}
+
+template <int MAXD>
+int inject_impl(const sb_inject_desc *descs, int n_desc, const sb_inject_params *params,
+                uint64_t *err, cudaStream_t st) {
+  InjectLaunch<MAXD> L;
+  memset(&L, 0, sizeof(L));
+  L.p = *params;
+  L.err = reinterpret_cast<unsigned long long *>(err);
+  L.n_desc = n_desc;
+  const int D = params->head_dim;
+  const int es = elem_bytes(params->dtype);
+  const int vec = pick_vec(descs, n_desc, D, es);
+  L.tpr = D / (2 * vec);
+  if (L.tpr > kThreads) return SB_ERR_UNSUPPORTED;
+  L.pairs_per_tile = kThreads / L.tpr;
+  L.n_kv_sel = params->kv_select == SB_KV_BOTH ? 2 : 1;
+  L.kv_first = params->kv_select == SB_KV_V ? 1 : 0;
+  L.n_units = (int64_t)params->n_layers * L.n_kv_sel * params->n_heads;
+  int64_t tiles = 0;
+  for (int i = 0; i < n_desc; ++i) {
+    L.desc[i] = descs[i];
+    L.tile_start[i] = tiles;
+    tiles += (descs[i].n_pairs + L.pairs_per_tile - 1) / L.pairs_per_tile;
+  }
+  L.tile_start[n_desc] = tiles;
+  if (tiles == 0) return SB_OK;
+  if (tiles > 0x7fffffffLL) return SB_ERR_TOO_LARGE;
+  // Aim for ~16 waves of resident CTAs so the last wave's imbalance is small,
+  // while keeping at least 4 rows per thread to amortise the cos/sin set-up.
+  const int64_t target = (int64_t)sm_count() * (2048 / kThreads) * 16;
+  int64_t chunks = std::max<int64_t>(1, (target + tiles - 1) / tiles);
+  chunks = std::min<int64_t>(chunks, std::max<int64_t>(1, (L.n_units + 3) / 4));
+  chunks = std::min<int64_t>(chunks, 65535);
+  int64_t upc = (L.n_units + chunks - 1) / chunks;
+  chunks = (L.n_units + upc - 1) / upc;
+  if (upc > 0x7fffffffLL) return SB_ERR_TOO_LARGE;
+  L.units_per_chunk = (int32_t)upc;
+  dim3 grid((unsigned)tiles, (unsigned)chunks);
+  return launch<MAXD>(L, vec, grid, st);
+}
+
+}  // namespace
+
+int inject_dispatch(const sb_inject_desc *descs, int32_t n_desc, const sb_inject_params *params,
+                    uint64_t *err_counter, cudaStream_t st) {
+  int s = validate_params(params);
+  if (s != SB_OK) return s;
+  if (n_desc < 0 || n_desc > SB_MAX_INJECT_DESC) return SB_ERR_INVALID_ARGUMENT;
+  if (n_desc == 0) return SB_OK;
+  if (descs == nullptr) return SB_ERR_INVALID_ARGUMENT;
+  for (int i = 0; i < n_desc; ++i) {
+    const sb_inject_desc &d = descs[i];
+    if (d.n_pairs < 0) return SB_ERR_INVALID_ARGUMENT;
+    if (d.n_pairs == 0) continue;
+    if (d.src_pos == nullptr || d.dst_pos == nullptr) return SB_ERR_INVALID_ARGUMENT;
+    if (d.pos_dtype != SB_INDEX_I32 && d.pos_dtype != SB_INDEX_I64) return SB_ERR_INVALID_ARGUMENT;
+    if (d.src_row < SB_ROW_AT_SRC_POS || d.src_row > SB_ROW_AT_PAIR) return SB_ERR_INVALID_ARGUMENT;
+    if (d.dst_row < SB_ROW_AT_SRC_POS || d.dst_row > SB_ROW_AT_PAIR) return SB_ERR_INVALID_ARGUMENT;
+    if (!rows_valid(d.src) || !rows_valid(d.dst)) return SB_ERR_INVALID_ARGUMENT;
+  }
+  if (n_desc == 1) return inject_impl<1>(descs, n_desc, params, err_counter, st);
+  return inject_impl<SB_MAX_INJECT_DESC>(descs, n_desc, params, err_counter, st);
+}
+
+}  // namespace sb
+
+extern "C" SB_API int sb_inject(const sb_inject_desc *descs, int32_t n_desc,
+                                const sb_inject_params *params, uint64_t *err_counter,
+                                void *stream) {
+  return sb::inject_dispatch(descs, n_desc, params, err_counter,
+                             reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" SB_API int64_t sb_permute_workspace_bytes(int64_t n_pairs, int32_t n_layers,
+                                                     int32_t n_heads, int32_t head_dim,
+                                                     int32_t dtype) {
+  const int es = sb::elem_bytes(dtype);
+  if (es == 0 || n_pairs < 0 || n_layers <= 0 || n_heads <= 0 || head_dim <= 0) return -1;
+  return n_pairs * (int64_t)n_layers * 2 * n_heads * head_dim * es;
+}
+
+extern "C" SB_API int sb_permute_paged(const sb_rows *cache, const void *src_pos,
+                                       const void *dst_pos, int64_t n_pairs, int32_t pos_dtype,
+                                       const sb_inject_params *params, void *workspace,
+                                       int64_t workspace_bytes, uint64_t *err_counter,
+                                       void *stream) {
+  if (cache == nullptr || params == nullptr) return SB_ERR_INVALID_ARGUMENT;
+  if (params->k_angle == SB_ANGLE_CONST) return SB_ERR_INVALID_ARGUMENT;
+  if (n_pairs < 0) return SB_ERR_INVALID_ARGUMENT;
+  if (n_pairs == 0) return SB_OK;
+  const int64_t need = sb_permute_workspace_bytes(n_pairs, params->n_layers, params->n_heads,
+                                                  params->head_dim, params->dtype);
+  if (need < 0) return SB_ERR_INVALID_ARGUMENT;
+  if (workspace == nullptr || workspace_bytes < need) return SB_ERR_WORKSPACE_TOO_SMALL;
+  if (reinterpret_cast<uintptr_t>(workspace) % 16) return SB_ERR_INVALID_ARGUMENT;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const int64_t H = params->n_heads, D = params->head_dim;
+
+  sb_rows ws;
+  memset(&ws, 0, sizeof(ws));
+  ws.base = workspace;
+  ws.stride_dim = 1;
+  ws.stride_head = D;
+  ws.stride_kv = H * D;
+  ws.stride_pos = 2 * H * D;
+  ws.stride_layer = n_pairs * 2 * H * D;
+  ws.n_logical = n_pairs;
+
+  // Phase 1: snapshot every source row (plain copy, uncounted).
+  sb_inject_desc g;
+  memset(&g, 0, sizeof(g));
+  g.src = *cache;
+  g.dst = ws;
+  g.src_pos = src_pos;
+  g.dst_pos = dst_pos;
+  g.n_pairs = n_pairs;
+  g.pos_dtype = pos_dtype;
+  g.src_row = SB_ROW_AT_SRC_POS;
+  g.dst_row = SB_ROW_AT_PAIR;
+  sb_inject_params gp = *params;
+  gp.k_angle = SB_ANGLE_NONE;
+  int s = sb::inject_dispatch(&g, 1, &gp, nullptr, st);
+  if (s != SB_OK) return s;
+
+  // Phase 2: write the snapshot to the destinations, rotating K.  Pairs whose
+  // source row was out of range (left unsnapshotted) are skipped and counted.
+  sb_inject_desc w = g;
+  w.src = ws;
+  w.dst = *cache;
+  w.src_row = SB_ROW_AT_PAIR;
+  w.dst_row = SB_ROW_AT_DST_POS;
+  w.flags = SB_DESC_CHECK_SRC_IN_DST;
+  return sb::inject_dispatch(&w, 1, params, err_counter, st);
+}
