@@ -190,18 +190,19 @@ def run_ours(args, world, rank, local) -> dict | None:
     from semblend_b200 import rope_correction as rc
 
     dev = torch.device("cuda", local)
+    n_req, n_layers = args.requests, args.layers
     rng = np.random.default_rng(SEED + rank)
-    pool = int(N_REQ * (SEQ // BLOCK) * 1.25)
-    plans = [make_request_plan(rng) for _ in range(N_REQ)]
-    tables = make_block_tables(rng, N_REQ, SEQ, pool)
+    pool = int(n_req * (SEQ // BLOCK) * 1.25)
+    plans = [make_request_plan(rng) for _ in range(n_req)]
+    tables = make_block_tables(rng, n_req, SEQ, pool)
     n_pairs = sum(p[0].shape[0] for p in plans)
 
     gen = torch.Generator(device=dev).manual_seed(SEED + rank)
-    cache = torch.empty(N_LAYERS, pool, 2, N_KV_HEADS, BLOCK, HEAD_DIM, dtype=torch.bfloat16, device=dev)
+    cache = torch.empty(n_layers, pool, 2, N_KV_HEADS, BLOCK, HEAD_DIM, dtype=torch.bfloat16, device=dev)
     cache.normal_(generator=gen)
     donors = []
-    for _ in range(N_REQ):
-        dk = torch.empty(N_LAYERS, 2, N_KV_HEADS, SEQ, HEAD_DIM, dtype=torch.bfloat16, device=dev)
+    for _ in range(n_req):
+        dk = torch.empty(n_layers, 2, N_KV_HEADS, SEQ, HEAD_DIM, dtype=torch.bfloat16, device=dev)
         dk.normal_(generator=gen)
         donors.append(dk)
 
@@ -210,7 +211,7 @@ def run_ours(args, world, rank, local) -> dict | None:
     host_bt = [torch.from_numpy(b).pin_memory() for b in tables]
     dev_pos = [h.to(dev) for h in host_pos]
     dev_bt = [h.to(dev) for h in host_bt]
-    injections = [rc.DonorInjection(donors[r], dev_bt[r], dev_pos[r][0], dev_pos[r][1]) for r in range(N_REQ)]
+    injections = [rc.DonorInjection(donors[r], dev_bt[r], dev_pos[r][0], dev_pos[r][1]) for r in range(n_req)]
     err = _lib.err_counter(dev)
     stream = torch.cuda.current_stream(dev)
 
@@ -249,7 +250,7 @@ def run_ours(args, world, rank, local) -> dict | None:
     status = torch.empty(1, dtype=torch.int64).pin_memory()
 
     def e2e_step():
-        for r in range(N_REQ):
+        for r in range(n_req):
             dev_pos[r].copy_(host_pos[r], non_blocking=True)
             dev_bt[r].copy_(host_bt[r], non_blocking=True)
         rc.inject_donors(cache, injections, rope_base=ROPE_THETA, rotary_style="neox")
@@ -270,7 +271,7 @@ def run_ours(args, world, rank, local) -> dict | None:
     skipped = int(status.item())
 
     elt = 2
-    per_rank_bytes = algorithmic_bytes(n_pairs, N_LAYERS, N_KV_HEADS, HEAD_DIM, elt, N_REQ * (SEQ // BLOCK))
+    per_rank_bytes = algorithmic_bytes(n_pairs, n_layers, N_KV_HEADS, HEAD_DIM, elt, n_req * (SEQ // BLOCK))
     total_bytes = per_rank_bytes * world  # every rank moves the same amount (weak scaling)
     ms_per_step = total_ms / args.steps
     value = total_bytes / (ms_per_step * 1e-3) / 1e9
@@ -299,7 +300,8 @@ def run_ours(args, world, rank, local) -> dict | None:
         "dtype": "bf16",
         "data": "synthetic (seeded N(0,1) K/V, seeded chunk deltas, recompute set and block tables)",
         "config": {
-            "workload": "c2: 8 req x 16384 tok donors, 28 L x 4 KV heads x 128, bf16, 85% reuse via 256-tok "
+            "workload": f"c2{'' if (n_req, n_layers) == (N_REQ, N_LAYERS) else ' (reduced)'}: {n_req} req x 16384 "
+                        f"tok donors, {n_layers} L x 4 KV heads x 128, bf16, 85% reuse via 256-tok "
                         "chunks (delta U[-4096,4096]), 15% recompute untouched, block 16, neox RoPE theta 1e6",
             "pairs_per_rank": n_pairs,
             "parallelism": f"tp{world} by kv-heads (4 kv-heads per rank, weak scaling, no collective)",
@@ -387,6 +389,8 @@ def main() -> int:
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--requests", type=int, default=N_REQ, help="requests per step (c2: 8)")
+    ap.add_argument("--layers", type=int, default=N_LAYERS, help="layers (c2: 28)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":

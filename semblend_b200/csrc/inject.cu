@@ -25,8 +25,14 @@
 namespace sb {
 namespace {
 
+#ifndef SB_INJECT_MIN_BLOCKS
+#define SB_INJECT_MIN_BLOCKS 4  // resident CTAs per SM the register budget targets
+#endif
+#ifndef SB_INJECT_UNROLL
+#define SB_INJECT_UNROLL 2  // rows in flight per thread
+#endif
 constexpr int kThreads = 256;
-constexpr int kUnroll = 4;
+constexpr int kUnroll = SB_INJECT_UNROLL;
 
 template <int MAXD> struct InjectLaunch {
   sb_inject_params p;
@@ -100,29 +106,32 @@ __device__ __forceinline__ void rotate_pair(T &a, T &b, float c1, float s1, floa
   b = Elem<T>::from_f32(y);
 }
 
+// c2 / s2 hold the second angle of the NoPE two-step and have one (unused)
+// slot otherwise.
 template <typename T, int VEC, bool NOPE>
 __device__ __forceinline__ void rotate_vectors(Vec<T, VEC> &va, Vec<T, VEC> &vb, bool neox,
                                                const float *c1, const float *s1,
                                                const float *c2, const float *s2) {
+  constexpr int kSlots2 = NOPE ? VEC : 1;
   if (neox || VEC == 1) {
     // element e of va pairs with element e of vb (frequency slot e)
 #pragma unroll
     for (int e = 0; e < VEC; ++e)
-      rotate_pair<T, NOPE>(va.e[e], vb.e[e], c1[e], s1[e], c2[e], s2[e]);
+      rotate_pair<T, NOPE>(va.e[e], vb.e[e], c1[e], s1[e], c2[e % kSlots2], s2[e % kSlots2]);
   } else {
     // interleaved: adjacent elements pair up; va holds slots [0, VEC/2),
     // vb holds slots [VEC/2, VEC)
 #pragma unroll
     for (int m = 0; m < VEC / 2; ++m) {
-      rotate_pair<T, NOPE>(va.e[2 * m], va.e[2 * m + 1], c1[m], s1[m], c2[m], s2[m]);
-      rotate_pair<T, NOPE>(vb.e[2 * m], vb.e[2 * m + 1], c1[VEC / 2 + m], s1[VEC / 2 + m],
-                           c2[VEC / 2 + m], s2[VEC / 2 + m]);
+      const int a = m, b = VEC / 2 + m;
+      rotate_pair<T, NOPE>(va.e[2 * m], va.e[2 * m + 1], c1[a], s1[a], c2[a % kSlots2], s2[a % kSlots2]);
+      rotate_pair<T, NOPE>(vb.e[2 * m], vb.e[2 * m + 1], c1[b], s1[b], c2[b % kSlots2], s2[b % kSlots2]);
     }
   }
 }
 
-template <typename T, int VEC, int MAXD>
-__global__ void __launch_bounds__(kThreads)
+template <typename T, int VEC, int MAXD, bool NOPE>
+__global__ void __launch_bounds__(kThreads, SB_INJECT_MIN_BLOCKS)
     inject_kernel(const __grid_constant__ InjectLaunch<MAXD> L) {
   const int tpr = L.tpr;
   const int pl = threadIdx.x / tpr;
@@ -167,10 +176,12 @@ __global__ void __launch_bounds__(kThreads)
   }
 
   const bool rot = P.k_angle != SB_ANGLE_NONE && (P.kv_select & SB_KV_K);
-  const bool nope = P.k_angle == SB_ANGLE_NOPE;
-  float c1[VEC], s1[VEC], c2[VEC], s2[VEC];
+  // c2 / s2 (the second angle) only exist in the NoPE instantiation
+  float c1[VEC], s1[VEC], c2[NOPE ? VEC : 1], s2[NOPE ? VEC : 1];
 #pragma unroll
-  for (int e = 0; e < VEC; ++e) c1[e] = 1.f, s1[e] = 0.f, c2[e] = 1.f, s2[e] = 0.f;
+  for (int e = 0; e < VEC; ++e) c1[e] = 1.f, s1[e] = 0.f;
+#pragma unroll
+  for (int e = 0; e < (NOPE ? VEC : 1); ++e) c2[e] = 1.f, s2[e] = 0.f;
   if (rot) {
     float m1, m2 = 0.f;
     if (P.k_angle == SB_ANGLE_DELTA) {
@@ -186,7 +197,7 @@ __global__ void __launch_bounds__(kThreads)
     for (int e = 0; e < VEC; ++e) {
       const float f = P.inv_freq[f0 + e];
       sincos_f32(__fmul_rn(m1, f), s1[e], c1[e]);
-      if (nope) sincos_f32(__fmul_rn(m2, f), s2[e], c2[e]);
+      if (NOPE) sincos_f32(__fmul_rn(m2, f), s2[e], c2[e]);
     }
   }
 
@@ -226,12 +237,7 @@ __global__ void __launch_bounds__(kThreads)
 #pragma unroll
     for (int r = 0; r < kUnroll; ++r) {
       if (dptr[r] == nullptr) continue;
-      if (rot && krow[r]) {
-        if (nope)
-          rotate_vectors<T, VEC, true>(va[r], vb[r], neox, c1, s1, c2, s2);
-        else
-          rotate_vectors<T, VEC, false>(va[r], vb[r], neox, c1, s1, c2, s2);
-      }
+      if (rot && krow[r]) rotate_vectors<T, VEC, NOPE>(va[r], vb[r], neox, c1, s1, c2, s2);
       if (VEC == 1) {
         dptr[r][oa * ddim] = va[r].e[0];
         dptr[r][ob * ddim] = vb[r].e[0];
@@ -283,7 +289,10 @@ int pick_vec(const sb_inject_desc *descs, int n, int D, int es) {
 
 template <typename T, int VEC, int MAXD>
 int launch_typed(const InjectLaunch<MAXD> &L, dim3 grid, cudaStream_t st) {
-  inject_kernel<T, VEC, MAXD><<<grid, kThreads, 0, st>>>(L);
+  if (L.p.k_angle == SB_ANGLE_NOPE && (L.p.kv_select & SB_KV_K))
+    inject_kernel<T, VEC, MAXD, true><<<grid, kThreads, 0, st>>>(L);
+  else
+    inject_kernel<T, VEC, MAXD, false><<<grid, kThreads, 0, st>>>(L);
   return launch_status();
 }
 
@@ -349,10 +358,10 @@ int inject_impl(const sb_inject_desc *descs, int n_desc, const sb_inject_params 
   if (tiles == 0) return SB_OK;
   if (tiles > 0x7fffffffLL) return SB_ERR_TOO_LARGE;
   // Aim for ~16 waves of resident CTAs so the last wave's imbalance is small,
-  // while keeping at least 4 rows per thread to amortise the cos/sin set-up.
+  // while keeping at least 8 rows per thread to amortise the cos/sin set-up.
   const int64_t target = (int64_t)sm_count() * (2048 / kThreads) * 16;
   int64_t chunks = std::max<int64_t>(1, (target + tiles - 1) / tiles);
-  chunks = std::min<int64_t>(chunks, std::max<int64_t>(1, (L.n_units + 3) / 4));
+  chunks = std::min<int64_t>(chunks, std::max<int64_t>(1, (L.n_units + 7) / 8));
   chunks = std::min<int64_t>(chunks, 65535);
   int64_t upc = (L.n_units + chunks - 1) / chunks;
   chunks = (L.n_units + upc - 1) / upc;
