@@ -171,6 +171,60 @@ SB_API int sb_permute_paged(const sb_rows *cache, const void *src_pos,
                             uint64_t *err_counter, void *stream);
 
 /* ------------------------------------------------------------------------ */
+/* Donor search                                                             */
+/* ------------------------------------------------------------------------ */
+/* Refresh the bf16 screening copy of rows of a row-major fp32 embedding
+ * matrix (row pitch ld_emb floats) into emb_bf16 (row pitch ld_bf16, columns
+ * [dim, dim_pad) zeroed), and raise stats[0] / stats[1] (device floats,
+ * start at 0) to the largest ||e - bf16(e)|| and ||bf16(e)|| seen.  Rows are
+ * rows[0..n_rows) (device int64) or, when rows is NULL, the range
+ * [row_begin, row_begin + n_rows).  This is the device side of the
+ * reference's row write in DonorStore.add_donor
+ * (semblend_core/donor_store.py:155-161). */
+SB_API int sb_search_prepare_rows(const float *emb, int64_t ld_emb, uint16_t *emb_bf16,
+                                  int64_t ld_bf16, int32_t dim, int32_t dim_pad,
+                                  const int64_t *rows, int64_t row_begin, int64_t n_rows,
+                                  float *stats, void *stream);
+
+/* Workspace bytes sb_cosine_topk needs. */
+SB_API int64_t sb_cosine_topk_workspace_bytes(int32_t n_queries, int32_t dim, int32_t dim_pad,
+                                              int32_t capacity);
+
+/* Exact brute-force cosine top-k for a batch of queries.
+ *
+ * For each query q (row of `queries`, pitch ld_q): qn = q / (||q|| + 1e-8)
+ * in fp32; returns the k rows j < n_rows with valid[j] != 0 (valid may be
+ * NULL) and fp32 similarity emb[j] . qn >= min_similarity, ordered by
+ * (similarity desc, j asc), as out_ids[q*k + r] = j + id_offset and
+ * out_scores[q*k + r]; missing entries are -1 / -inf.  Screening runs on the
+ * tensor cores in bf16 (emb_bf16, dim_pad a multiple of 64, <= 512) and every
+ * candidate within the proven bf16 error bound is rescored exactly, so the
+ * result equals the fp32 computation.  k <= 32; capacity (>= k) bounds the
+ * screening candidates kept per query.  *status (device int32, zeroed by the
+ * caller) gets bit 0 set if some query had more than `capacity` candidates
+ * (its results are withheld: retry with a larger capacity) and a value >= 2
+ * if a kernel wait timed out.
+ *
+ * Replaces the cosine / threshold / top-k stage of DonorStore.find_donors
+ * (semblend_core/donor_store.py:323-341) and DonorStore.find_donor (:205-229),
+ * one query at a time there. */
+SB_API int sb_cosine_topk(const float *emb, int64_t ld_emb, const uint16_t *emb_bf16,
+                          int64_t ld_bf16, const uint8_t *valid, int64_t n_rows, int32_t dim,
+                          int32_t dim_pad, const float *stats, const float *queries,
+                          int64_t ld_q, int32_t n_queries, int32_t k, float min_similarity,
+                          int64_t id_offset, int64_t *out_ids, float *out_scores,
+                          int32_t capacity, void *workspace, int64_t workspace_bytes,
+                          int32_t *status, void *stream);
+
+/* Merge n_lists (<= 16) per-query sorted top-k lists [n_lists][n_queries][k]
+ * into one [n_queries][k] by (score desc, id asc); ids < 0 are empty.  Used
+ * after an all-gather of per-shard sb_cosine_topk results (no reference
+ * counterpart: the reference searches one process's matrix). */
+SB_API int sb_topk_merge(const int64_t *ids, const float *scores, int32_t n_lists,
+                         int32_t n_queries, int32_t k, int64_t *out_ids, float *out_scores,
+                         void *stream);
+
+/* ------------------------------------------------------------------------ */
 /* Miscellaneous                                                            */
 /* ------------------------------------------------------------------------ */
 SB_API const char *sb_status_string(int status);
@@ -178,6 +232,13 @@ SB_API int sb_version(void);
 /* The last CUDA error code seen by this library on the calling thread (0 if
  * none), for diagnosing SB_ERR_CUDA. */
 SB_API int sb_last_cuda_error(void);
+
+/* Failure-detection self-test: launches one CTA that waits on an mbarrier
+ * nothing arrives on, gives up after max_cycles clock cycles and writes 7 to
+ * *status (device int32, zeroed by the caller), the way every pipelined
+ * kernel here reports a stalled wait instead of hanging.  No reference
+ * counterpart (the reference has no device-side waits). */
+SB_API int sb_selftest_wait_timeout(int32_t *status, int64_t max_cycles, void *stream);
 
 #ifdef __cplusplus
 }

@@ -97,6 +97,25 @@ _SIGNATURES: dict[str, tuple] = {
         [_P(SbRows), ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int32, _P(SbInjectParams),
          ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p],
     ),
+    "sb_search_prepare_rows": (
+        ctypes.c_int,
+        [ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int32, ctypes.c_int32,
+         ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p],
+    ),
+    "sb_cosine_topk_workspace_bytes": (ctypes.c_int64, [ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32]),
+    "sb_cosine_topk": (
+        ctypes.c_int,
+        [ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p, ctypes.c_int64,
+         ctypes.c_int32, ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int32,
+         ctypes.c_int32, ctypes.c_float, ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32,
+         ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p],
+    ),
+    "sb_topk_merge": (
+        ctypes.c_int,
+        [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_void_p,
+         ctypes.c_void_p, ctypes.c_void_p],
+    ),
+    "sb_selftest_wait_timeout": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p]),
     "sb_status_string": (ctypes.c_char_p, [ctypes.c_int]),
     "sb_version": (ctypes.c_int, []),
     "sb_last_cuda_error": (ctypes.c_int, []),

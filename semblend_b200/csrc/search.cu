@@ -1,0 +1,631 @@
+// Brute-force cosine top-k donor search (sm_100a).
+//
+// The reference (semblend_core/donor_store.py:323-341) computes, per query,
+//     sims = E[valid] @ (q / (||q|| + 1e-8));  keep sims >= min_similarity;
+//     top fetch_k by similarity
+// in fp32 numpy.  Here a batch of queries is searched in three launches:
+//
+//  1. prep:    normalise each query exactly as the reference does (fp32), keep
+//              the fp32 copy for rescoring and a bf16 copy for the tensor
+//              cores, and a per-query bound delta_q on |exact - bf16 score|.
+//  2. screen:  a persistent, warp-specialised tcgen05 GEMM of the bf16 query
+//              tile (128 queries, resident in shared memory) against streamed
+//              256-donor bf16 tiles (TMA, 128-byte swizzle), fp32 accumulators
+//              double-buffered in tensor memory.  The epilogue warps own one
+//              query row each and keep, without any cross-thread exchange, a
+//              register top-k of bf16 scores; a donor becomes a *candidate* if
+//              its bf16 score is >= max(min_similarity - delta, L - 2 delta),
+//              where L is a lower bound on the k-th best bf16 score shared by
+//              all CTAs through one atomicMax word per query.  Every true
+//              top-k donor satisfies this (its bf16 score is >= its exact score
+//              - delta >= the k-th exact score - delta >= L - 2 delta), so the
+//              candidate set provably contains the exact answer.
+//  3. rescore: exact fp32 dot products (double accumulation) of every
+//              candidate, threshold, and selection of the top k by
+//              (score desc, row asc).
+//
+// delta_q = ||q~|| max||e - e~|| + ||q - q~|| max||e~|| + ||q - q~|| max||e - e~||
+//           + dim 2^-23 ||q~|| max||e~||  (Cauchy-Schwarz on the rounding
+// residuals plus the fp32 accumulation error); the row maxima come from
+// sb_search_prepare_rows.
+#include <algorithm>
+#include <cfloat>
+
+#include "common.cuh"
+#include "tcgen05.cuh"
+#include "tma.cuh"
+
+namespace sb {
+namespace {
+
+constexpr int kBM = 128;             // queries per tile (one TMEM lane each)
+constexpr int kBN = 256;             // donors per MMA tile
+constexpr int kBK = 64;              // K elements per shared-memory stage (128 B rows)
+constexpr int kQBlockBytes = kBM * 128;
+constexpr int kEStageBytes = kBN * 128;
+constexpr int kThreads = 192;        // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
+constexpr int kTilesPerChunk = 32;   // donor tiles per work unit
+constexpr int kMaxStages = 6;
+constexpr int kSmemLimit = 232448;
+constexpr long long kWaitCycles = 2000000000LL;  // ~1 s at 1.9 GHz
+
+struct ScreenParams {
+  int nq;
+  int k_blocks;
+  int n_qtiles;
+  int stages;
+  int64_t n_rows;
+  int64_t n_ntiles;
+  int64_t n_units;
+  float thr;
+  int cap;
+  const uint8_t *valid;
+  const float *delta;
+  int *count;
+  int *lower;
+  int *cand;
+  int *status;
+};
+
+__global__ void query_prep_kernel(const float *__restrict__ q, int64_t ld_q, int nq, int dim, int dim_pad,
+                                  const float *__restrict__ stats, float *__restrict__ qn,
+                                  __nv_bfloat16 *__restrict__ qb, float *__restrict__ delta,
+                                  int *__restrict__ count, int *__restrict__ lower) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) / 32;
+  const int lane = threadIdx.x % 32;
+  if (warp >= nq) return;
+  const float *row = q + (int64_t)warp * ld_q;
+  float ss = 0.f;
+  for (int i = lane; i < dim; i += 32) ss = fmaf(row[i], row[i], ss);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  // donor_store.py:326: q / (np.linalg.norm(q) + 1e-8), all in fp32
+  const float denom = __fadd_rn(sqrtf(ss), 1e-8f);
+  float nb = 0.f, nd = 0.f;
+  for (int i = lane; i < dim_pad; i += 32) {
+    float v = 0.f;
+    if (i < dim) {
+      v = __fdiv_rn(row[i], denom);
+      qn[(int64_t)warp * dim + i] = v;
+    }
+    const __nv_bfloat16 b = __float2bfloat16_rn(v);
+    qb[(int64_t)warp * dim_pad + i] = b;
+    const float bf = __bfloat162float(b);
+    nb = fmaf(bf, bf, nb);
+    nd = fmaf(v - bf, v - bf, nd);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    nb += __shfl_xor_sync(0xffffffffu, nb, o);
+    nd += __shfl_xor_sync(0xffffffffu, nd, o);
+  }
+  if (lane == 0) {
+    const float dmax = stats[0], emax = stats[1];
+    const float qbn = sqrtf(nb), dqn = sqrtf(nd);
+    const float acc = (float)dim * 1.1920929e-7f * qbn * emax;
+    delta[warp] = (qbn * dmax + dqn * emax + dqn * dmax + acc) * 1.001f + 1e-6f;
+    count[warp] = 0;
+    lower[warp] = tc::float_to_ordered(-INFINITY);
+  }
+}
+
+// Descending insertion into a register-resident sorted list.
+template <int KT>
+__device__ __forceinline__ void topk_insert(float (&tk)[KT], float s) {
+#pragma unroll
+  for (int i = KT - 1; i > 0; --i) {
+    const float a = tk[i - 1];
+    tk[i] = s > a ? a : (s > tk[i] ? s : tk[i]);
+  }
+  tk[0] = fmaxf(tk[0], s);
+}
+
+template <int KT>
+__global__ void __launch_bounds__(kThreads, 1)
+    screen_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmE,
+                  const ScreenParams P) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t *sQ = smem;
+  uint8_t *sE = sQ + P.k_blocks * kQBlockBytes;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(sE + P.stages * kEStageBytes);
+  uint64_t *full = bars;                   // [kMaxStages]
+  uint64_t *empty = bars + kMaxStages;     // [kMaxStages]
+  uint64_t *q_full = bars + 2 * kMaxStages;
+  uint64_t *q_empty = q_full + 1;
+  uint64_t *acc_full = q_full + 2;         // [2]
+  uint64_t *acc_empty = q_full + 4;        // [2]
+  uint64_t *final_bar = q_full + 6;
+  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(q_full + 7);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(q_full + 8);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < P.stages; ++s) {
+      tc::mbar_init(&full[s], 1);
+      tc::mbar_init(&empty[s], 1);
+    }
+    tc::mbar_init(q_full, 1);
+    tc::mbar_init(q_empty, 1);
+    tc::mbar_init(&acc_full[0], 1);
+    tc::mbar_init(&acc_full[1], 1);
+    tc::mbar_init(&acc_empty[0], 4);
+    tc::mbar_init(&acc_empty[1], 4);
+    tc::mbar_init(final_bar, 1);
+    *abort_flag = 0;
+    tc::fence_mbar_init();
+  }
+  if (warp == 1) {
+    tc::tmem_alloc(tmem_holder, 512);
+    tc::tmem_relinquish();
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = *tmem_holder;
+  const tc::Abort ab{abort_flag, P.status};
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer ----------------
+      tc::tma_prefetch_desc(&tmQ);
+      tc::tma_prefetch_desc(&tmE);
+      uint32_t it = 0, qi = 0;
+      bool ok = true;
+      for (int64_t u = blockIdx.x; u < P.n_units && ok; u += gridDim.x) {
+        const int qt = (int)(u % P.n_qtiles);
+        const int64_t t0 = (u / P.n_qtiles) * kTilesPerChunk;
+        const int64_t t1 = min(t0 + kTilesPerChunk, P.n_ntiles);
+        if (qi > 0 && !tc::mbar_wait(q_empty, (qi - 1) & 1, ab, 2, kWaitCycles)) break;
+        tc::mbar_arrive_expect_tx(q_full, P.k_blocks * kQBlockBytes);
+        for (int kb = 0; kb < P.k_blocks; ++kb)
+          tc::tma_load_2d(sQ + kb * kQBlockBytes, &tmQ, q_full, kb * kBK, qt * kBM);
+        ++qi;
+        for (int64_t t = t0; t < t1 && ok; ++t) {
+          for (int kb = 0; kb < P.k_blocks; ++kb) {
+            const uint32_t s = it % P.stages, ph = (it / P.stages) & 1;
+            if (!tc::mbar_wait(&empty[s], ph ^ 1, ab, 2, kWaitCycles)) {
+              ok = false;
+              break;
+            }
+            tc::mbar_arrive_expect_tx(&full[s], kEStageBytes);
+            tc::tma_load_2d(sE + s * kEStageBytes, &tmE, &full[s], kb * kBK, (int)(t * kBN));
+            ++it;
+          }
+        }
+      }
+      // Let every load this thread issued land before the CTA can exit.
+      const uint32_t n_out = it < (uint32_t)P.stages ? it : (uint32_t)P.stages;
+      for (uint32_t i = it - n_out; i < it; ++i) {
+        const tc::Abort quiet{abort_flag, nullptr};
+        volatile int never = 0;
+        const tc::Abort drain{&never, nullptr};
+        (void)quiet;
+        tc::mbar_wait(&full[i % P.stages], (i / P.stages) & 1, drain, 0, kWaitCycles);
+      }
+      if (qi > 0) {
+        volatile int never = 0;
+        const tc::Abort drain{&never, nullptr};
+        tc::mbar_wait(q_full, (qi - 1) & 1, drain, 0, kWaitCycles);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------- MMA issuer ----------------
+      constexpr uint32_t idesc = tc::idesc_bf16_f32(kBM, kBN);
+      uint32_t it = 0, qi = 0, ai = 0;
+      bool ok = true;
+      for (int64_t u = blockIdx.x; u < P.n_units && ok; u += gridDim.x) {
+        const int64_t t0 = (u / P.n_qtiles) * kTilesPerChunk;
+        const int64_t t1 = min(t0 + kTilesPerChunk, P.n_ntiles);
+        if (!tc::mbar_wait(q_full, qi & 1, ab, 3, kWaitCycles)) break;
+        tc::fence_after_sync();
+        for (int64_t t = t0; t < t1 && ok; ++t) {
+          const uint32_t b = ai & 1;
+          if (!tc::mbar_wait(&acc_empty[b], ((ai >> 1) & 1) ^ 1, ab, 3, kWaitCycles)) {
+            ok = false;
+            break;
+          }
+          tc::fence_after_sync();
+          const uint32_t d_tmem = tmem + b * kBN;
+          for (int kb = 0; kb < P.k_blocks; ++kb) {
+            const uint32_t s = it % P.stages, ph = (it / P.stages) & 1;
+            if (!tc::mbar_wait(&full[s], ph, ab, 3, kWaitCycles)) {
+              ok = false;
+              break;
+            }
+            tc::fence_after_sync();
+#pragma unroll
+            for (int kk = 0; kk < kBK / 16; ++kk) {
+              const uint64_t da = tc::desc_kmajor_sw128(sQ + kb * kQBlockBytes, kk * 32);
+              const uint64_t db = tc::desc_kmajor_sw128(sE + s * kEStageBytes, kk * 32);
+              tc::mma_bf16_ss(d_tmem, da, db, idesc, (kb | kk) != 0);
+            }
+            tc::mma_commit(&empty[s]);
+            ++it;
+          }
+          if (!ok) break;
+          tc::mma_commit(&acc_full[b]);
+          ++ai;
+        }
+        tc::mma_commit(q_empty);
+        ++qi;
+      }
+      // All MMAs this thread issued must finish before TMEM is released.
+      tc::mma_commit(final_bar);
+      volatile int never = 0;
+      const tc::Abort drain{&never, nullptr};
+      tc::mbar_wait(final_bar, 0, drain, 0, kWaitCycles);
+    }
+  } else {
+    // ---------------- epilogue: one query row per thread ----------------
+    const int quarter = warp & 3;  // TMEM lanes this warp may read
+    const int row = quarter * 32 + lane;
+    uint32_t ai = 0;
+    bool ok = true;
+    for (int64_t u = blockIdx.x; u < P.n_units && ok; u += gridDim.x) {
+      const int qt = (int)(u % P.n_qtiles);
+      const int64_t t0 = (u / P.n_qtiles) * kTilesPerChunk;
+      const int64_t t1 = min(t0 + kTilesPerChunk, P.n_ntiles);
+      const int q = qt * kBM + row;
+      const bool active = q < P.nq;
+      const float dq = active ? P.delta[q] : 0.f;
+      const float two_d = 2.f * dq;
+      float tk[KT];
+#pragma unroll
+      for (int i = 0; i < KT; ++i) tk[i] = -INFINITY;
+      float cut = P.thr - dq;
+      for (int64_t t = t0; t < t1; ++t) {
+        const uint32_t b = ai & 1;
+        if (!tc::mbar_wait(&acc_full[b], (ai >> 1) & 1, ab, 4, kWaitCycles)) {
+          ok = false;
+          break;
+        }
+        tc::fence_after_sync();
+        const uint32_t base = tmem + ((uint32_t)(quarter * 32) << 16) + b * kBN;
+        const int64_t n0 = t * kBN;
+#pragma unroll 1
+        for (int c = 0; c < kBN / 32; ++c) {
+          uint32_t r[32];
+          tc::tmem_ld32(base + c * 32, r);
+          tc::tmem_ld_wait();
+          if (active) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              const float s = __uint_as_float(r[i]);
+              if (s >= cut) {
+                const int64_t j = n0 + c * 32 + i;
+                if (j < P.n_rows && (P.valid == nullptr || P.valid[j])) {
+                  const int slot = atomicAdd(&P.count[q], 1);
+                  if (slot < P.cap) P.cand[(int64_t)q * P.cap + slot] = (int)j;
+                  if (s > tk[KT - 1]) {
+                    topk_insert<KT>(tk, s);
+                    cut = fmaxf(cut, tk[KT - 1] - two_d);
+                  }
+                }
+              }
+            }
+          }
+        }
+        tc::fence_before_sync();
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(&acc_empty[b]);
+        ++ai;
+        if (active) {
+          // publish this CTA's k-th best and read everyone's
+          const int mine = tc::float_to_ordered(tk[KT - 1]);
+          const int g = max(atomicMax(&P.lower[q], mine), mine);
+          cut = fmaxf(cut, tc::ordered_to_float(g) - two_d);
+        }
+      }
+    }
+  }
+
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  if (warp == 1) tc::tmem_dealloc(tmem, 512);
+}
+
+// Exact rescoring of the candidates of one query and top-k selection.
+__global__ void rescore_kernel(const float *__restrict__ emb, int64_t ld_emb, int dim,
+                               const float *__restrict__ qn, const int *__restrict__ count,
+                               const int *__restrict__ cand, int cap, float thr, int k, int64_t id_offset,
+                               int64_t *__restrict__ out_ids, float *__restrict__ out_scores, int *status) {
+  extern __shared__ float sh[];
+  float *sq = sh;                                  // [dim]
+  float *sc = sq + ((dim + 3) & ~3);               // [cap]
+  int *sid = reinterpret_cast<int *>(sc + cap);    // [cap]
+  __shared__ float red_s[32];
+  __shared__ int red_i[32];
+  __shared__ int red_p[32];
+  const int q = blockIdx.x;
+  const int tid = threadIdx.x, lane = tid % 32, warp = tid / 32, nwarps = blockDim.x / 32;
+  int n = count[q];
+  if (n > cap) {
+    if (tid == 0) atomicOr(status, 1);
+    n = 0;  // results for this query are withheld (reported as overflow)
+  }
+  for (int i = tid; i < dim; i += blockDim.x) sq[i] = qn[(int64_t)q * dim + i];
+  __syncthreads();
+  for (int i = warp; i < n; i += nwarps) {
+    const int j = cand[(int64_t)q * cap + i];
+    const float *e = emb + (int64_t)j * ld_emb;
+    double acc = 0.0;
+    for (int d = lane; d < dim; d += 32) acc = fma((double)sq[d], (double)e[d], acc);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if (lane == 0) {
+      const float s = (float)acc;
+      sc[i] = s >= thr ? s : -INFINITY;
+      sid[i] = j;
+    }
+  }
+  __syncthreads();
+  for (int r = 0; r < k; ++r) {
+    float bs = -INFINITY;
+    int bi = INT_MAX, bp = -1;
+    for (int i = tid; i < n; i += blockDim.x) {
+      const float s = sc[i];
+      const int id = sid[i];
+      if (s > bs || (s == bs && s > -INFINITY && id < bi)) bs = s, bi = id, bp = i;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float os = __shfl_xor_sync(0xffffffffu, bs, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      const int op = __shfl_xor_sync(0xffffffffu, bp, o);
+      if (os > bs || (os == bs && oi < bi)) bs = os, bi = oi, bp = op;
+    }
+    if (lane == 0) red_s[warp] = bs, red_i[warp] = bi, red_p[warp] = bp;
+    __syncthreads();
+    if (warp == 0) {
+      bs = lane < nwarps ? red_s[lane] : -INFINITY;
+      bi = lane < nwarps ? red_i[lane] : INT_MAX;
+      bp = lane < nwarps ? red_p[lane] : -1;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float os = __shfl_xor_sync(0xffffffffu, bs, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        const int op = __shfl_xor_sync(0xffffffffu, bp, o);
+        if (os > bs || (os == bs && oi < bi)) bs = os, bi = oi, bp = op;
+      }
+      if (lane == 0) {
+        const bool hit = bs > -INFINITY;
+        out_ids[(int64_t)q * k + r] = hit ? (int64_t)bi + id_offset : -1;
+        out_scores[(int64_t)q * k + r] = hit ? bs : -INFINITY;
+        if (hit) sc[bp] = -INFINITY;
+      }
+    }
+    __syncthreads();
+  }
+}
+
+__global__ void fill_empty_kernel(int64_t *ids, float *scores, int64_t n) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) ids[i] = -1, scores[i] = -INFINITY;
+}
+
+__global__ void prepare_rows_kernel(const float *__restrict__ emb, int64_t ld_emb, __nv_bfloat16 *__restrict__ eb,
+                                    int64_t ld_b, int dim, int dim_pad, const int64_t *__restrict__ rows,
+                                    int64_t row_begin, int64_t n, float *stats) {
+  const int64_t w = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) / 32;
+  const int lane = threadIdx.x % 32;
+  if (w >= n) return;
+  const int64_t r = rows != nullptr ? rows[w] : row_begin + w;
+  const float *e = emb + r * ld_emb;
+  float nb = 0.f, nd = 0.f;
+  for (int i = lane; i < dim_pad; i += 32) {
+    const float v = i < dim ? e[i] : 0.f;
+    const __nv_bfloat16 b = __float2bfloat16_rn(v);
+    eb[r * ld_b + i] = b;
+    const float bf = __bfloat162float(b);
+    nb = fmaf(bf, bf, nb);
+    nd = fmaf(v - bf, v - bf, nd);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    nb += __shfl_xor_sync(0xffffffffu, nb, o);
+    nd += __shfl_xor_sync(0xffffffffu, nd, o);
+  }
+  if (lane == 0) {
+    // non-negative floats order like their bit patterns
+    atomicMax(reinterpret_cast<int *>(&stats[0]), __float_as_int(sqrtf(nd) * 1.0001f));
+    atomicMax(reinterpret_cast<int *>(&stats[1]), __float_as_int(sqrtf(nb) * 1.0001f));
+  }
+}
+
+// Merge n_lists sorted top-k lists per query (shards of a row-partitioned
+// search) into one, by (score desc, id asc).
+__global__ void topk_merge_kernel(const int64_t *__restrict__ ids, const float *__restrict__ scores, int n_lists,
+                                  int nq, int k, int64_t *__restrict__ out_ids, float *__restrict__ out_scores) {
+  const int q = blockIdx.x * blockDim.x + threadIdx.x;
+  if (q >= nq) return;
+  int head[16];
+  for (int l = 0; l < n_lists; ++l) head[l] = 0;
+  for (int r = 0; r < k; ++r) {
+    int best = -1;
+    float bs = -INFINITY;
+    int64_t bi = INT64_MAX;
+    for (int l = 0; l < n_lists; ++l) {
+      if (head[l] >= k) continue;
+      const int64_t off = ((int64_t)l * nq + q) * k + head[l];
+      const int64_t id = ids[off];
+      const float s = scores[off];
+      if (id < 0) continue;
+      if (s > bs || (s == bs && id < bi)) bs = s, bi = id, best = l;
+    }
+    if (best < 0) {
+      out_ids[(int64_t)q * k + r] = -1;
+      out_scores[(int64_t)q * k + r] = -INFINITY;
+    } else {
+      out_ids[(int64_t)q * k + r] = bi;
+      out_scores[(int64_t)q * k + r] = bs;
+      ++head[best];
+    }
+  }
+}
+
+inline int64_t align256(int64_t x) { return (x + 255) & ~int64_t(255); }
+
+struct Workspace {
+  int *count, *lower;
+  float *delta, *qn;
+  __nv_bfloat16 *qb;
+  int *cand;
+  int64_t bytes;
+};
+
+Workspace carve(void *base, int nq, int dim, int dim_pad, int cap) {
+  Workspace w;
+  char *p = reinterpret_cast<char *>(base);
+  int64_t off = 0;
+  auto take = [&](int64_t bytes) {
+    char *r = p ? p + off : nullptr;
+    off += align256(bytes);
+    return r;
+  };
+  w.count = reinterpret_cast<int *>(take(4LL * nq));
+  w.lower = reinterpret_cast<int *>(take(4LL * nq));
+  w.delta = reinterpret_cast<float *>(take(4LL * nq));
+  w.qn = reinterpret_cast<float *>(take(4LL * nq * dim));
+  w.qb = reinterpret_cast<__nv_bfloat16 *>(take(2LL * nq * dim_pad));
+  w.cand = reinterpret_cast<int *>(take(4LL * nq * cap));
+  w.bytes = off;
+  return w;
+}
+
+int sm_count() {
+  int dev = 0, n = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 148;
+  return n > 0 ? n : 148;
+}
+
+template <int KT>
+int launch_screen(const CUtensorMap &tq, const CUtensorMap &te, const ScreenParams &P, int grid, int smem,
+                  cudaStream_t st) {
+  cudaError_t e = cudaFuncSetAttribute(screen_kernel<KT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) {
+    set_last_cuda_error(e);
+    return SB_ERR_CUDA;
+  }
+  screen_kernel<KT><<<grid, kThreads, smem, st>>>(tq, te, P);
+  return launch_status();
+}
+
+}  // namespace
+}  // namespace sb
+
+extern "C" SB_API int sb_search_prepare_rows(const float *emb, int64_t ld_emb, uint16_t *emb_bf16, int64_t ld_bf16,
+                                             int32_t dim, int32_t dim_pad, const int64_t *rows, int64_t row_begin,
+                                             int64_t n_rows, float *stats, void *stream) {
+  if (n_rows < 0 || dim <= 0 || dim_pad < dim || ld_emb < dim || ld_bf16 < dim_pad) return SB_ERR_INVALID_ARGUMENT;
+  if (n_rows == 0) return SB_OK;
+  if (emb == nullptr || emb_bf16 == nullptr || stats == nullptr) return SB_ERR_INVALID_ARGUMENT;
+  const int64_t threads = 256, warps_per_block = threads / 32;
+  const int64_t blocks = (n_rows + warps_per_block - 1) / warps_per_block;
+  sb::prepare_rows_kernel<<<(unsigned)blocks, (unsigned)threads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      emb, ld_emb, reinterpret_cast<__nv_bfloat16 *>(emb_bf16), ld_bf16, dim, dim_pad, rows, row_begin, n_rows,
+      stats);
+  return sb::launch_status();
+}
+
+extern "C" SB_API int64_t sb_cosine_topk_workspace_bytes(int32_t n_queries, int32_t dim, int32_t dim_pad,
+                                                         int32_t capacity) {
+  if (n_queries < 0 || dim <= 0 || dim_pad < dim || capacity <= 0) return -1;
+  return sb::carve(nullptr, n_queries, dim, dim_pad, capacity).bytes;
+}
+
+extern "C" SB_API int sb_cosine_topk(const float *emb, int64_t ld_emb, const uint16_t *emb_bf16, int64_t ld_bf16,
+                                     const uint8_t *valid, int64_t n_rows, int32_t dim, int32_t dim_pad,
+                                     const float *stats, const float *queries, int64_t ld_q, int32_t n_queries,
+                                     int32_t k, float min_similarity, int64_t id_offset, int64_t *out_ids,
+                                     float *out_scores, int32_t capacity, void *workspace, int64_t workspace_bytes,
+                                     int32_t *status, void *stream) {
+  using namespace sb;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (n_queries < 0 || n_rows < 0 || k < 1 || k > 32 || dim <= 0) return SB_ERR_INVALID_ARGUMENT;
+  if (dim_pad < dim || dim_pad % kBK != 0 || dim_pad > 512) return SB_ERR_UNSUPPORTED;
+  if (capacity < k || capacity > 16384) return SB_ERR_INVALID_ARGUMENT;
+  if (n_rows > 0x7fffffffLL) return SB_ERR_TOO_LARGE;
+  if (n_queries == 0) return SB_OK;
+  if (queries == nullptr || out_ids == nullptr || out_scores == nullptr || status == nullptr || stats == nullptr)
+    return SB_ERR_INVALID_ARGUMENT;
+  if (ld_q < dim || ld_emb < dim || ld_bf16 < dim_pad) return SB_ERR_INVALID_ARGUMENT;
+  if ((reinterpret_cast<uintptr_t>(emb_bf16) % 16) || ((ld_bf16 * 2) % 16)) return SB_ERR_INVALID_ARGUMENT;
+  Workspace w = carve(workspace, n_queries, dim, dim_pad, capacity);
+  if (workspace == nullptr || workspace_bytes < w.bytes) return SB_ERR_WORKSPACE_TOO_SMALL;
+  if (n_rows == 0) {
+    const int64_t n = (int64_t)n_queries * k;
+    fill_empty_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(out_ids, out_scores, n);
+    return launch_status();
+  }
+  if (emb == nullptr || emb_bf16 == nullptr) return SB_ERR_INVALID_ARGUMENT;
+
+  {
+    const int threads = 256;
+    const int blocks = (n_queries * 32 + threads - 1) / threads;
+    query_prep_kernel<<<blocks, threads, 0, st>>>(queries, ld_q, n_queries, dim, dim_pad, stats, w.qn, w.qb,
+                                                  w.delta, w.count, w.lower);
+    int s = launch_status();
+    if (s != SB_OK) return s;
+  }
+
+  CUtensorMap tq, te;
+  if (!make_tmap_bf16_2d(&tq, w.qb, dim_pad, n_queries, (uint64_t)dim_pad * 2, kBK, kBM) ||
+      !make_tmap_bf16_2d(&te, emb_bf16, dim_pad, n_rows, (uint64_t)ld_bf16 * 2, kBK, kBN))
+    return SB_ERR_CUDA;
+
+  ScreenParams P;
+  P.nq = n_queries;
+  P.k_blocks = dim_pad / kBK;
+  P.n_qtiles = (n_queries + kBM - 1) / kBM;
+  P.n_rows = n_rows;
+  P.n_ntiles = (n_rows + kBN - 1) / kBN;
+  const int64_t n_chunks = (P.n_ntiles + kTilesPerChunk - 1) / kTilesPerChunk;
+  P.n_units = n_chunks * P.n_qtiles;
+  P.thr = min_similarity;
+  P.cap = capacity;
+  P.valid = valid;
+  P.delta = w.delta;
+  P.count = w.count;
+  P.lower = w.lower;
+  P.cand = w.cand;
+  P.status = status;
+  const int fixed = 1024 + P.k_blocks * kQBlockBytes + 256;
+  P.stages = std::min<int>(kMaxStages, (kSmemLimit - fixed) / kEStageBytes);
+  if (P.stages < 2) return SB_ERR_UNSUPPORTED;
+  const int smem = fixed + P.stages * kEStageBytes;
+  const int grid = (int)std::min<int64_t>(sm_count(), P.n_units);
+  int s;
+  if (k <= 8)
+    s = launch_screen<8>(tq, te, P, grid, smem, st);
+  else if (k <= 16)
+    s = launch_screen<16>(tq, te, P, grid, smem, st);
+  else
+    s = launch_screen<32>(tq, te, P, grid, smem, st);
+  if (s != SB_OK) return s;
+
+  const int rs_smem = (int)(((dim + 3) & ~3) * 4 + (int64_t)capacity * 8);
+  if (rs_smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(rescore_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, rs_smem);
+    if (e != cudaSuccess) {
+      set_last_cuda_error(e);
+      return SB_ERR_CUDA;
+    }
+  }
+  rescore_kernel<<<n_queries, 256, rs_smem, st>>>(emb, ld_emb, dim, w.qn, w.count, w.cand, capacity,
+                                                  min_similarity, k, id_offset, out_ids, out_scores, status);
+  return launch_status();
+}
+
+extern "C" SB_API int sb_topk_merge(const int64_t *ids, const float *scores, int32_t n_lists, int32_t n_queries,
+                                    int32_t k, int64_t *out_ids, float *out_scores, void *stream) {
+  if (n_lists < 1 || n_lists > 16 || n_queries < 0 || k < 1) return SB_ERR_INVALID_ARGUMENT;
+  if (n_queries == 0) return SB_OK;
+  if (!ids || !scores || !out_ids || !out_scores) return SB_ERR_INVALID_ARGUMENT;
+  sb::topk_merge_kernel<<<(n_queries + 127) / 128, 128, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      ids, scores, n_lists, n_queries, k, out_ids, out_scores);
+  return sb::launch_status();
+}

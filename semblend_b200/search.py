@@ -1,0 +1,190 @@
+"""Device-resident donor embedding matrix and exact cosine top-k search.
+
+:class:`DeviceDonorMatrix` mirrors the reference DonorStore's row storage
+(``_embeddings [max_entries, dim]`` fp32 and ``_valid_mask``,
+semblend_core/donor_store.py:95-96) in HBM, plus the bf16 screening copy and
+the rounding statistics the tensor-core search needs.  :meth:`search` runs
+``sb_cosine_topk`` — the reference's per-query stage (normalise, cosine,
+threshold, top-k; donor_store.py:323-341) for a whole batch of queries.
+
+Results are exact: every returned similarity is an fp32 dot product of the
+normalised query with the stored fp32 row, and the returned rows are the
+``k`` best rows with similarity ``>= min_similarity`` ordered by (similarity
+descending, row ascending); ``-1`` / ``-inf`` pad queries with fewer hits.
+"""
+
+from __future__ import annotations
+
+import threading
+
+import numpy as np
+import torch
+
+from . import _lib
+
+DEFAULT_CAPACITY = 4096  # screening candidates kept per query before rescoring
+
+
+def _pad64(d: int) -> int:
+    return (d + 63) // 64 * 64
+
+
+class DeviceDonorMatrix:
+    """Fixed-capacity fp32 row matrix on one CUDA device with a bf16 shadow."""
+
+    def __init__(self, max_entries: int, dim: int, device: torch.device | str | int | None = None):
+        if device is None:
+            device = torch.device("cuda", torch.cuda.current_device())
+        self.device = torch.device(device) if not isinstance(device, int) else torch.device("cuda", device)
+        if self.device.type != "cuda":
+            raise _lib.NativeLibraryError("DeviceDonorMatrix needs a CUDA device (there is no CPU search path)")
+        self.max_entries = int(max_entries)
+        self.dim = int(dim)
+        self.dim_pad = _pad64(self.dim)
+        if self.dim_pad > 512:
+            raise ValueError(f"embedding dim {dim} > 512 is not supported by the search kernel")
+        self.emb = torch.zeros(self.max_entries, self.dim, dtype=torch.float32, device=self.device)
+        self.emb_bf16 = torch.zeros(self.max_entries, self.dim_pad, dtype=torch.bfloat16, device=self.device)
+        self.valid = torch.zeros(self.max_entries, dtype=torch.uint8, device=self.device)
+        # [max ||e - bf16(e)||, max ||bf16(e)||] over rows ever written (upper bounds)
+        self.stats = torch.zeros(2, dtype=torch.float32, device=self.device)
+        self._ws: torch.Tensor | None = None
+        self._status = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self._lock = threading.Lock()
+
+    # -- row updates -----------------------------------------------------------
+    def write_rows(self, rows: torch.Tensor | np.ndarray | list[int], values) -> None:
+        """Store fp32 ``values [n, dim]`` at row indices ``rows`` and mark them valid."""
+        rows_t = torch.as_tensor(np.asarray(rows, dtype=np.int64)).to(self.device, non_blocking=True)
+        vals = torch.as_tensor(values, dtype=torch.float32).reshape(-1, self.dim)
+        if vals.shape[0] != rows_t.shape[0]:
+            raise ValueError("rows and values disagree in length")
+        if rows_t.numel() == 0:
+            return
+        vals = vals.to(self.device, non_blocking=True)
+        self.emb.index_copy_(0, rows_t, vals)
+        self.valid.index_fill_(0, rows_t, 1)
+        self._prepare(rows_t)
+
+    def write_range(self, begin: int, values: torch.Tensor) -> None:
+        """Store contiguous rows ``[begin, begin + n)`` from a device or host tensor."""
+        n = values.shape[0]
+        if n == 0:
+            return
+        self.emb[begin : begin + n].copy_(values, non_blocking=True)
+        self.valid[begin : begin + n] = 1
+        lib = _lib.load()
+        _lib.check(
+            lib.sb_search_prepare_rows(
+                self.emb.data_ptr(), self.dim, self.emb_bf16.data_ptr(), self.dim_pad, self.dim, self.dim_pad,
+                None, begin, n, self.stats.data_ptr(), _lib.stream_ptr(self.device),
+            ),
+            "sb_search_prepare_rows",
+        )
+
+    def invalidate(self, rows) -> None:
+        rows_t = torch.as_tensor(np.asarray(rows, dtype=np.int64)).to(self.device, non_blocking=True)
+        if rows_t.numel():
+            self.valid.index_fill_(0, rows_t, 0)
+
+    def _prepare(self, rows_t: torch.Tensor) -> None:
+        lib = _lib.load()
+        _lib.check(
+            lib.sb_search_prepare_rows(
+                self.emb.data_ptr(), self.dim, self.emb_bf16.data_ptr(), self.dim_pad, self.dim, self.dim_pad,
+                rows_t.data_ptr(), 0, rows_t.shape[0], self.stats.data_ptr(), _lib.stream_ptr(self.device),
+            ),
+            "sb_search_prepare_rows",
+        )
+
+    # -- search ------------------------------------------------------------------
+    def search(self, queries, k: int, min_similarity: float, *, n_rows: int | None = None,
+               id_offset: int = 0, capacity: int = DEFAULT_CAPACITY) -> tuple[torch.Tensor, torch.Tensor]:
+        """Top-``k`` rows per query (see module docstring); returns device
+        tensors ``ids [Q, k]`` (int64, ``+ id_offset``) and ``scores [Q, k]``."""
+        q = torch.as_tensor(queries)
+        if q.ndim == 1:
+            q = q.unsqueeze(0)
+        if q.shape[-1] != self.dim:
+            raise ValueError(f"query dim {q.shape[-1]} != store dim {self.dim}")
+        q = q.to(device=self.device, dtype=torch.float32, non_blocking=True).contiguous()
+        n_rows = self.max_entries if n_rows is None else int(n_rows)
+        return cosine_topk(
+            self.emb, self.emb_bf16, self.valid, self.stats, q, k, min_similarity, n_rows=n_rows,
+            id_offset=id_offset, capacity=capacity, status=self._status, workspace_owner=self,
+        )
+
+
+def _workspace(owner, nbytes: int, device: torch.device) -> torch.Tensor:
+    ws = getattr(owner, "_ws", None) if owner is not None else None
+    if ws is None or ws.numel() < nbytes:
+        ws = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=device)
+        if owner is not None:
+            owner._ws = ws
+    return ws
+
+
+def cosine_topk(emb: torch.Tensor, emb_bf16: torch.Tensor, valid: torch.Tensor | None, stats: torch.Tensor,
+                queries: torch.Tensor, k: int, min_similarity: float, *, n_rows: int | None = None,
+                id_offset: int = 0, capacity: int = DEFAULT_CAPACITY, status: torch.Tensor | None = None,
+                workspace_owner=None) -> tuple[torch.Tensor, torch.Tensor]:
+    """Functional form of :meth:`DeviceDonorMatrix.search` over raw tensors.
+
+    Retries with a 4x larger candidate capacity if screening overflowed it
+    (many near-ties); raises if the kernel reports a wait timeout.
+    """
+    for t, name in ((emb, "emb"), (emb_bf16, "emb_bf16"), (queries, "queries"), (stats, "stats")):
+        _lib.require_cuda(t, name)
+    dev = emb.device
+    nq, dim = queries.shape
+    n_rows = emb.shape[0] if n_rows is None else n_rows
+    dim_pad = emb_bf16.shape[1]
+    k = int(k)
+    if not 1 <= k <= 32:
+        raise ValueError(f"k must be in [1, 32], got {k}")
+    ids = torch.empty(nq, k, dtype=torch.int64, device=dev)
+    scores = torch.empty(nq, k, dtype=torch.float32, device=dev)
+    if status is None:
+        status = torch.zeros(1, dtype=torch.int32, device=dev)
+    lib = _lib.load()
+    cap = max(int(capacity), k)
+    while True:
+        nbytes = lib.sb_cosine_topk_workspace_bytes(nq, dim, dim_pad, cap)
+        ws = _workspace(workspace_owner, nbytes, dev)
+        status.zero_()
+        _lib.check(
+            lib.sb_cosine_topk(
+                emb.data_ptr(), emb.stride(0), emb_bf16.data_ptr(), emb_bf16.stride(0),
+                valid.data_ptr() if valid is not None else None, n_rows, dim, dim_pad, stats.data_ptr(),
+                queries.data_ptr(), queries.stride(0), nq, k, float(min_similarity), int(id_offset),
+                ids.data_ptr(), scores.data_ptr(), cap, ws.data_ptr(), ws.numel(), status.data_ptr(),
+                _lib.stream_ptr(dev),
+            ),
+            "sb_cosine_topk",
+        )
+        st = int(status.item())
+        if st & ~1:
+            raise _lib.NativeLibraryError(f"sb_cosine_topk: kernel wait timed out (code {st})")
+        if st & 1 and cap < 16384:
+            cap = min(cap * 4, 16384)
+            continue
+        if st & 1:
+            raise _lib.NativeLibraryError("sb_cosine_topk: more than 16384 screening candidates for a query")
+        return ids, scores
+
+
+def merge_topk(ids: torch.Tensor, scores: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """Merge per-shard sorted lists ``[n_lists, Q, k]`` into ``[Q, k]`` by
+    (score desc, id asc) with ``sb_topk_merge``."""
+    _lib.require_cuda(ids, "ids")
+    n_lists, nq, k = ids.shape
+    ids_c, scores_c = ids.contiguous(), scores.to(torch.float32).contiguous()
+    out_i = torch.empty(nq, k, dtype=torch.int64, device=ids.device)
+    out_s = torch.empty(nq, k, dtype=torch.float32, device=ids.device)
+    lib = _lib.load()
+    _lib.check(
+        lib.sb_topk_merge(ids_c.data_ptr(), scores_c.data_ptr(), n_lists, nq, k,
+                          out_i.data_ptr(), out_s.data_ptr(), _lib.stream_ptr(ids.device)),
+        "sb_topk_merge",
+    )
+    return out_i, out_s

@@ -1,0 +1,182 @@
+"""GPU parity of the tensor-core cosine top-k search against the CPU oracle
+(the reference's per-query numpy stage) and the DonorStore golden fixture.
+
+Bar: returned rows equal the oracle's except where similarities tie within
+1e-6; every similarity within 1e-6 of the oracle's fp32 value.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import search as osearch
+from semblend_b200 import donor_store as ds
+from semblend_b200.search import DeviceDonorMatrix, merge_topk
+from tests.helpers import load_golden
+
+pytestmark = pytest.mark.gpu
+DEV = torch.device("cuda", 0)
+TOL = 1e-6
+
+
+def exact_scores(E: np.ndarray, q: np.ndarray, ids: np.ndarray) -> np.ndarray:
+    qn = osearch.normalize_query(q)
+    return np.array([float(E[i] @ qn) if i >= 0 else -np.inf for i in ids], dtype=np.float64)
+
+
+def assert_topk_equivalent(E, valid, Q, thr, ids_g, s_g, k):
+    ids_o, s_o = osearch.topk_batch(E, valid, Q, thr, k)
+    for qi in range(Q.shape[0]):
+        go, gg = ids_o[qi], ids_g[qi]
+        so, sg = s_o[qi].astype(np.float64), s_g[qi].astype(np.float64)
+        no, ng = int((go >= 0).sum()), int((gg >= 0).sum())
+        if no != ng:
+            # only a similarity within TOL of the threshold may flip membership
+            extra = so[ng:no] if no > ng else sg[no:ng]
+            assert np.all(np.abs(extra - thr) <= TOL), (qi, no, ng, extra)
+        n = min(no, ng)
+        assert np.all(np.abs(so[:n] - sg[:n]) <= TOL), (qi, so[:n], sg[:n])
+        assert len(set(gg[:ng].tolist())) == ng, "duplicate ids"
+        if ng:
+            assert np.all(valid[gg[:ng]]), "invalid row returned"
+            ex = exact_scores(E, Q[qi], gg[:ng])
+            assert np.all(np.abs(ex - sg[:ng]) <= TOL)
+        for r in range(n):
+            if go[r] != gg[r]:
+                assert abs(so[r] - sg[r]) <= TOL, (qi, r)
+
+
+def clustered(n, dim, n_centers, seed, sigma=0.3):
+    rng = np.random.default_rng(seed)
+    centers = rng.standard_normal((n_centers, dim)).astype(np.float32)
+    lab = rng.integers(0, n_centers, n)
+    E = centers[lab] + sigma * rng.standard_normal((n, dim)).astype(np.float32)
+    E /= np.linalg.norm(E, axis=1, keepdims=True)
+    return E.astype(np.float32), centers, rng
+
+
+def queries_for(centers, rng, nq, dim, frac_cluster=0.7, sigma=0.3):
+    nc = int(round(frac_cluster * nq))
+    lab = rng.integers(0, centers.shape[0], nc)
+    Qc = centers[lab] + sigma * rng.standard_normal((nc, dim)).astype(np.float32)
+    Qu = rng.standard_normal((nq - nc, dim)).astype(np.float32)
+    Q = np.concatenate([Qc, Qu]) * rng.uniform(0.5, 3.0, (nq, 1)).astype(np.float32)  # un-normalised
+    return Q.astype(np.float32)
+
+
+def build(E, valid=None):
+    m = DeviceDonorMatrix(E.shape[0], E.shape[1], DEV)
+    m.write_range(0, torch.from_numpy(E).to(DEV))
+    if valid is not None:
+        m.invalidate(np.where(~valid)[0])
+    return m
+
+
+@pytest.mark.parametrize("k", [1, 5, 8, 10, 16, 32])
+def test_clustered_vs_oracle(k):
+    E, centers, rng = clustered(20000, 384, 64, seed=k)
+    Q = queries_for(centers, rng, 300, 384)
+    m = build(E)
+    ids, s = m.search(Q, k, 0.6)
+    valid = np.ones(E.shape[0], bool)
+    assert_topk_equivalent(E, valid, Q, 0.6, ids.cpu().numpy(), s.cpu().numpy(), k)
+
+
+def test_valid_mask_ragged_sizes():
+    E, centers, rng = clustered(9999, 384, 16, seed=3)
+    valid = rng.random(9999) > 0.3
+    Q = queries_for(centers, rng, 129, 384)
+    m = build(E, valid)
+    ids, s = m.search(Q, 8, 0.5)
+    assert_topk_equivalent(E, valid, Q, 0.5, ids.cpu().numpy(), s.cpu().numpy(), 8)
+
+
+@pytest.mark.parametrize("dim", [64, 100, 128, 512])
+def test_other_dims(dim):
+    E, centers, rng = clustered(3000, dim, 8, seed=dim)
+    Q = queries_for(centers, rng, 50, dim)
+    m = build(E)
+    ids, s = m.search(Q, 8, 0.4)
+    assert_topk_equivalent(E, np.ones(3000, bool), Q, 0.4, ids.cpu().numpy(), s.cpu().numpy(), 8)
+
+
+def test_single_query_and_no_hits():
+    E, centers, rng = clustered(1000, 384, 4, seed=5)
+    m = build(E)
+    ids, s = m.search(rng.standard_normal(384).astype(np.float32), 5, 0.99)
+    assert ids.shape == (1, 5) and torch.all(ids == -1) and torch.all(torch.isinf(s))
+    zero = np.zeros((2, 384), np.float32)  # norm 0: q / (0 + 1e-8) = 0, all similarities 0
+    ids, s = m.search(zero, 3, 0.6)
+    assert torch.all(ids == -1)
+    ids, s = m.search(zero, 3, -0.5)
+    assert torch.equal(ids.cpu(), torch.tensor([[0, 1, 2], [0, 1, 2]]))
+
+
+def test_many_exact_ties_overflow_and_retry():
+    rng = np.random.default_rng(7)
+    v = rng.standard_normal(384).astype(np.float32)
+    v /= np.linalg.norm(v)
+    E = np.repeat(v[None, :], 6000, axis=0)  # 6000 identical rows: more candidates than the default capacity
+    m = build(E)
+    ids, s = m.search(v[None, :], 8, 0.6)
+    assert ids.cpu().tolist() == [list(range(8))]
+    assert np.allclose(s.cpu().numpy(), float(E[0] @ osearch.normalize_query(v)), atol=TOL)
+
+
+def test_empty_store_rows():
+    m = DeviceDonorMatrix(100, 384, DEV)  # nothing written: all rows invalid
+    ids, _ = m.search(np.ones((3, 384), np.float32), 4, 0.0)
+    assert torch.all(ids == -1)
+
+
+def test_sharded_merge_equals_full_search():
+    E, centers, rng = clustered(12000, 384, 32, seed=9)
+    Q = queries_for(centers, rng, 200, 384)
+    full = build(E)
+    ids_f, s_f = full.search(Q, 8, 0.6)
+    bounds = [0, 3500, 8000, 12000]
+    parts_i, parts_s = [], []
+    for a, b in zip(bounds[:-1], bounds[1:]):
+        m = build(E[a:b])
+        i, s = m.search(Q, 8, 0.6, id_offset=a)
+        parts_i.append(i)
+        parts_s.append(s)
+    mi, ms = merge_topk(torch.stack(parts_i), torch.stack(parts_s))
+    assert torch.equal(mi, ids_f)
+    assert torch.equal(ms, s_f)
+
+
+def test_donor_store_golden():
+    g = load_golden("donor_store")
+
+    class _A:
+        reuse_ratio = 1.0
+
+    store = ds.DonorStore(max_entries=300, embedding_dim=384, min_similarity=0.6, device=DEV,
+                          alignment=(lambda *a, **k: 1.0, lambda *a, **k: _A()))
+    for i, (rid, emb, none) in enumerate(zip(g["add_ids"].tolist(), g["add_embeddings"].numpy(),
+                                             g["add_is_none"].numpy())):
+        store.add_donor(ds.DonorNode(request_id=rid, token_ids=[i, i + 1, i + 2],
+                                     embedding=None if none else emb, timestamp=0.0))
+    assert np.array_equal(store._embeddings, g["embeddings"].numpy())
+    assert np.array_equal(store._valid_mask, g["valid"].numpy())
+    for qi, q in enumerate(g["queries"].numpy()):
+        ms = store.find_donors(q, query_tokens=[-1], top_k=4, min_reuse_ratio=0.0)
+        want = [x for x in g["result_ids"][qi].tolist() if x]
+        assert [m.donor.request_id for m in ms] == want
+        np.testing.assert_allclose([m.similarity for m in ms], g["result_sims"][qi].numpy()[: len(want)], atol=TOL)
+
+
+def test_donor_store_batch_add_matches_sequential():
+    rng = np.random.default_rng(2)
+    nodes = [ds.DonorNode(f"r{i % 70}", [i], rng.standard_normal(64).astype(np.float32), 0.0) for i in range(150)]
+    a = ds.DonorStore(max_entries=50, embedding_dim=64, device=DEV)
+    b = ds.DonorStore(max_entries=50, embedding_dim=64, device=DEV)
+    for n in nodes:
+        a.add_donor(n)
+    b.add_donors(nodes)
+    assert np.array_equal(a._embeddings, b._embeddings)
+    assert np.array_equal(a._valid_mask, b._valid_mask)
+    assert torch.equal(a.device_matrix.valid.cpu().bool(), torch.from_numpy(a._valid_mask))
