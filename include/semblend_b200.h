@@ -233,6 +233,15 @@ SB_API int sb_version(void);
  * none), for diagnosing SB_ERR_CUDA. */
 SB_API int sb_last_cuda_error(void);
 
+/* Timing of the dominant kernel of each later call (inject_kernel for
+ * sb_inject / sb_permute_paged, the tensor-core screening kernel for
+ * sb_cosine_topk): CUDA events are recorded on the launch stream around each
+ * of the next max_launches such launches.  sb_profile_stop synchronises on
+ * them, reports the summed milliseconds and the number of launches timed, and
+ * turns timing off. */
+SB_API int sb_profile_start(int32_t max_launches);
+SB_API int sb_profile_stop(float *total_ms, int32_t *n_launches);
+
 /* Failure-detection self-test: launches one CTA that waits on an mbarrier
  * nothing arrives on, gives up after max_cycles clock cycles and writes 7 to
  * *status (device int32, zeroed by the caller), the way every pipelined

@@ -115,6 +115,8 @@ _SIGNATURES: dict[str, tuple] = {
         [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_void_p,
          ctypes.c_void_p, ctypes.c_void_p],
     ),
+    "sb_profile_start": (ctypes.c_int, [ctypes.c_int32]),
+    "sb_profile_stop": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p]),
     "sb_selftest_wait_timeout": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p]),
     "sb_status_string": (ctypes.c_char_p, [ctypes.c_int]),
     "sb_version": (ctypes.c_int, []),
@@ -246,3 +248,28 @@ def inv_freq(rope_base: float, head_dim: int, device: torch.device) -> torch.Ten
         with _state_lock:
             _inv_freq_cache[key] = t
     return t
+
+
+class KernelTimer:
+    """Times the dominant kernel of the C-ABI calls made inside the ``with``
+    block (CUDA events on the launch stream, recorded by the library)."""
+
+    def __init__(self, max_launches: int = 4096):
+        self.max_launches = max_launches
+        self.total_ms = 0.0
+        self.launches = 0
+
+    def __enter__(self):
+        check(load().sb_profile_start(self.max_launches), "sb_profile_start")
+        return self
+
+    def __exit__(self, *exc):
+        ms = ctypes.c_float()
+        n = ctypes.c_int32()
+        check(load().sb_profile_stop(ctypes.byref(ms), ctypes.byref(n)), "sb_profile_stop")
+        self.total_ms, self.launches = float(ms.value), int(n.value)
+        return False
+
+    @property
+    def mean_ms(self) -> float:
+        return self.total_ms / self.launches if self.launches else float("nan")

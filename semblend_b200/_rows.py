@@ -119,6 +119,10 @@ def paged_rows(
         base, layer_ptrs = kv_cache.data_ptr(), None
     nb, nh, bs, hd = paged_geometry(per_shape, layout)
     b, kv, h, p, d = _AXES[layout]
+    # a dimension of size 1 is only ever indexed at 0 and may carry any stride
+    per_stride = [0 if n == 1 else st for n, st in zip(per_shape, per_stride)]
+    if n_layers == 1:
+        stride_layer = 0
     rows = _lib.SbRows()
     rows.base = base
     rows.layer_ptrs = layer_ptrs
@@ -146,7 +150,7 @@ def flat_rows(
     dim_axis: int,
 ) -> _lib.SbRows:
     """Describe a flat (unpaged) KV tensor by the axes of its dimensions."""
-    s = t.stride()
+    s = [0 if n == 1 else st for n, st in zip(t.shape, t.stride())]  # size-1 dims: any stride
     rows = _lib.SbRows()
     rows.base = t.data_ptr()
     rows.layer_ptrs = None

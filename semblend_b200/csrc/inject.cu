@@ -21,6 +21,7 @@
 #include <algorithm>
 
 #include "common.cuh"
+#include "prof.cuh"
 
 namespace sb {
 namespace {
@@ -289,10 +290,12 @@ int pick_vec(const sb_inject_desc *descs, int n, int D, int es) {
 
 template <typename T, int VEC, int MAXD>
 int launch_typed(const InjectLaunch<MAXD> &L, dim3 grid, cudaStream_t st) {
+  const int slot = prof_before(st);
   if (L.p.k_angle == SB_ANGLE_NOPE && (L.p.kv_select & SB_KV_K))
     inject_kernel<T, VEC, MAXD, true><<<grid, kThreads, 0, st>>>(L);
   else
     inject_kernel<T, VEC, MAXD, false><<<grid, kThreads, 0, st>>>(L);
+  prof_after(slot, st);
   return launch_status();
 }
 

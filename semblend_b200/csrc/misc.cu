@@ -1,5 +1,9 @@
-// Status strings, version and error bookkeeping of the C ABI.
+// Status strings, version, error bookkeeping and kernel timing of the C ABI.
+#include <mutex>
+#include <vector>
+
 #include "common.cuh"
+#include "prof.cuh"
 
 namespace sb {
 namespace {
@@ -56,4 +60,67 @@ extern "C" SB_API int sb_selftest_wait_timeout(int32_t *status, int64_t max_cycl
   if (status == nullptr || max_cycles <= 0) return SB_ERR_INVALID_ARGUMENT;
   sb::wait_timeout_selftest_kernel<<<1, 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>(status, max_cycles, 7);
   return sb::launch_status();
+}
+
+// ---------------------------------------------------------------------------
+// Dominant-kernel timing
+// ---------------------------------------------------------------------------
+namespace sb {
+namespace {
+std::mutex g_prof_mu;
+bool g_prof_on = false;
+int g_prof_used = 0;
+std::vector<cudaEvent_t> g_prof_ev;  // pairs: before, after
+}  // namespace
+
+int prof_before(cudaStream_t st) {
+  std::lock_guard<std::mutex> lk(g_prof_mu);
+  if (!g_prof_on || 2 * (g_prof_used + 1) > (int)g_prof_ev.size()) return -1;
+  const int slot = g_prof_used++;
+  cudaEventRecord(g_prof_ev[2 * slot], st);
+  return slot;
+}
+
+void prof_after(int slot, cudaStream_t st) {
+  if (slot < 0) return;
+  std::lock_guard<std::mutex> lk(g_prof_mu);
+  cudaEventRecord(g_prof_ev[2 * slot + 1], st);
+}
+}  // namespace sb
+
+extern "C" SB_API int sb_profile_start(int32_t max_launches) {
+  if (max_launches <= 0 || max_launches > (1 << 20)) return SB_ERR_INVALID_ARGUMENT;
+  std::lock_guard<std::mutex> lk(sb::g_prof_mu);
+  while ((int)sb::g_prof_ev.size() < 2 * max_launches) {
+    cudaEvent_t e;
+    cudaError_t r = cudaEventCreate(&e);
+    if (r != cudaSuccess) {
+      sb::set_last_cuda_error(r);
+      return SB_ERR_CUDA;
+    }
+    sb::g_prof_ev.push_back(e);
+  }
+  sb::g_prof_used = 0;
+  sb::g_prof_on = true;
+  return SB_OK;
+}
+
+extern "C" SB_API int sb_profile_stop(float *total_ms, int32_t *n_launches) {
+  std::lock_guard<std::mutex> lk(sb::g_prof_mu);
+  sb::g_prof_on = false;
+  float total = 0.f;
+  for (int i = 0; i < sb::g_prof_used; ++i) {
+    cudaError_t r = cudaEventSynchronize(sb::g_prof_ev[2 * i + 1]);
+    float ms = 0.f;
+    if (r == cudaSuccess) r = cudaEventElapsedTime(&ms, sb::g_prof_ev[2 * i], sb::g_prof_ev[2 * i + 1]);
+    if (r != cudaSuccess) {
+      sb::set_last_cuda_error(r);
+      return SB_ERR_CUDA;
+    }
+    total += ms;
+  }
+  if (total_ms) *total_ms = total;
+  if (n_launches) *n_launches = sb::g_prof_used;
+  sb::g_prof_used = 0;
+  return SB_OK;
 }

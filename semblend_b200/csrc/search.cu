@@ -32,6 +32,7 @@
 #include <cfloat>
 
 #include "common.cuh"
+#include "prof.cuh"
 #include "tcgen05.cuh"
 #include "tma.cuh"
 
@@ -510,7 +511,9 @@ int launch_screen(const CUtensorMap &tq, const CUtensorMap &te, const ScreenPara
     set_last_cuda_error(e);
     return SB_ERR_CUDA;
   }
+  const int slot = prof_before(st);
   screen_kernel<KT><<<grid, kThreads, smem, st>>>(tq, te, P);
+  prof_after(slot, st);
   return launch_status();
 }
 

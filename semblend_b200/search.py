@@ -124,14 +124,16 @@ def _workspace(owner, nbytes: int, device: torch.device) -> torch.Tensor:
     return ws
 
 
-def cosine_topk(emb: torch.Tensor, emb_bf16: torch.Tensor, valid: torch.Tensor | None, stats: torch.Tensor,
-                queries: torch.Tensor, k: int, min_similarity: float, *, n_rows: int | None = None,
-                id_offset: int = 0, capacity: int = DEFAULT_CAPACITY, status: torch.Tensor | None = None,
-                workspace_owner=None) -> tuple[torch.Tensor, torch.Tensor]:
-    """Functional form of :meth:`DeviceDonorMatrix.search` over raw tensors.
+def cosine_topk_async(emb: torch.Tensor, emb_bf16: torch.Tensor, valid: torch.Tensor | None,
+                      stats: torch.Tensor, queries: torch.Tensor, k: int, min_similarity: float, *,
+                      n_rows: int | None = None, id_offset: int = 0, capacity: int = DEFAULT_CAPACITY,
+                      status: torch.Tensor | None = None, workspace_owner=None,
+                      out: tuple[torch.Tensor, torch.Tensor] | None = None):
+    """One search attempt, enqueued without synchronising.
 
-    Retries with a 4x larger candidate capacity if screening overflowed it
-    (many near-ties); raises if the kernel reports a wait timeout.
+    Returns ``(ids, scores, status)``; ``status`` (device int32) must be read
+    before the results are trusted: bit 0 = a query overflowed ``capacity``
+    (retry larger), values >= 2 = a kernel wait timed out.
     """
     for t, name in ((emb, "emb"), (emb_bf16, "emb_bf16"), (queries, "queries"), (stats, "stats")):
         _lib.require_cuda(t, name)
@@ -142,27 +144,53 @@ def cosine_topk(emb: torch.Tensor, emb_bf16: torch.Tensor, valid: torch.Tensor |
     k = int(k)
     if not 1 <= k <= 32:
         raise ValueError(f"k must be in [1, 32], got {k}")
-    ids = torch.empty(nq, k, dtype=torch.int64, device=dev)
-    scores = torch.empty(nq, k, dtype=torch.float32, device=dev)
+    ld_q = queries.stride(0) if nq > 1 else dim  # a size-1 dim may carry any stride
+    ld_e = emb.stride(0) if emb.shape[0] > 1 else dim
+    ld_b = emb_bf16.stride(0) if emb_bf16.shape[0] > 1 else dim_pad
+    if queries.stride(1) != 1 or emb.stride(1) != 1 or emb_bf16.stride(1) != 1:
+        raise ValueError("queries and embedding rows must be contiguous along the embedding dimension")
+    if out is None:
+        ids = torch.empty(nq, k, dtype=torch.int64, device=dev)
+        scores = torch.empty(nq, k, dtype=torch.float32, device=dev)
+    else:
+        ids, scores = out
     if status is None:
         status = torch.zeros(1, dtype=torch.int32, device=dev)
+    else:
+        status.zero_()
     lib = _lib.load()
     cap = max(int(capacity), k)
+    nbytes = lib.sb_cosine_topk_workspace_bytes(nq, dim, dim_pad, cap)
+    ws = _workspace(workspace_owner, nbytes, dev)
+    _lib.check(
+        lib.sb_cosine_topk(
+            emb.data_ptr(), ld_e, emb_bf16.data_ptr(), ld_b,
+            valid.data_ptr() if valid is not None else None, n_rows, dim, dim_pad, stats.data_ptr(),
+            queries.data_ptr(), ld_q, nq, k, float(min_similarity), int(id_offset),
+            ids.data_ptr(), scores.data_ptr(), cap, ws.data_ptr(), ws.numel(), status.data_ptr(),
+            _lib.stream_ptr(dev),
+        ),
+        "sb_cosine_topk",
+    )
+    return ids, scores, status
+
+
+def cosine_topk(emb: torch.Tensor, emb_bf16: torch.Tensor, valid: torch.Tensor | None, stats: torch.Tensor,
+                queries: torch.Tensor, k: int, min_similarity: float, *, n_rows: int | None = None,
+                id_offset: int = 0, capacity: int = DEFAULT_CAPACITY, status: torch.Tensor | None = None,
+                workspace_owner=None) -> tuple[torch.Tensor, torch.Tensor]:
+    """Functional form of :meth:`DeviceDonorMatrix.search` over raw tensors.
+
+    Synchronises to read the kernel status; retries with a 4x larger
+    candidate capacity if screening overflowed it (many near-ties); raises if
+    a kernel wait timed out.
+    """
+    cap = max(int(capacity), int(k))
     while True:
-        nbytes = lib.sb_cosine_topk_workspace_bytes(nq, dim, dim_pad, cap)
-        ws = _workspace(workspace_owner, nbytes, dev)
-        status.zero_()
-        _lib.check(
-            lib.sb_cosine_topk(
-                emb.data_ptr(), emb.stride(0), emb_bf16.data_ptr(), emb_bf16.stride(0),
-                valid.data_ptr() if valid is not None else None, n_rows, dim, dim_pad, stats.data_ptr(),
-                queries.data_ptr(), queries.stride(0), nq, k, float(min_similarity), int(id_offset),
-                ids.data_ptr(), scores.data_ptr(), cap, ws.data_ptr(), ws.numel(), status.data_ptr(),
-                _lib.stream_ptr(dev),
-            ),
-            "sb_cosine_topk",
-        )
-        st = int(status.item())
+        ids, scores, st_t = cosine_topk_async(
+            emb, emb_bf16, valid, stats, queries, k, min_similarity, n_rows=n_rows, id_offset=id_offset,
+            capacity=cap, status=status, workspace_owner=workspace_owner)
+        st = int(st_t.item())
         if st & ~1:
             raise _lib.NativeLibraryError(f"sb_cosine_topk: kernel wait timed out (code {st})")
         if st & 1 and cap < 16384:
