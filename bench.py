@@ -429,6 +429,7 @@ def run_search(args, local: int) -> dict:
     pk = peaks()
     achieved = flops / (kt.mean_ms * 1e-3) / 1e12
     hits = float((out[0] >= 0).float().mean().item())
+    cand = m._ws[: 4 * S_QUERIES].view(torch.int32).float()  # per-query screening candidates (workspace head)
     return {
         "metric": "donor search q/s",
         "value": round(S_QUERIES / (ms * 1e-3), 1),
@@ -437,7 +438,8 @@ def run_search(args, local: int) -> dict:
         "steps": steps,
         "config": {"workload": "c3: 1,048,576 x 384 fp32 donors (256 clusters, sigma 0.3, L2-normalised), "
                                "4096 queries (70% clustered, 30% uniform), top-8, threshold 0.60",
-                   "fill": round(hits, 4), "status": st},
+                   "fill": round(hits, 4), "status": st,
+                   "candidates_per_query": {"mean": round(float(cand.mean()), 1), "max": int(cand.max())}},
         "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
                      "frac": round(achieved / pk["bf16_tflops"], 4), "peak_source": pk["source"],
                      "kernel": "screen_kernel<8> (bf16 tcgen05, 2*N*Q*d flops)", "kernel_ms": round(kt.mean_ms, 4),

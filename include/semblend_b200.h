@@ -187,8 +187,8 @@ SB_API int sb_search_prepare_rows(const float *emb, int64_t ld_emb, uint16_t *em
                                   float *stats, void *stream);
 
 /* Workspace bytes sb_cosine_topk needs. */
-SB_API int64_t sb_cosine_topk_workspace_bytes(int32_t n_queries, int32_t dim, int32_t dim_pad,
-                                              int32_t capacity);
+SB_API int64_t sb_cosine_topk_workspace_bytes(int32_t n_queries, int64_t n_rows, int32_t dim,
+                                              int32_t dim_pad, int32_t capacity);
 
 /* Exact brute-force cosine top-k for a batch of queries.
  *

@@ -44,7 +44,7 @@ constexpr int kBN = 256;             // donors per MMA tile
 constexpr int kBK = 64;              // K elements per shared-memory stage (128 B rows)
 constexpr int kQBlockBytes = kBM * 128;
 constexpr int kEStageBytes = kBN * 128;
-constexpr int kThreads = 192;        // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
+constexpr int kThreads = 320;        // warp 0 TMA, warp 1 MMA, warps 2-9 epilogue
 constexpr int kTilesPerChunk = 32;   // donor tiles per work unit
 constexpr int kMaxStages = 6;
 constexpr int kSmemLimit = 232448;
@@ -60,7 +60,8 @@ struct ScreenParams {
   int64_t n_units;
   float thr;
   int cap;
-  const uint8_t *valid;
+  const uint32_t *valid_bits;  // bit j = row j searchable (bits past n_rows are 0)
+  int64_t n_valid_words;
   const float *delta;
   int *count;
   int *lower;
@@ -110,6 +111,20 @@ __global__ void query_prep_kernel(const float *__restrict__ q, int64_t ld_q, int
   }
 }
 
+// Bit-pack the row validity (all rows valid when `valid` is null); bits at
+// or past n_rows are cleared.
+__global__ void valid_bits_kernel(const uint8_t *__restrict__ valid, int64_t n_rows, uint32_t *__restrict__ bits,
+                                  int64_t n_words) {
+  const int64_t w = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (w >= n_words) return;
+  uint32_t v = 0;
+  for (int i = 0; i < 32; ++i) {
+    const int64_t j = w * 32 + i;
+    if (j < n_rows && (valid == nullptr || valid[j])) v |= 1u << i;
+  }
+  bits[w] = v;
+}
+
 // Descending insertion into a register-resident sorted list.
 template <int KT>
 __device__ __forceinline__ void topk_insert(float (&tk)[KT], float s) {
@@ -150,8 +165,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc::mbar_init(q_empty, 1);
     tc::mbar_init(&acc_full[0], 1);
     tc::mbar_init(&acc_full[1], 1);
-    tc::mbar_init(&acc_empty[0], 4);
-    tc::mbar_init(&acc_empty[1], 4);
+    tc::mbar_init(&acc_empty[0], 8);
+    tc::mbar_init(&acc_empty[1], 8);
     tc::mbar_init(final_bar, 1);
     *abort_flag = 0;
     tc::fence_mbar_init();
@@ -259,8 +274,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc::mbar_wait(final_bar, 0, drain, 0, kWaitCycles);
     }
   } else {
-    // ---------------- epilogue: one query row per thread ----------------
-    const int quarter = warp & 3;  // TMEM lanes this warp may read
+    // ---------------- epilogue ----------------
+    // 8 warps: warp w reads TMEM lanes [32*(w%4), +32) (its quarter of the
+    // query rows) and one half of the tile's 256 donor columns, so every
+    // query row is scanned by two threads, each with its own top-k list.
+    const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;
     const int row = quarter * 32 + lane;
     uint32_t ai = 0;
     bool ok = true;
@@ -277,28 +296,51 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int i = 0; i < KT; ++i) tk[i] = -INFINITY;
       float cut = P.thr - dq;
       for (int64_t t = t0; t < t1; ++t) {
+        const int64_t c0 = t * kBN + half * (kBN / 2);  // first donor column of this thread
+        // prefetch: validity bits of the 128 columns and the shared lower bound
+        uint32_t vb[4];
+#pragma unroll
+        for (int w = 0; w < 4; ++w) {
+          const int64_t word = (c0 >> 5) + w;
+          vb[w] = word < P.n_valid_words ? __ldg(P.valid_bits + word) : 0u;
+        }
+        const int lg = active ? *reinterpret_cast<volatile int *>(P.lower + q) : 0;
         const uint32_t b = ai & 1;
         if (!tc::mbar_wait(&acc_full[b], (ai >> 1) & 1, ab, 4, kWaitCycles)) {
           ok = false;
           break;
         }
         tc::fence_after_sync();
-        const uint32_t base = tmem + ((uint32_t)(quarter * 32) << 16) + b * kBN;
-        const int64_t n0 = t * kBN;
+        const uint32_t base = tmem + ((uint32_t)(quarter * 32) << 16) + b * kBN + half * (kBN / 2);
+        const float tk_before = tk[KT - 1];
+        int nc = 0, cbuf0 = 0, cbuf1 = 0, cbuf2 = 0, cbuf3 = 0;
+        auto flush = [&]() {
+          const int slot = atomicAdd(&P.count[q], nc);
+          const int v[4] = {cbuf0, cbuf1, cbuf2, cbuf3};
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            if (i < nc && slot + i < P.cap) P.cand[(int64_t)q * P.cap + slot + i] = v[i];
+          nc = 0;
+        };
 #pragma unroll 1
-        for (int c = 0; c < kBN / 32; ++c) {
-          uint32_t r[32];
-          tc::tmem_ld32(base + c * 32, r);
+        for (int c = 0; c < kBN / 2; c += 64) {
+          uint32_t r0[32], r1[32];
+          tc::tmem_ld32(base + c, r0);
+          tc::tmem_ld32(base + c + 32, r1);
           tc::tmem_ld_wait();
           if (active) {
 #pragma unroll
-            for (int i = 0; i < 32; ++i) {
-              const float s = __uint_as_float(r[i]);
+            for (int i = 0; i < 64; ++i) {
+              const float s = __uint_as_float(i < 32 ? r0[i] : r1[i - 32]);
               if (s >= cut) {
-                const int64_t j = n0 + c * 32 + i;
-                if (j < P.n_rows && (P.valid == nullptr || P.valid[j])) {
-                  const int slot = atomicAdd(&P.count[q], 1);
-                  if (slot < P.cap) P.cand[(int64_t)q * P.cap + slot] = (int)j;
+                const int col = c + i;
+                if ((vb[col >> 5] >> (col & 31)) & 1u) {
+                  const int j = (int)(c0 + col);
+                  if (nc == 0) cbuf0 = j;
+                  else if (nc == 1) cbuf1 = j;
+                  else if (nc == 2) cbuf2 = j;
+                  else cbuf3 = j;
+                  if (++nc == 4) flush();
                   if (s > tk[KT - 1]) {
                     topk_insert<KT>(tk, s);
                     cut = fmaxf(cut, tk[KT - 1] - two_d);
@@ -313,10 +355,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) tc::mbar_arrive(&acc_empty[b]);
         ++ai;
         if (active) {
-          // publish this CTA's k-th best and read everyone's
-          const int mine = tc::float_to_ordered(tk[KT - 1]);
-          const int g = max(atomicMax(&P.lower[q], mine), mine);
-          cut = fmaxf(cut, tc::ordered_to_float(g) - two_d);
+          if (nc) flush();
+          if (tk[KT - 1] > tk_before) atomicMax(&P.lower[q], tc::float_to_ordered(tk[KT - 1]));
+          cut = fmaxf(cut, tc::ordered_to_float(lg) - two_d);
         }
       }
     }
@@ -474,10 +515,11 @@ struct Workspace {
   float *delta, *qn;
   __nv_bfloat16 *qb;
   int *cand;
+  uint32_t *bits;
   int64_t bytes;
 };
 
-Workspace carve(void *base, int nq, int dim, int dim_pad, int cap) {
+Workspace carve(void *base, int nq, int dim, int dim_pad, int cap, int64_t n_rows) {
   Workspace w;
   char *p = reinterpret_cast<char *>(base);
   int64_t off = 0;
@@ -492,6 +534,7 @@ Workspace carve(void *base, int nq, int dim, int dim_pad, int cap) {
   w.qn = reinterpret_cast<float *>(take(4LL * nq * dim));
   w.qb = reinterpret_cast<__nv_bfloat16 *>(take(2LL * nq * dim_pad));
   w.cand = reinterpret_cast<int *>(take(4LL * nq * cap));
+  w.bits = reinterpret_cast<uint32_t *>(take(4LL * ((n_rows + 31) / 32 + 8)));
   w.bytes = off;
   return w;
 }
@@ -534,10 +577,10 @@ extern "C" SB_API int sb_search_prepare_rows(const float *emb, int64_t ld_emb, u
   return sb::launch_status();
 }
 
-extern "C" SB_API int64_t sb_cosine_topk_workspace_bytes(int32_t n_queries, int32_t dim, int32_t dim_pad,
-                                                         int32_t capacity) {
-  if (n_queries < 0 || dim <= 0 || dim_pad < dim || capacity <= 0) return -1;
-  return sb::carve(nullptr, n_queries, dim, dim_pad, capacity).bytes;
+extern "C" SB_API int64_t sb_cosine_topk_workspace_bytes(int32_t n_queries, int64_t n_rows, int32_t dim,
+                                                         int32_t dim_pad, int32_t capacity) {
+  if (n_queries < 0 || n_rows < 0 || dim <= 0 || dim_pad < dim || capacity <= 0) return -1;
+  return sb::carve(nullptr, n_queries, dim, dim_pad, capacity, n_rows).bytes;
 }
 
 extern "C" SB_API int sb_cosine_topk(const float *emb, int64_t ld_emb, const uint16_t *emb_bf16, int64_t ld_bf16,
@@ -557,7 +600,7 @@ extern "C" SB_API int sb_cosine_topk(const float *emb, int64_t ld_emb, const uin
     return SB_ERR_INVALID_ARGUMENT;
   if (ld_q < dim || ld_emb < dim || ld_bf16 < dim_pad) return SB_ERR_INVALID_ARGUMENT;
   if ((reinterpret_cast<uintptr_t>(emb_bf16) % 16) || ((ld_bf16 * 2) % 16)) return SB_ERR_INVALID_ARGUMENT;
-  Workspace w = carve(workspace, n_queries, dim, dim_pad, capacity);
+  Workspace w = carve(workspace, n_queries, dim, dim_pad, capacity, n_rows);
   if (workspace == nullptr || workspace_bytes < w.bytes) return SB_ERR_WORKSPACE_TOO_SMALL;
   if (n_rows == 0) {
     const int64_t n = (int64_t)n_queries * k;
@@ -566,11 +609,13 @@ extern "C" SB_API int sb_cosine_topk(const float *emb, int64_t ld_emb, const uin
   }
   if (emb == nullptr || emb_bf16 == nullptr) return SB_ERR_INVALID_ARGUMENT;
 
+  const int64_t n_words = (n_rows + 31) / 32;
   {
     const int threads = 256;
     const int blocks = (n_queries * 32 + threads - 1) / threads;
     query_prep_kernel<<<blocks, threads, 0, st>>>(queries, ld_q, n_queries, dim, dim_pad, stats, w.qn, w.qb,
                                                   w.delta, w.count, w.lower);
+    valid_bits_kernel<<<(unsigned)((n_words + 255) / 256), 256, 0, st>>>(valid, n_rows, w.bits, n_words);
     int s = launch_status();
     if (s != SB_OK) return s;
   }
@@ -590,7 +635,8 @@ extern "C" SB_API int sb_cosine_topk(const float *emb, int64_t ld_emb, const uin
   P.n_units = n_chunks * P.n_qtiles;
   P.thr = min_similarity;
   P.cap = capacity;
-  P.valid = valid;
+  P.valid_bits = w.bits;
+  P.n_valid_words = n_words;
   P.delta = w.delta;
   P.count = w.count;
   P.lower = w.lower;

@@ -160,7 +160,7 @@ def cosine_topk_async(emb: torch.Tensor, emb_bf16: torch.Tensor, valid: torch.Te
         status.zero_()
     lib = _lib.load()
     cap = max(int(capacity), k)
-    nbytes = lib.sb_cosine_topk_workspace_bytes(nq, dim, dim_pad, cap)
+    nbytes = lib.sb_cosine_topk_workspace_bytes(nq, n_rows, dim, dim_pad, cap)
     ws = _workspace(workspace_owner, nbytes, dev)
     _lib.check(
         lib.sb_cosine_topk(
