@@ -358,8 +358,9 @@ def run_search(args, local: int) -> dict:
     from semblend_b200.search import DeviceDonorMatrix, cosine_topk_async
 
     dev = torch.device("cuda", local)
-    emb, queries = make_search_inputs(dev, SEED + 3)
-    m = DeviceDonorMatrix(S_ROWS, S_DIM, dev)
+    n_rows = args.search_rows
+    emb, queries = make_search_inputs(dev, SEED + 3, n_rows=n_rows)
+    m = DeviceDonorMatrix(n_rows, S_DIM, dev)
     m.write_range(0, emb)
     out = (torch.empty(S_QUERIES, S_K, dtype=torch.int64, device=dev),
            torch.empty(S_QUERIES, S_K, dtype=torch.float32, device=dev))
@@ -415,7 +416,7 @@ def run_search(args, local: int) -> dict:
     ids_g, sc_g = out[0].cpu().numpy(), out[1].cpu().numpy()
     sample = np.random.default_rng(SEED).choice(S_QUERIES, 16, replace=False)
     E = m.emb.cpu().numpy()
-    valid = np.ones(S_ROWS, bool)
+    valid = np.ones(n_rows, bool)
     Qs = queries.cpu().numpy()[sample]
     torch.set_num_threads(os.cpu_count() or 1)
     c0 = time.perf_counter()
@@ -425,7 +426,7 @@ def run_search(args, local: int) -> dict:
         np.array_equal(ids_o[j][ids_o[j] >= 0], ids_g[q][ids_g[q] >= 0])
         or np.allclose(sc_o[j][: (ids_o[j] >= 0).sum()], sc_g[q][: (ids_o[j] >= 0).sum()], atol=1e-6)
         for j, q in enumerate(sample)))
-    flops = 2.0 * S_ROWS * S_QUERIES * S_DIM
+    flops = 2.0 * n_rows * S_QUERIES * S_DIM
     pk = peaks()
     achieved = flops / (kt.mean_ms * 1e-3) / 1e12
     hits = float((out[0] >= 0).float().mean().item())
@@ -436,8 +437,9 @@ def run_search(args, local: int) -> dict:
         "unit": "q/s",
         "ms_per_step": round(ms, 4),
         "steps": steps,
-        "config": {"workload": "c3: 1,048,576 x 384 fp32 donors (256 clusters, sigma 0.3, L2-normalised), "
-                               "4096 queries (70% clustered, 30% uniform), top-8, threshold 0.60",
+        "config": {"workload": f"c3{'' if n_rows == S_ROWS else ' (reduced)'}: {n_rows:,} x 384 fp32 donors "
+                               "(256 clusters, sigma 0.3, L2-normalised), 4096 queries (70% clustered, 30% "
+                               "uniform), top-8, threshold 0.60",
                    "fill": round(hits, 4), "status": st,
                    "candidates_per_query": {"mean": round(float(cand.mean()), 1), "max": int(cand.max())}},
         "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
@@ -451,7 +453,7 @@ def run_search(args, local: int) -> dict:
         "oracle_check": f"{agree}/{len(sample)} sampled queries equivalent",
         "cpu_baseline": {"value": round(1.0 / cpu_s, 3), "unit": "q/s", "cores": torch.get_num_threads(),
                          "kind": "port", "sample": f"{len(sample)} queries through oracle.search.topk_batch "
-                         "(the reference's per-query numpy stage) on the full 1M x 384 matrix"},
+                         f"(the reference's per-query numpy stage) on the full {n_rows:,} x 384 matrix"},
     }
 
 
@@ -518,6 +520,9 @@ def main() -> int:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-components", action="store_true", help="skip the search / attention components")
+    ap.add_argument("--only", choices=["all", "search"], default="all",
+                    help="'search': print only the donor-search component line")
+    ap.add_argument("--search-rows", type=int, default=S_ROWS, help="donor rows of the search (c3: 1048576)")
     ap.add_argument("--requests", type=int, default=N_REQ, help="requests per step (c2: 8)")
     ap.add_argument("--layers", type=int, default=N_LAYERS, help="layers (c2: 28)")
     args = ap.parse_args()
@@ -530,6 +535,10 @@ def main() -> int:
             print(json.dumps(line), flush=True)
         return 0
     world, rank, local = dist_setup(args.gpus)
+    if args.only == "search":
+        if rank == 0:
+            print(json.dumps(run_search(args, local)), flush=True)
+        return 0
     line = run_ours(args, world, rank, local)
     if line is not None:
         if world == 1 and not args.no_cpu_baseline:

@@ -225,6 +225,44 @@ SB_API int sb_topk_merge(const int64_t *ids, const float *scores, int32_t n_list
                          void *stream);
 
 /* ------------------------------------------------------------------------ */
+/* Partial-prefill attention                                                */
+/* ------------------------------------------------------------------------ */
+/* A [batch, heads, seq, head_dim] tensor with a contiguous last dimension;
+ * strides are in elements. */
+typedef struct sb_attn_tensor {
+  void *data;
+  int64_t stride_batch, stride_head, stride_seq;
+} sb_attn_tensor;
+
+/* Compact a per-batch compute mask (uint8, [batch][seq_len] with batch stride
+ * mask_stride) into ascending row indices rows[b*rows_stride + i] and
+ * counts[b] (device int32), with no host synchronisation.  Replaces the mask
+ * scan of _partial_prefill_attention_kernel
+ * (semblend_core/triton_kernels.py:571-581) and the .item() of
+ * partial_prefill_attention (:680). */
+SB_API int sb_mask_to_rows(const uint8_t *mask, int64_t mask_stride, int32_t batch, int32_t seq_len,
+                           int32_t *rows, int64_t rows_stride, int32_t *counts, void *stream);
+
+/* Causal attention at compute rows only, with grouped-query attention:
+ * for b < batch, i < counts[b], p = rows[b*rows_stride + i] (ascending) and
+ * query head h, out[b,h,p] = softmax(q[b,h,p] . k[b,g,0..p]^T * scale)
+ * v[b,g,0..p] with g = h / (n_q_heads / n_kv_heads); other rows of out are
+ * not written.  max_rows bounds every counts[b].  bf16 / fp16 with
+ * head_dim 128 run on the tensor cores (fp32 accumulation and softmax);
+ * other head dims (<= 256) and fp32 run on CUDA cores.  *status (device
+ * int32, zeroed by the caller) receives a value >= 2 if a kernel wait timed
+ * out.
+ *
+ * Replaces partial_prefill_attention (semblend_core/triton_kernels.py:655-734;
+ * kernel :532-652), which has the same math for n_q_heads == n_kv_heads and
+ * batch 1. */
+SB_API int sb_partial_attention(sb_attn_tensor q, sb_attn_tensor k, sb_attn_tensor v, sb_attn_tensor out,
+                                const int32_t *rows, int64_t rows_stride, const int32_t *counts,
+                                int32_t max_rows, int32_t batch, int32_t n_q_heads, int32_t n_kv_heads,
+                                int32_t seq_len, int32_t head_dim, float scale, int32_t dtype,
+                                int32_t *status, void *stream);
+
+/* ------------------------------------------------------------------------ */
 /* Miscellaneous                                                            */
 /* ------------------------------------------------------------------------ */
 SB_API const char *sb_status_string(int status);
@@ -235,7 +273,7 @@ SB_API int sb_last_cuda_error(void);
 
 /* Timing of the dominant kernel of each later call (inject_kernel for
  * sb_inject / sb_permute_paged, the tensor-core screening kernel for
- * sb_cosine_topk): CUDA events are recorded on the launch stream around each
+ * sb_cosine_topk, the attention kernel for sb_partial_attention): CUDA events are recorded on the launch stream around each
  * of the next max_launches such launches.  sb_profile_stop synchronises on
  * them, reports the summed milliseconds and the number of launches timed, and
  * turns timing off. */

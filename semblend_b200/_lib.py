@@ -88,6 +88,15 @@ class SbInjectParams(ctypes.Structure):
     ]
 
 
+class SbAttnTensor(ctypes.Structure):
+    _fields_ = [
+        ("data", ctypes.c_void_p),
+        ("stride_batch", ctypes.c_int64),
+        ("stride_head", ctypes.c_int64),
+        ("stride_seq", ctypes.c_int64),
+    ]
+
+
 _P = ctypes.POINTER
 _SIGNATURES: dict[str, tuple] = {
     "sb_inject": (ctypes.c_int, [_P(SbInjectDesc), ctypes.c_int32, _P(SbInjectParams), ctypes.c_void_p, ctypes.c_void_p]),
@@ -115,6 +124,17 @@ _SIGNATURES: dict[str, tuple] = {
         ctypes.c_int,
         [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_void_p,
          ctypes.c_void_p, ctypes.c_void_p],
+    ),
+    "sb_mask_to_rows": (
+        ctypes.c_int,
+        [ctypes.c_void_p, ctypes.c_int64, ctypes.c_int32, ctypes.c_int32, ctypes.c_void_p, ctypes.c_int64,
+         ctypes.c_void_p, ctypes.c_void_p],
+    ),
+    "sb_partial_attention": (
+        ctypes.c_int,
+        [SbAttnTensor, SbAttnTensor, SbAttnTensor, SbAttnTensor, ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p,
+         ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
+         ctypes.c_float, ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p],
     ),
     "sb_profile_start": (ctypes.c_int, [ctypes.c_int32]),
     "sb_profile_stop": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p]),

@@ -1,0 +1,595 @@
+// Partial-prefill attention over compacted query rows (sm_100a).
+//
+// For every compute row p of batch element b and query head h:
+//     out[b, h, p] = softmax(q[b, h, p] . K[b, g(h), 0..p]^T * scale) V[b, g(h), 0..p]
+// with g(h) = h / (Hq / Hkv) (grouped-query attention).  This is the
+// reference's partial_prefill_attention (semblend_core/triton_kernels.py:
+// 532-734), which runs one program per (row, head) with CUDA-core dot
+// products, finds its row by scanning the mask and has no GQA.
+//
+// Tensor-core path (bf16 / fp16, head_dim 128): one CTA tile holds the
+// G = Hq / Hkv query heads of a KV group at Pt = 128 / G consecutive compute
+// rows (M = G * Pt <= 128 rows), so every K/V tile is read once for all heads
+// sharing it and the rows of a tile share nearly the same causal bound.
+//   warp 0     TMA producer: K and V tiles of 128 keys (3-stage ring)
+//   warp 1     tcgen05.mma issuer: S = Q K^T into TMEM (double-buffered),
+//              O += P V with P read from TMEM (kind::f16, fp32 accumulate)
+//   warps 2-5  softmax: one row per thread; online softmax in the exp2
+//              domain, P written back to TMEM over S, O rescaled in TMEM only
+//              when the running max grows by more than 2^8 (exact: the final
+//              normalisation uses the same reference max); then the epilogue.
+// Work units (b, kv group, row tile) are assigned longest-first.
+//
+// CUDA-core path: any head_dim <= 256 and fp32 (the reference's own dtype in
+// its tests), one CTA per (row, head), fp32 online softmax with expf.
+#include <algorithm>
+
+#include "common.cuh"
+#include "prof.cuh"
+#include "tcgen05.cuh"
+#include "tma.cuh"
+
+namespace sb {
+namespace {
+
+constexpr int kBM = 128;
+constexpr int kBN = 128;
+constexpr int kD = 128;
+constexpr int kThreads = 192;
+constexpr int kStages = 3;
+constexpr int kTileBytes = 128 * 128 * 2;  // one [128 x 128] 16-bit operand tile (two 64-column boxes)
+constexpr int kHalfTile = kTileBytes / 2;
+constexpr int kSmemBytes = 1024 + kTileBytes * (1 + 2 * kStages) + 256;
+constexpr long long kWaitCycles = 2000000000LL;
+constexpr uint32_t kTmemS = 0;    // two S / P buffers: columns [0, 128) and [128, 256)
+constexpr uint32_t kTmemO = 256;  // O accumulator: columns [256, 384)
+
+struct AttnParams {
+  const void *q;
+  int64_t q_sb, q_sh, q_ss;
+  void *out;
+  int64_t o_sb, o_sh, o_ss;
+  const int32_t *rows;
+  int64_t rows_sb;
+  const int32_t *counts;
+  int B, Hq, Hkv, S, G, Pt, T_max;
+  int64_t n_units;
+  float scale_log2;
+  int *status;
+};
+
+struct Unit {
+  int b, g, t, r0, n_rows;
+  int pos_max;
+  int nblk;
+};
+
+__device__ __forceinline__ bool decode_unit(const AttnParams &P, int64_t u, Unit &w) {
+  const int64_t bg_all = (int64_t)P.B * P.Hkv;
+  w.t = P.T_max - 1 - (int)(u / bg_all);
+  const int bg = (int)(u % bg_all);
+  w.b = bg / P.Hkv;
+  w.g = bg % P.Hkv;
+  w.r0 = w.t * P.Pt;
+  const int cnt = P.counts[w.b];
+  if (w.r0 >= cnt) return false;
+  w.n_rows = min(P.Pt, cnt - w.r0);
+  w.pos_max = P.rows[(int64_t)w.b * P.rows_sb + w.r0 + w.n_rows - 1];
+  w.nblk = w.pos_max / kBN + 1;
+  return true;
+}
+
+template <typename T> struct Pack2;
+template <> struct Pack2<__nv_bfloat16> {
+  static __device__ __forceinline__ uint32_t pack(float a, float b) {
+    __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t *>(&v);
+  }
+};
+template <> struct Pack2<__half> {
+  static __device__ __forceinline__ uint32_t pack(float a, float b) {
+    __half2 v = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t *>(&v);
+  }
+};
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads, 1)
+    attn_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+                   const AttnParams P) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t *sQ = smem;
+  uint8_t *sK = sQ + kTileBytes;               // [kStages]
+  uint8_t *sV = sK + kStages * kTileBytes;     // [kStages]
+  uint64_t *bars = reinterpret_cast<uint64_t *>(sV + kStages * kTileBytes);
+  uint64_t *k_full = bars;                     // [3]
+  uint64_t *v_full = bars + 3;                 // [3]
+  uint64_t *kv_empty = bars + 6;               // [3]
+  uint64_t *q_full = bars + 9;
+  uint64_t *q_empty = bars + 10;
+  uint64_t *s_full = bars + 11;                // [2]
+  uint64_t *p_full = bars + 13;                // [2]
+  uint64_t *pv_done = bars + 15;
+  uint64_t *final_bar = bars + 16;
+  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 17);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(bars + 18);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      tc::mbar_init(&k_full[s], 1);
+      tc::mbar_init(&v_full[s], 1);
+      tc::mbar_init(&kv_empty[s], 1);
+    }
+    tc::mbar_init(q_full, 4);
+    tc::mbar_init(q_empty, 1);
+    tc::mbar_init(&s_full[0], 1);
+    tc::mbar_init(&s_full[1], 1);
+    tc::mbar_init(&p_full[0], 4);
+    tc::mbar_init(&p_full[1], 4);
+    tc::mbar_init(pv_done, 1);
+    tc::mbar_init(final_bar, 1);
+    *abort_flag = 0;
+    tc::fence_mbar_init();
+  }
+  if (warp == 1) {
+    tc::tmem_alloc(tmem_holder, 512);
+    tc::tmem_relinquish();
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = *tmem_holder;
+  const tc::Abort ab{abort_flag, P.status};
+  volatile int never = 0;
+  const tc::Abort drain{&never, nullptr};
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------ TMA producer ------------------------------
+      tc::tma_prefetch_desc(&tmK);
+      tc::tma_prefetch_desc(&tmV);
+      uint32_t gl = 0;
+      bool ok = true;
+      for (int64_t u = blockIdx.x; u < P.n_units && ok; u += gridDim.x) {
+        Unit w;
+        if (!decode_unit(P, u, w)) continue;
+        for (int j = 0; j < w.nblk; ++j) {
+          const uint32_t st = gl % kStages, ph = (gl / kStages) & 1;
+          if (!tc::mbar_wait(&kv_empty[st], ph ^ 1, ab, 2, kWaitCycles)) {
+            ok = false;
+            break;
+          }
+          uint8_t *k_dst = sK + st * kTileBytes;
+          uint8_t *v_dst = sV + st * kTileBytes;
+          tc::mbar_arrive_expect_tx(&k_full[st], kTileBytes);
+          tc::tma_load_4d(k_dst, &tmK, &k_full[st], 0, j * kBN, w.g, w.b);
+          tc::tma_load_4d(k_dst + kHalfTile, &tmK, &k_full[st], 64, j * kBN, w.g, w.b);
+          tc::mbar_arrive_expect_tx(&v_full[st], kTileBytes);
+          tc::tma_load_4d(v_dst, &tmV, &v_full[st], 0, j * kBN, w.g, w.b);
+          tc::tma_load_4d(v_dst + kHalfTile, &tmV, &v_full[st], 64, j * kBN, w.g, w.b);
+          ++gl;
+        }
+      }
+      const uint32_t n_out = gl < (uint32_t)kStages ? gl : (uint32_t)kStages;
+      for (uint32_t i = gl - n_out; i < gl; ++i) {
+        tc::mbar_wait(&k_full[i % kStages], (i / kStages) & 1, drain, 0, kWaitCycles);
+        tc::mbar_wait(&v_full[i % kStages], (i / kStages) & 1, drain, 0, kWaitCycles);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ------------------------------ MMA issuer ------------------------------
+      constexpr uint32_t fmt = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
+      constexpr uint32_t idesc_qk = tc::idesc_f16(kBM, kBN, fmt, 0);
+      constexpr uint32_t idesc_pv = tc::idesc_f16(kBM, kD, fmt, 1);
+      uint32_t gl = 0, gb = 0, qi = 0;
+      bool ok = true;
+      auto issue_pv = [&](uint32_t st, uint32_t glx, uint32_t gbx, bool first) -> bool {
+        if (!tc::mbar_wait(&p_full[gbx & 1], (gbx >> 1) & 1, ab, 3, kWaitCycles)) return false;
+        if (!tc::mbar_wait(&v_full[st], (glx / kStages) & 1, ab, 3, kWaitCycles)) return false;
+        tc::fence_after_sync();
+        const uint32_t p_tmem = tmem + kTmemS + (gbx & 1) * kBN;
+#pragma unroll
+        for (int kk = 0; kk < kBN / 16; ++kk) {
+          const uint64_t dv = tc::desc_mnmajor_sw128(sV + st * kTileBytes, kk * 2048, kHalfTile);
+          tc::mma_bf16_ts(tmem + kTmemO, p_tmem + kk * 8, dv, idesc_pv, (first && kk == 0) ? 0u : 1u);
+        }
+        tc::mma_commit(&kv_empty[st]);
+        tc::mma_commit(pv_done);
+        return true;
+      };
+      for (int64_t u = blockIdx.x; u < P.n_units && ok; u += gridDim.x) {
+        Unit w;
+        if (!decode_unit(P, u, w)) continue;
+        if (!tc::mbar_wait(q_full, qi & 1, ab, 3, kWaitCycles)) break;
+        tc::fence_after_sync();
+        uint32_t prev_st = 0, prev_gl = 0, prev_gb = 0;
+        for (int j = 0; j < w.nblk && ok; ++j) {
+          const uint32_t st = gl % kStages;
+          if (!tc::mbar_wait(&k_full[st], (gl / kStages) & 1, ab, 3, kWaitCycles)) {
+            ok = false;
+            break;
+          }
+          tc::fence_after_sync();
+          const uint32_t s_tmem = tmem + kTmemS + (gb & 1) * kBN;
+#pragma unroll
+          for (int kb = 0; kb < 2; ++kb)
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+              const uint64_t dq = tc::desc_kmajor_sw128(sQ + kb * kHalfTile, kk * 32);
+              const uint64_t dk = tc::desc_kmajor_sw128(sK + st * kTileBytes + kb * kHalfTile, kk * 32);
+              tc::mma_bf16_ss(s_tmem, dq, dk, idesc_qk, (kb | kk) != 0);
+            }
+          tc::mma_commit(&s_full[gb & 1]);
+          if (j > 0 && !issue_pv(prev_st, prev_gl, prev_gb, j == 1)) {
+            ok = false;
+            break;
+          }
+          prev_st = st, prev_gl = gl, prev_gb = gb;
+          ++gl, ++gb;
+        }
+        if (!ok) break;
+        tc::mma_commit(q_empty);
+        ++qi;
+        if (!issue_pv(prev_st, prev_gl, prev_gb, w.nblk == 1)) break;
+      }
+      tc::mma_commit(final_bar);
+      tc::mbar_wait(final_bar, 0, drain, 0, kWaitCycles);
+    }
+  } else {
+    // ------------------------------ softmax / epilogue ------------------------------
+    const int quarter = warp & 3;
+    const int m = quarter * 32 + lane;  // tile row == TMEM lane
+    const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
+    uint32_t gb = 0, qi = 0;
+    int64_t pv_known = -1;  // every PV group with global index <= pv_known has completed
+    bool ok = true;
+    auto wait_pv_through = [&](int64_t idx) -> bool {
+      while (pv_known < idx) {
+        ++pv_known;
+        if (!tc::mbar_wait(pv_done, (uint32_t)(pv_known & 1), ab, 4, kWaitCycles)) return false;
+      }
+      return true;
+    };
+    for (int64_t u = blockIdx.x; u < P.n_units && ok; u += gridDim.x) {
+      Unit w;
+      if (!decode_unit(P, u, w)) continue;
+      const int hh = m / P.Pt, pi = m - hh * P.Pt;
+      const bool valid = hh < P.G && pi < w.n_rows;
+      const int pos = valid ? P.rows[(int64_t)w.b * P.rows_sb + w.r0 + pi] : -1;
+      const int head = w.g * P.G + hh;
+      // gather this row of Q into the 128-byte-swizzled K-major tile
+      if (qi > 0 && !tc::mbar_wait(q_empty, (qi - 1) & 1, ab, 4, kWaitCycles)) break;
+      {
+        const uint4 *src = reinterpret_cast<const uint4 *>(
+            reinterpret_cast<const T *>(P.q) + (valid ? (int64_t)w.b * P.q_sb + (int64_t)head * P.q_sh +
+                                                            (int64_t)pos * P.q_ss
+                                                      : 0));
+#pragma unroll
+        for (int c = 0; c < 16; ++c) {
+          const uint4 v = valid ? src[c] : make_uint4(0, 0, 0, 0);
+          const int kb = c >> 3, cc = c & 7;
+          *reinterpret_cast<uint4 *>(sQ + kb * kHalfTile + m * 128 + ((cc ^ (m & 7)) << 4)) = v;
+        }
+      }
+      tc::fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(q_full);
+
+      float m_used = -INFINITY, l = 0.f;
+      for (int j = 0; j < w.nblk; ++j) {
+        if (!tc::mbar_wait(&s_full[gb & 1], (gb >> 1) & 1, ab, 4, kWaitCycles)) {
+          ok = false;
+          break;
+        }
+        tc::fence_after_sync();
+        // S for this block proves every PV group issued before it has completed
+        pv_known = max(pv_known, (int64_t)gb - (j == 0 ? 1 : 2));
+        const uint32_t s_addr = tmem + lane_addr + kTmemS + (gb & 1) * kBN;
+        float s[kBN];
+        {
+          uint32_t r[32];
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            tc::tmem_ld32(s_addr + c * 32, r);
+            tc::tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) s[c * 32 + i] = __uint_as_float(r[i]);
+          }
+        }
+        const int key0 = j * kBN;
+        float mx = -INFINITY;
+#pragma unroll
+        for (int c = 0; c < kBN; ++c) {
+          const float x = (key0 + c <= pos) ? s[c] * P.scale_log2 : -INFINITY;
+          s[c] = x;
+          mx = fmaxf(mx, x);
+        }
+        float m_new = m_used;
+        bool need = false;
+        if (mx > -INFINITY && (m_used == -INFINITY || mx > m_used + 8.f)) {
+          need = m_used != -INFINITY;
+          m_new = mx;
+        }
+        if (__any_sync(0xffffffffu, need)) {
+          if (!wait_pv_through((int64_t)gb - 1)) {
+            ok = false;
+            break;
+          }
+          tc::fence_after_sync();
+          const float alpha = need ? tc::ex2_approx(m_used - m_new) : 1.f;
+          const uint32_t o_addr = tmem + lane_addr + kTmemO;
+#pragma unroll 1
+          for (int c = 0; c < kD; c += 16) {
+            uint32_t r[16];
+            tc::tmem_ld16(o_addr + c, r);
+            tc::tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 16; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
+            tc::tmem_st16(o_addr + c, r);
+          }
+          tc::tmem_st_wait();
+          l *= alpha;
+        }
+        m_used = m_new;
+        float sum = 0.f;
+        const uint32_t p_addr = tmem + lane_addr + kTmemS + (gb & 1) * kBN;
+#pragma unroll
+        for (int c = 0; c < kBN; c += 32) {
+          uint32_t r[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const float p0 = m_used == -INFINITY ? 0.f : tc::ex2_approx(s[c + 2 * i] - m_used);
+            const float p1 = m_used == -INFINITY ? 0.f : tc::ex2_approx(s[c + 2 * i + 1] - m_used);
+            sum += p0 + p1;
+            r[i] = Pack2<T>::pack(p0, p1);
+          }
+          tc::tmem_st16(p_addr + c / 2, r);
+        }
+        tc::tmem_st_wait();
+        l += sum;
+        tc::fence_before_sync();
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(&p_full[gb & 1]);
+        ++gb;
+      }
+      if (!ok) break;
+      // epilogue: O / l for this row
+      if (!wait_pv_through((int64_t)gb - 1)) break;
+      tc::fence_after_sync();
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      uint4 *dst = reinterpret_cast<uint4 *>(
+          reinterpret_cast<T *>(P.out) +
+          (valid ? (int64_t)w.b * P.o_sb + (int64_t)head * P.o_sh + (int64_t)pos * P.o_ss : 0));
+      const uint32_t o_addr = tmem + lane_addr + kTmemO;
+#pragma unroll 1
+      for (int c = 0; c < kD; c += 16) {
+        uint32_t r[16];
+        tc::tmem_ld16(o_addr + c, r);
+        tc::tmem_ld_wait();
+        if (valid) {
+          uint32_t pk[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            pk[i] = Pack2<T>::pack(__uint_as_float(r[2 * i]) * inv, __uint_as_float(r[2 * i + 1]) * inv);
+          dst[c / 8] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+          dst[c / 8 + 1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+        }
+      }
+      tc::fence_before_sync();
+      ++qi;
+    }
+  }
+
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  if (warp == 1) tc::tmem_dealloc(tmem, 512);
+}
+
+// ---------------------------------------------------------------------------
+// CUDA-core path
+// ---------------------------------------------------------------------------
+template <typename T>
+__global__ void __launch_bounds__(128) attn_simt_kernel(const T *__restrict__ q, const T *__restrict__ k,
+                                                        const T *__restrict__ v, T *__restrict__ out, AttnParams P,
+                                                        int64_t k_sb, int64_t k_sh, int64_t k_ss, int64_t v_sb,
+                                                        int64_t v_sh, int64_t v_ss, int D, float scale) {
+  const int r = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  if (r >= P.counts[b]) return;
+  const int pos = P.rows[(int64_t)b * P.rows_sb + r];
+  const int g = h / P.G;
+  __shared__ float qs[256];
+  __shared__ float ps[128];
+  __shared__ float red[4];
+  const int tid = threadIdx.x;
+  for (int d = tid; d < D; d += 128)
+    qs[d] = Elem<T>::to_f32(q[(int64_t)b * P.q_sb + (int64_t)h * P.q_sh + (int64_t)pos * P.q_ss + d]);
+  __syncthreads();
+  const T *kb = k + (int64_t)b * k_sb + (int64_t)g * k_sh;
+  const T *vb = v + (int64_t)b * v_sb + (int64_t)g * v_sh;
+  float mrun = -INFINITY, lrun = 0.f, acc0 = 0.f, acc1 = 0.f;
+  for (int k0 = 0; k0 <= pos; k0 += 128) {
+    const int key = k0 + tid;
+    float sc = -INFINITY;
+    if (key <= pos) {
+      float dot = 0.f;
+      const T *kr = kb + (int64_t)key * k_ss;
+      for (int d = 0; d < D; ++d) dot = fmaf(qs[d], Elem<T>::to_f32(kr[d]), dot);
+      sc = dot * scale;
+    }
+    float mx = sc;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if ((tid & 31) == 0) red[tid >> 5] = mx;
+    __syncthreads();
+    mx = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+    __syncthreads();
+    const float m_new = fmaxf(mrun, mx);
+    const float corr = mrun == -INFINITY ? 0.f : expf(mrun - m_new);
+    const float p = key <= pos ? expf(sc - m_new) : 0.f;
+    ps[tid] = p;
+    float sum = p;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    if ((tid & 31) == 0) red[tid >> 5] = sum;
+    __syncthreads();
+    sum = red[0] + red[1] + red[2] + red[3];
+    lrun = lrun * corr + sum;
+    const int nk = min(128, pos + 1 - k0);
+    float a0 = 0.f, a1 = 0.f;
+    for (int j = 0; j < nk; ++j) {
+      const T *vr = vb + (int64_t)(k0 + j) * v_ss;
+      const float pj = ps[j];
+      if (tid < D) a0 = fmaf(pj, Elem<T>::to_f32(vr[tid]), a0);
+      if (tid + 128 < D) a1 = fmaf(pj, Elem<T>::to_f32(vr[tid + 128]), a1);
+    }
+    acc0 = acc0 * corr + a0;
+    acc1 = acc1 * corr + a1;
+    mrun = m_new;
+    __syncthreads();
+  }
+  T *o = out + (int64_t)b * P.o_sb + (int64_t)h * P.o_sh + (int64_t)pos * P.o_ss;
+  if (tid < D) o[tid] = Elem<T>::from_f32(acc0 / lrun);
+  if (tid + 128 < D) o[tid + 128] = Elem<T>::from_f32(acc1 / lrun);
+}
+
+// Compute-mask -> sorted row indices and counts, one CTA per batch element.
+__global__ void mask_to_rows_kernel(const uint8_t *__restrict__ mask, int64_t mask_sb, int S,
+                                    int32_t *__restrict__ rows, int64_t rows_sb, int32_t *__restrict__ counts) {
+  const int b = blockIdx.x;
+  __shared__ int warp_tot[32];
+  __shared__ int base;
+  if (threadIdx.x == 0) base = 0;
+  __syncthreads();
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  for (int s0 = 0; s0 < S; s0 += blockDim.x) {
+    const int s = s0 + threadIdx.x;
+    const int f = (s < S && mask[(int64_t)b * mask_sb + s]) ? 1 : 0;
+    const unsigned bal = __ballot_sync(0xffffffffu, f);
+    const int before = __popc(bal & ((1u << lane) - 1));
+    if (lane == 0) warp_tot[wid] = __popc(bal);
+    __syncthreads();
+    int off = 0, tot = 0;
+    for (int i = 0; i < nw; ++i) {
+      if (i < wid) off += warp_tot[i];
+      tot += warp_tot[i];
+    }
+    if (f) rows[(int64_t)b * rows_sb + base + off + before] = s;
+    __syncthreads();
+    if (threadIdx.x == 0) base += tot;
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) counts[b] = base;
+}
+
+int sm_count() {
+  int dev = 0, n = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 148;
+  return n > 0 ? n : 148;
+}
+
+template <typename T>
+int launch_tc(const sb_attn_tensor &k, const sb_attn_tensor &v, const AttnParams &P, CUtensorMapDataType dt,
+              cudaStream_t st) {
+  CUtensorMap tk, tv;
+  const uint64_t es = sizeof(T);
+  if (!make_tmap_4d(&tk, dt, k.data, kD, P.S, P.Hkv, P.B, k.stride_seq * es, k.stride_head * es,
+                    k.stride_batch * es, 64, kBN) ||
+      !make_tmap_4d(&tv, dt, v.data, kD, P.S, P.Hkv, P.B, v.stride_seq * es, v.stride_head * es,
+                    v.stride_batch * es, 64, kBN))
+    return SB_ERR_CUDA;
+  cudaError_t e = cudaFuncSetAttribute(attn_tc_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+  if (e != cudaSuccess) {
+    set_last_cuda_error(e);
+    return SB_ERR_CUDA;
+  }
+  const int grid = (int)std::min<int64_t>(sm_count(), P.n_units);
+  const int slot = prof_before(st);
+  attn_tc_kernel<T><<<grid, kThreads, kSmemBytes, st>>>(tk, tv, P);
+  prof_after(slot, st);
+  return launch_status();
+}
+
+template <typename T>
+int launch_simt(const sb_attn_tensor &q, const sb_attn_tensor &k, const sb_attn_tensor &v,
+                const sb_attn_tensor &out, const AttnParams &P, int D, float scale, int max_rows, cudaStream_t st) {
+  dim3 grid((unsigned)max_rows, (unsigned)P.Hq, (unsigned)P.B);
+  const int slot = prof_before(st);
+  attn_simt_kernel<T><<<grid, 128, 0, st>>>(
+      reinterpret_cast<const T *>(q.data), reinterpret_cast<const T *>(k.data), reinterpret_cast<const T *>(v.data),
+      reinterpret_cast<T *>(out.data), P, k.stride_batch, k.stride_head, k.stride_seq, v.stride_batch,
+      v.stride_head, v.stride_seq, D, scale);
+  prof_after(slot, st);
+  return launch_status();
+}
+
+bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+}  // namespace
+}  // namespace sb
+
+extern "C" SB_API int sb_mask_to_rows(const uint8_t *mask, int64_t mask_stride, int32_t batch, int32_t seq_len,
+                                      int32_t *rows, int64_t rows_stride, int32_t *counts, void *stream) {
+  if (batch < 0 || seq_len < 0) return SB_ERR_INVALID_ARGUMENT;
+  if (batch == 0) return SB_OK;
+  if (!mask || !rows || !counts || rows_stride < seq_len) return SB_ERR_INVALID_ARGUMENT;
+  sb::mask_to_rows_kernel<<<batch, 1024, 0, reinterpret_cast<cudaStream_t>(stream)>>>(mask, mask_stride, seq_len,
+                                                                                       rows, rows_stride, counts);
+  return sb::launch_status();
+}
+
+extern "C" SB_API int sb_partial_attention(sb_attn_tensor q, sb_attn_tensor k, sb_attn_tensor v, sb_attn_tensor out,
+                                           const int32_t *rows, int64_t rows_stride, const int32_t *counts,
+                                           int32_t max_rows, int32_t batch, int32_t n_q_heads, int32_t n_kv_heads,
+                                           int32_t seq_len, int32_t head_dim, float scale, int32_t dtype,
+                                           int32_t *status, void *stream) {
+  using namespace sb;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (batch < 0 || n_q_heads <= 0 || n_kv_heads <= 0 || seq_len < 0 || head_dim <= 0 || max_rows < 0)
+    return SB_ERR_INVALID_ARGUMENT;
+  if (n_q_heads % n_kv_heads) return SB_ERR_INVALID_ARGUMENT;
+  if (batch == 0 || seq_len == 0 || max_rows == 0) return SB_OK;
+  if (!q.data || !k.data || !v.data || !out.data || !rows || !counts || !status) return SB_ERR_INVALID_ARGUMENT;
+  if (head_dim > 256) return SB_ERR_UNSUPPORTED;
+  if (elem_bytes(dtype) == 0) return SB_ERR_UNSUPPORTED;
+  AttnParams P;
+  P.q = q.data;
+  P.q_sb = q.stride_batch, P.q_sh = q.stride_head, P.q_ss = q.stride_seq;
+  P.out = out.data;
+  P.o_sb = out.stride_batch, P.o_sh = out.stride_head, P.o_ss = out.stride_seq;
+  P.rows = rows;
+  P.rows_sb = rows_stride;
+  P.counts = counts;
+  P.B = batch, P.Hq = n_q_heads, P.Hkv = n_kv_heads, P.S = seq_len;
+  P.G = n_q_heads / n_kv_heads;
+  P.status = status;
+  const int es = elem_bytes(dtype);
+  const bool tc_ok = dtype != SB_DTYPE_F32 && head_dim == kD && P.G <= kBM && aligned16(q.data) &&
+                     aligned16(out.data) && aligned16(k.data) && aligned16(v.data) && (q.stride_seq * es) % 16 == 0 &&
+                     (q.stride_head * es) % 16 == 0 && (q.stride_batch * es) % 16 == 0 &&
+                     (out.stride_seq * es) % 16 == 0 && (out.stride_head * es) % 16 == 0 &&
+                     (out.stride_batch * es) % 16 == 0 && (k.stride_seq * es) % 16 == 0 &&
+                     (k.stride_head * es) % 16 == 0 && (k.stride_batch * es) % 16 == 0 &&
+                     (v.stride_seq * es) % 16 == 0 && (v.stride_head * es) % 16 == 0 &&
+                     (v.stride_batch * es) % 16 == 0;
+  if (tc_ok) {
+    P.Pt = kBM / P.G;
+    P.T_max = (max_rows + P.Pt - 1) / P.Pt;
+    P.n_units = (int64_t)P.T_max * batch * n_kv_heads;
+    P.scale_log2 = scale * 1.4426950408889634f;
+    if (dtype == SB_DTYPE_BF16) return launch_tc<__nv_bfloat16>(k, v, P, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, st);
+    return launch_tc<__half>(k, v, P, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, st);
+  }
+  P.Pt = 1;
+  if (max_rows > 0x7fffffff) return SB_ERR_TOO_LARGE;
+  if (n_q_heads > 65535 || batch > 65535) return SB_ERR_TOO_LARGE;
+  switch (dtype) {
+    case SB_DTYPE_F32: return launch_simt<float>(q, k, v, out, P, head_dim, scale, max_rows, st);
+    case SB_DTYPE_F16: return launch_simt<__half>(q, k, v, out, P, head_dim, scale, max_rows, st);
+    default: return launch_simt<__nv_bfloat16>(q, k, v, out, P, head_dim, scale, max_rows, st);
+  }
+}

@@ -128,6 +128,47 @@ __device__ __forceinline__ uint64_t desc_kmajor_sw128(const void *tile, uint32_t
   return d;
 }
 
+// Instruction descriptor: kind::f16, fp32 D; `fmt` 0 = fp16, 1 = bf16 for
+// both A and B; b_mn_major selects an MN-major B operand.
+__host__ __device__ constexpr uint32_t idesc_f16(int M, int N, uint32_t fmt, uint32_t b_mn_major) {
+  return (1u << 4) | (fmt << 7) | (fmt << 10) | (b_mn_major << 16) | ((uint32_t)(N >> 3) << 17) |
+         ((uint32_t)(M >> 4) << 24);
+}
+
+// Shared-memory descriptor of an MN-major operand stored as 128-byte-swizzled
+// rows of 64 elements along MN (one TMA box of 64 x rows per 64 MN elements):
+// consecutive K rows are 128 B apart, 8-row groups 1024 B apart (stride byte
+// offset) and the next 64 MN elements lbo_bytes further (leading byte offset).
+__device__ __forceinline__ uint64_t desc_mnmajor_sw128(const void *tile, uint32_t k_byte_offset,
+                                                       uint32_t lbo_bytes) {
+  const uint64_t addr = smem_u32(tile) + k_byte_offset;
+  uint64_t d = (addr >> 4) & 0x3FFFull;
+  d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFF) << 16;
+  d |= (uint64_t)(1024 >> 4) << 32;
+  d |= 1ull << 46;
+  d |= 2ull << 61;
+  return d;
+}
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__device__ __forceinline__ void tma_load_4d(void *dst, const CUtensorMap *map, uint64_t *bar, int x, int y, int z,
+                                            int w) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5, %6}], "
+      "[%2];" ::"r"(smem_u32(dst)),
+      "l"(map), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z), "r"(w)
+      : "memory");
+}
+
 // Instruction descriptor: kind::f16 with bf16 A and B (both K-major), fp32 D.
 __host__ __device__ constexpr uint32_t idesc_bf16_f32(int M, int N) {
   return (1u << 4)                       // D format: f32

@@ -57,3 +57,23 @@ inline bool make_tmap_bf16_3d(CUtensorMap *map, const void *base, uint64_t cols,
 }
 
 }  // namespace sb
+
+namespace sb {
+// 4-D tensor [d3, d2, d1, cols] (cols contiguous) with byte pitches for
+// dims 1..3, boxes of box_cols x box_rows x 1 x 1, 128-byte swizzle, zero
+// fill out of range.  `dtype` is a CUtensorMapDataType (bf16 or fp16).
+inline bool make_tmap_4d(CUtensorMap *map, CUtensorMapDataType dtype, const void *base, uint64_t cols,
+                         uint64_t d1, uint64_t d2, uint64_t d3, uint64_t p1, uint64_t p2, uint64_t p3,
+                         uint32_t box_cols, uint32_t box_rows) {
+  auto enc = tensor_map_encoder();
+  if (enc == nullptr) return false;
+  cuuint64_t gdim[4] = {cols, d1, d2, d3};
+  cuuint64_t gstride[3] = {p1, p2, p3};
+  cuuint32_t box[4] = {box_cols, box_rows, 1, 1};
+  cuuint32_t estride[4] = {1, 1, 1, 1};
+  CUresult r = enc(map, dtype, 4, const_cast<void *>(base), gdim, gstride, box, estride,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+}  // namespace sb

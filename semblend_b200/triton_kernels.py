@@ -9,6 +9,8 @@ runs a hand-written sm_100a kernel of ``libsemblend_b200``.  CPU tensors raise
 
 from __future__ import annotations
 
+import math
+
 import torch
 
 from . import _lib, _rows
@@ -95,8 +97,128 @@ def scatter_donor_kv_paged(
     return kv_cache
 
 
+def _attn_tensor(t: torch.Tensor) -> _lib.SbAttnTensor:
+    """[B, H, S, D] view with a contiguous last dim as an sb_attn_tensor."""
+    if t.stride(-1) != 1:
+        raise ValueError("attention tensors need a contiguous head dimension")
+    a = _lib.SbAttnTensor()
+    a.data = t.data_ptr()
+    # a size-1 dim may carry any stride: give it the packed one so tensor maps stay well formed
+    st = list(t.stride())
+    for i in (2, 1, 0):
+        if t.shape[i] == 1:
+            st[i] = st[i + 1] * t.shape[i + 1]
+    a.stride_batch, a.stride_head, a.stride_seq = st[0], st[1], st[2]
+    return a
+
+
+def mask_to_rows(compute_mask: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """Compact a ``[B, S]`` (or ``[S]``) bool mask into ascending row indices
+    ``[B, S]`` (int32, valid up to ``counts[b]``) and ``counts [B]`` on the
+    device, without synchronising (``sb_mask_to_rows``)."""
+    _lib.require_cuda(compute_mask, "compute_mask")
+    m = compute_mask if compute_mask.ndim == 2 else compute_mask.unsqueeze(0)
+    m = m.to(torch.uint8).contiguous()
+    B, S = m.shape
+    rows = torch.empty(B, max(S, 1), dtype=torch.int32, device=m.device)
+    counts = torch.empty(B, dtype=torch.int32, device=m.device)
+    lib = _lib.load()
+    _lib.check(lib.sb_mask_to_rows(m.data_ptr(), S, B, S, rows.data_ptr(), rows.shape[1], counts.data_ptr(),
+                                   _lib.stream_ptr(m.device)), "sb_mask_to_rows")
+    return rows, counts
+
+
+def gqa_partial_attention(
+    query: torch.Tensor,
+    key: torch.Tensor,
+    value: torch.Tensor,
+    rows: torch.Tensor,
+    counts: torch.Tensor,
+    out: torch.Tensor,
+    scale: float | None = None,
+    max_rows: int | None = None,
+    status: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """Causal attention at compacted rows with grouped-query heads.
+
+    ``query``/``out`` ``[B, Hq, S, D]``, ``key``/``value`` ``[B, Hkv, S, D]``
+    (``Hq % Hkv == 0``; query head h reads KV head ``h // (Hq // Hkv)``),
+    ``rows [B, R]`` ascending positions valid up to ``counts[b]``.  Writes
+    ``out`` at those rows only and returns it.  bf16 / fp16 with D = 128 run
+    on the tensor cores; fp32 and other head dims on CUDA cores.  ``status``
+    (device int32) receives a value >= 2 if a kernel wait timed out.
+    """
+    for t, n in ((query, "query"), (key, "key"), (value, "value"), (out, "out"), (rows, "rows"), (counts, "counts")):
+        _lib.require_cuda(t, n)
+    B, Hq, S, D = query.shape
+    Hkv = key.shape[1]
+    if key.shape != (B, Hkv, S, D) or value.shape != key.shape or out.shape != query.shape:
+        raise ValueError(f"shape mismatch: q {tuple(query.shape)} k {tuple(key.shape)} v {tuple(value.shape)}")
+    if Hq % Hkv:
+        raise ValueError(f"{Hq} query heads are not a multiple of {Hkv} KV heads")
+    if not (query.dtype == key.dtype == value.dtype == out.dtype):
+        raise TypeError("query, key, value and out must share a dtype")
+    if rows.dtype != torch.int32 or counts.dtype != torch.int32:
+        raise TypeError("rows and counts must be int32")
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    if max_rows is None:
+        max_rows = rows.shape[1]
+    dev = query.device
+    if status is None:
+        status = torch.zeros(1, dtype=torch.int32, device=dev)
+    lib = _lib.load()
+    _lib.check(
+        lib.sb_partial_attention(
+            _attn_tensor(query), _attn_tensor(key), _attn_tensor(value), _attn_tensor(out),
+            rows.data_ptr(), rows.stride(0) if rows.shape[0] > 1 else rows.shape[1], counts.data_ptr(),
+            int(max_rows), B, Hq, Hkv, S, D, float(scale), _lib.dtype_code(query.dtype), status.data_ptr(),
+            _lib.stream_ptr(dev),
+        ),
+        "sb_partial_attention",
+    )
+    return out
+
+
+def partial_prefill_attention(
+    query: torch.Tensor,
+    key: torch.Tensor,
+    value: torch.Tensor,
+    compute_mask: torch.Tensor,
+    scale: float | None = None,
+) -> torch.Tensor:
+    """Causal attention only at compute-mask rows; other rows are zero.
+
+    Mirrors semblend_core/triton_kernels.py:655-734: ``query``/``key``/
+    ``value`` ``[H, S, D]``, ``compute_mask [S]`` bool, returns
+    ``[H, S, D]`` in the query's dtype.  Extensions: ``key``/``value`` may
+    have fewer heads than ``query`` (grouped-query attention), and a leading
+    batch dimension (``[B, H, S, D]`` with a ``[B, S]`` mask) is accepted.
+    The compacted rows are built on the device (no ``.item()`` sync on the
+    tensor-core path).
+    """
+    batched = query.ndim == 4
+    q = query if batched else query.unsqueeze(0)
+    k = key if batched else key.unsqueeze(0)
+    v = value if batched else value.unsqueeze(0)
+    _lib.require_cuda(q, "query")
+    output = torch.zeros_like(q)
+    S, D = q.shape[2], q.shape[3]
+    if S == 0:
+        return output if batched else output[0]
+    rows, counts = mask_to_rows(compute_mask)
+    tc_path = q.dtype in (torch.float16, torch.bfloat16) and D == 128
+    max_rows = S if tc_path else int(counts.max().item())
+    if max_rows > 0:
+        gqa_partial_attention(q, k.to(q.dtype), v.to(q.dtype), rows, counts, output, scale, max_rows=max_rows)
+    return output if batched else output[0]
+
+
 __all__ = [
     "HAS_TRITON",
+    "gqa_partial_attention",
+    "mask_to_rows",
+    "partial_prefill_attention",
     "scatter_donor_kv",
     "scatter_donor_kv_paged",
 ]

@@ -70,7 +70,8 @@ def _c_layout(tmp_path: Path, structs: dict[str, list[str]]) -> dict[str, int]:
 
 def test_struct_layouts_match_header(tmp_path):
     mirrors = {name: cls for name, cls in _lib.__dict__.items() if isinstance(cls, type) and issubclass(cls, ctypes.Structure)}
-    c_names = {"SbRows": "sb_rows", "SbInjectDesc": "sb_inject_desc", "SbInjectParams": "sb_inject_params"}
+    c_names = {"SbRows": "sb_rows", "SbInjectDesc": "sb_inject_desc", "SbInjectParams": "sb_inject_params",
+               "SbAttnTensor": "sb_attn_tensor"}
     c_names.update({k: v for k, v in getattr(_lib, "C_STRUCT_NAMES", {}).items()})
     structs = {c_names[n]: [f[0] for f in cls._fields_] for n, cls in mirrors.items() if n in c_names}
     layout = _c_layout(tmp_path, structs)
