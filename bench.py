@@ -367,7 +367,7 @@ def run_search(args, local: int) -> dict:
     status = torch.zeros(1, dtype=torch.int32, device=dev)
 
     def step(q):
-        return cosine_topk_async(m.emb, m.emb_bf16, m.valid, m.stats, q, S_K, S_THR, status=status,
+        return cosine_topk_async(m.emb, m.emb16, m.valid, m.stats, q, S_K, S_THR, status=status,
                                  workspace_owner=m, out=out)
 
     for _ in range(args.warmup):
@@ -444,7 +444,7 @@ def run_search(args, local: int) -> dict:
                    "candidates_per_query": {"mean": round(float(cand.mean()), 1), "max": int(cand.max())}},
         "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
                      "frac": round(achieved / pk["bf16_tflops"], 4), "peak_source": pk["source"],
-                     "kernel": "screen_kernel<8> (bf16 tcgen05, 2*N*Q*d flops)", "kernel_ms": round(kt.mean_ms, 4),
+                     "kernel": "screen_kernel<8> (fp16 tcgen05, 2*N*Q*d flops)", "kernel_ms": round(kt.mean_ms, 4),
                      "traffic": None},
         "e2e": {"value": round(S_QUERIES / (e2e_ms * 1e-3), 1), "unit": "q/s",
                 "h2d_bytes_per_step": hq.numel() * 4, "d2h_bytes_per_step": S_QUERIES * S_K * 12},

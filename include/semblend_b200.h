@@ -173,16 +173,17 @@ SB_API int sb_permute_paged(const sb_rows *cache, const void *src_pos,
 /* ------------------------------------------------------------------------ */
 /* Donor search                                                             */
 /* ------------------------------------------------------------------------ */
-/* Refresh the bf16 screening copy of rows of a row-major fp32 embedding
- * matrix (row pitch ld_emb floats) into emb_bf16 (row pitch ld_bf16, columns
- * [dim, dim_pad) zeroed), and raise stats[0] / stats[1] (device floats,
- * start at 0) to the largest ||e - bf16(e)|| and ||bf16(e)|| seen.  Rows are
- * rows[0..n_rows) (device int64) or, when rows is NULL, the range
+/* Refresh the 16-bit screening copy of rows of a row-major fp32 embedding
+ * matrix (row pitch ld_emb floats) into emb16 (shadow_dtype SB_DTYPE_F16 or
+ * SB_DTYPE_BF16, row pitch ld_16 elements, columns [dim, dim_pad) zeroed),
+ * and raise stats[0] / stats[1] (device floats, start at 0) to the largest
+ * ||e - e16|| and ||e16|| seen (+inf if a value overflows the 16-bit type).
+ * Rows are rows[0..n_rows) (device int64) or, when rows is NULL, the range
  * [row_begin, row_begin + n_rows).  This is the device side of the
  * reference's row write in DonorStore.add_donor
  * (semblend_core/donor_store.py:155-161). */
-SB_API int sb_search_prepare_rows(const float *emb, int64_t ld_emb, uint16_t *emb_bf16,
-                                  int64_t ld_bf16, int32_t dim, int32_t dim_pad,
+SB_API int sb_search_prepare_rows(const float *emb, int64_t ld_emb, void *emb16, int64_t ld_16,
+                                  int32_t dim, int32_t dim_pad, int32_t shadow_dtype,
                                   const int64_t *rows, int64_t row_begin, int64_t n_rows,
                                   float *stats, void *stream);
 
@@ -197,9 +198,9 @@ SB_API int64_t sb_cosine_topk_workspace_bytes(int32_t n_queries, int64_t n_rows,
  * NULL) and fp32 similarity emb[j] . qn >= min_similarity, ordered by
  * (similarity desc, j asc), as out_ids[q*k + r] = j + id_offset and
  * out_scores[q*k + r]; missing entries are -1 / -inf.  Screening runs on the
- * tensor cores in bf16 (emb_bf16, dim_pad a multiple of 64, <= 512) and every
- * candidate within the proven bf16 error bound is rescored exactly, so the
- * result equals the fp32 computation.  k <= 32; capacity (>= k) bounds the
+ * tensor cores on the 16-bit copy (emb16 of shadow_dtype, dim_pad a multiple
+ * of 64, <= 512) and every candidate within the proven 16-bit error bound is
+ * rescored exactly in fp32, so the result equals the fp32 computation.  k <= 32; capacity (>= k) bounds the
  * screening candidates kept per query.  *status (device int32, zeroed by the
  * caller) gets bit 0 set if some query had more than `capacity` candidates
  * (its results are withheld: retry with a larger capacity) and a value >= 2
@@ -208,8 +209,8 @@ SB_API int64_t sb_cosine_topk_workspace_bytes(int32_t n_queries, int64_t n_rows,
  * Replaces the cosine / threshold / top-k stage of DonorStore.find_donors
  * (semblend_core/donor_store.py:323-341) and DonorStore.find_donor (:205-229),
  * one query at a time there. */
-SB_API int sb_cosine_topk(const float *emb, int64_t ld_emb, const uint16_t *emb_bf16,
-                          int64_t ld_bf16, const uint8_t *valid, int64_t n_rows, int32_t dim,
+SB_API int sb_cosine_topk(const float *emb, int64_t ld_emb, const void *emb16, int64_t ld_16,
+                          int32_t shadow_dtype, const uint8_t *valid, int64_t n_rows, int32_t dim,
                           int32_t dim_pad, const float *stats, const float *queries,
                           int64_t ld_q, int32_t n_queries, int32_t k, float min_similarity,
                           int64_t id_offset, int64_t *out_ids, float *out_scores,

@@ -8,21 +8,26 @@
 //  1. prep:    normalise each query exactly as the reference does (fp32), keep
 //              the fp32 copy for rescoring and a bf16 copy for the tensor
 //              cores, and a per-query bound delta_q on |exact - bf16 score|.
-//  2. screen:  a persistent, warp-specialised tcgen05 GEMM of the bf16 query
+//  2. screen:  a persistent, warp-specialised tcgen05 GEMM of the 16-bit query
 //              tile (128 queries, resident in shared memory) against streamed
-//              256-donor bf16 tiles (TMA, 128-byte swizzle), fp32 accumulators
-//              double-buffered in tensor memory.  The epilogue warps own one
-//              query row each and keep, without any cross-thread exchange, a
-//              register top-k of bf16 scores; a donor becomes a *candidate* if
-//              its bf16 score is >= max(min_similarity - delta, L - 2 delta),
-//              where L is a lower bound on the k-th best bf16 score shared by
-//              all CTAs through one atomicMax word per query.  Every true
-//              top-k donor satisfies this (its bf16 score is >= its exact score
-//              - delta >= the k-th exact score - delta >= L - 2 delta), so the
-//              candidate set provably contains the exact answer.
-//  3. rescore: exact fp32 dot products (double accumulation) of every
-//              candidate, threshold, and selection of the top k by
-//              (score desc, row asc).
+//              256-donor 16-bit tiles (TMA, 128-byte swizzle), fp32
+//              accumulators double-buffered in tensor memory.  The 16-bit copy
+//              is fp16 (10 mantissa bits; the default for bounded embeddings)
+//              or bf16.  Eight epilogue warps each own one query row and half
+//              of the tile's columns and keep, without cross-thread exchange,
+//              a register top-k of screening scores; a donor becomes a
+//              *candidate* (row, screening score) if its screening score is
+//              >= max(min_similarity - delta, L - 2 delta), where L is a lower
+//              bound on the k-th best screening score A_k, shared by all CTAs
+//              through one atomicMax word per query.
+//  3. rescore: per query, the exact A_k over all candidates, then exact fp32
+//              dot products (double accumulation) of the candidates whose
+//              screening score is >= A_k - 2 delta, threshold, and selection
+//              of the top k by (score desc, row asc).
+// Every true top-k donor passes both filters: its screening score is >= its
+// exact score - delta >= the k-th exact score - delta >= A_k - 2 delta >=
+// L - 2 delta (the k rows with the best screening scores all have exact
+// scores >= A_k - delta), so the result equals the fp32 computation.
 //
 // delta_q = ||q~|| max||e - e~|| + ||q - q~|| max||e~|| + ||q - q~|| max||e - e~||
 //           + dim 2^-23 ||q~|| max||e~||  (Cauchy-Schwarz on the rounding
@@ -60,19 +65,30 @@ struct ScreenParams {
   int64_t n_units;
   float thr;
   int cap;
+  uint32_t idesc;
   const uint32_t *valid_bits;  // bit j = row j searchable (bits past n_rows are 0)
   int64_t n_valid_words;
   const float *delta;
   int *count;
   int *lower;
-  int *cand;
+  int2 *cand;  // (row, screening score bits)
   int *status;
 };
 
+template <typename T> struct Half16;
+template <> struct Half16<__nv_bfloat16> {
+  static __device__ __forceinline__ __nv_bfloat16 from(float x) { return __float2bfloat16_rn(x); }
+  static __device__ __forceinline__ float to(__nv_bfloat16 x) { return __bfloat162float(x); }
+};
+template <> struct Half16<__half> {
+  static __device__ __forceinline__ __half from(float x) { return __float2half_rn(x); }
+  static __device__ __forceinline__ float to(__half x) { return __half2float(x); }
+};
+
+template <typename T>
 __global__ void query_prep_kernel(const float *__restrict__ q, int64_t ld_q, int nq, int dim, int dim_pad,
-                                  const float *__restrict__ stats, float *__restrict__ qn,
-                                  __nv_bfloat16 *__restrict__ qb, float *__restrict__ delta,
-                                  int *__restrict__ count, int *__restrict__ lower) {
+                                  const float *__restrict__ stats, float *__restrict__ qn, T *__restrict__ qb,
+                                  float *__restrict__ delta, int *__restrict__ count, int *__restrict__ lower) {
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) / 32;
   const int lane = threadIdx.x % 32;
   if (warp >= nq) return;
@@ -90,9 +106,9 @@ __global__ void query_prep_kernel(const float *__restrict__ q, int64_t ld_q, int
       v = __fdiv_rn(row[i], denom);
       qn[(int64_t)warp * dim + i] = v;
     }
-    const __nv_bfloat16 b = __float2bfloat16_rn(v);
+    const T b = Half16<T>::from(v);
     qb[(int64_t)warp * dim_pad + i] = b;
-    const float bf = __bfloat162float(b);
+    const float bf = Half16<T>::to(b);
     nb = fmaf(bf, bf, nb);
     nd = fmaf(v - bf, v - bf, nd);
   }
@@ -105,7 +121,8 @@ __global__ void query_prep_kernel(const float *__restrict__ q, int64_t ld_q, int
     const float dmax = stats[0], emax = stats[1];
     const float qbn = sqrtf(nb), dqn = sqrtf(nd);
     const float acc = (float)dim * 1.1920929e-7f * qbn * emax;
-    delta[warp] = (qbn * dmax + dqn * emax + dqn * dmax + acc) * 1.001f + 1e-6f;
+    const float d = (qbn * dmax + dqn * emax + dqn * dmax + acc) * 1.001f + 1e-6f;
+    delta[warp] = isfinite(d) ? d : INFINITY;  // a 16-bit overflow disables screening
     count[warp] = 0;
     lower[warp] = tc::float_to_ordered(-INFINITY);
   }
@@ -228,7 +245,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     if (lane == 0) {
       // ---------------- MMA issuer ----------------
-      constexpr uint32_t idesc = tc::idesc_bf16_f32(kBM, kBN);
+      const uint32_t idesc = P.idesc;
       uint32_t it = 0, qi = 0, ai = 0;
       bool ok = true;
       for (int64_t u = blockIdx.x; u < P.n_units && ok; u += gridDim.x) {
@@ -313,40 +330,52 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc::fence_after_sync();
         const uint32_t base = tmem + ((uint32_t)(quarter * 32) << 16) + b * kBN + half * (kBN / 2);
         const float tk_before = tk[KT - 1];
-        int nc = 0, cbuf0 = 0, cbuf1 = 0, cbuf2 = 0, cbuf3 = 0;
-        auto flush = [&]() {
-          const int slot = atomicAdd(&P.count[q], nc);
-          const int v[4] = {cbuf0, cbuf1, cbuf2, cbuf3};
-#pragma unroll
-          for (int i = 0; i < 4; ++i)
-            if (i < nc && slot + i < P.cap) P.cand[(int64_t)q * P.cap + slot + i] = v[i];
-          nc = 0;
-        };
+        int nc = 0;
+        int2 cb0 = make_int2(0, 0), cb1 = cb0, cb2 = cb0, cb3 = cb0;
 #pragma unroll 1
         for (int c = 0; c < kBN / 2; c += 64) {
           uint32_t r0[32], r1[32];
           tc::tmem_ld32(base + c, r0);
           tc::tmem_ld32(base + c + 32, r1);
           tc::tmem_ld_wait();
-          if (active) {
+          if (!active) continue;
+          // compact hot path: one compare per column into a hit mask
+          // (!(x < cut) also keeps NaN scores, and everything once cut is -inf)
+          uint32_t h0 = 0, h1 = 0;
 #pragma unroll
-            for (int i = 0; i < 64; ++i) {
-              const float s = __uint_as_float(i < 32 ? r0[i] : r1[i - 32]);
-              if (s >= cut) {
-                const int col = c + i;
-                if ((vb[col >> 5] >> (col & 31)) & 1u) {
-                  const int j = (int)(c0 + col);
-                  if (nc == 0) cbuf0 = j;
-                  else if (nc == 1) cbuf1 = j;
-                  else if (nc == 2) cbuf2 = j;
-                  else cbuf3 = j;
-                  if (++nc == 4) flush();
-                  if (s > tk[KT - 1]) {
-                    topk_insert<KT>(tk, s);
-                    cut = fmaxf(cut, tk[KT - 1] - two_d);
-                  }
-                }
-              }
+          for (int i = 0; i < 32; ++i) {
+            h0 |= (__uint_as_float(r0[i]) < cut ? 0u : 1u) << i;
+            h1 |= (__uint_as_float(r1[i]) < cut ? 0u : 1u) << i;
+          }
+          h0 &= vb[c >> 5];
+          h1 &= vb[(c >> 5) + 1];
+          // rare path, emitted once: every hit becomes a candidate
+#pragma unroll 1
+          while (h0 | h1) {
+            const bool lo = h0 != 0;
+            const int i = __ffs(lo ? h0 : h1) - 1;
+            if (lo) h0 &= h0 - 1; else h1 &= h1 - 1;
+            uint32_t bits = 0;
+#pragma unroll
+            for (int x = 0; x < 32; ++x) bits = (x == i) ? (lo ? r0[x] : r1[x]) : bits;
+            const float sc = __uint_as_float(bits);
+            const int2 e = make_int2((int)(c0 + c + (lo ? 0 : 32) + i), (int)bits);
+            if (nc == 0) cb0 = e;
+            else if (nc == 1) cb1 = e;
+            else if (nc == 2) cb2 = e;
+            else cb3 = e;
+            if (++nc == 4) {
+              const int slot = atomicAdd(&P.count[q], 4);
+              int2 *dst = P.cand + (int64_t)q * P.cap;
+              if (slot + 0 < P.cap) dst[slot + 0] = cb0;
+              if (slot + 1 < P.cap) dst[slot + 1] = cb1;
+              if (slot + 2 < P.cap) dst[slot + 2] = cb2;
+              if (slot + 3 < P.cap) dst[slot + 3] = cb3;
+              nc = 0;
+            }
+            if (sc > tk[KT - 1]) {
+              topk_insert<KT>(tk, sc);
+              cut = fmaxf(cut, tk[KT - 1] - two_d);
             }
           }
         }
@@ -355,7 +384,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) tc::mbar_arrive(&acc_empty[b]);
         ++ai;
         if (active) {
-          if (nc) flush();
+          if (nc) {
+            const int slot = atomicAdd(&P.count[q], nc);
+            int2 *dst = P.cand + (int64_t)q * P.cap;
+            if (slot + 0 < P.cap) dst[slot + 0] = cb0;
+            if (nc > 1 && slot + 1 < P.cap) dst[slot + 1] = cb1;
+            if (nc > 2 && slot + 2 < P.cap) dst[slot + 2] = cb2;
+          }
           if (tk[KT - 1] > tk_before) atomicMax(&P.lower[q], tc::float_to_ordered(tk[KT - 1]));
           cut = fmaxf(cut, tc::ordered_to_float(lg) - two_d);
         }
@@ -369,14 +404,51 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) tc::tmem_dealloc(tmem, 512);
 }
 
-// Exact rescoring of the candidates of one query and top-k selection.
+// Block-wide argmax over (score desc, id asc) of n entries; returns the
+// winner's position in `pos` (or -1) to every thread.
+__device__ __forceinline__ void block_argmax(const float *sc, const int *sid, int n, float &bs, int &bi, int &bp,
+                                             float *red_s, int *red_i, int *red_p) {
+  const int tid = threadIdx.x, lane = tid % 32, warp = tid / 32, nwarps = blockDim.x / 32;
+  bs = -INFINITY, bi = INT_MAX, bp = -1;
+  for (int i = tid; i < n; i += blockDim.x) {
+    const float s = sc[i];
+    const int id = sid[i];
+    if (s > bs || (s == bs && s > -INFINITY && id < bi)) bs = s, bi = id, bp = i;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float os = __shfl_xor_sync(0xffffffffu, bs, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    const int op = __shfl_xor_sync(0xffffffffu, bp, o);
+    if (os > bs || (os == bs && oi < bi)) bs = os, bi = oi, bp = op;
+  }
+  if (lane == 0) red_s[warp] = bs, red_i[warp] = bi, red_p[warp] = bp;
+  __syncthreads();
+  bs = lane < nwarps ? red_s[lane] : -INFINITY;
+  bi = lane < nwarps ? red_i[lane] : INT_MAX;
+  bp = lane < nwarps ? red_p[lane] : -1;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float os = __shfl_xor_sync(0xffffffffu, bs, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    const int op = __shfl_xor_sync(0xffffffffu, bp, o);
+    if (os > bs || (os == bs && oi < bi)) bs = os, bi = oi, bp = op;
+  }
+  __syncthreads();
+}
+
+// Per query: the exact k-th best screening score A_k over the candidates,
+// exact fp32 rescoring of candidates with screening score >= A_k - 2 delta,
+// threshold and top-k selection by (score desc, row asc).
 __global__ void rescore_kernel(const float *__restrict__ emb, int64_t ld_emb, int dim,
-                               const float *__restrict__ qn, const int *__restrict__ count,
-                               const int *__restrict__ cand, int cap, float thr, int k, int64_t id_offset,
-                               int64_t *__restrict__ out_ids, float *__restrict__ out_scores, int *status) {
+                               const float *__restrict__ qn, const float *__restrict__ delta,
+                               const int *__restrict__ count, const int2 *__restrict__ cand, int cap, float thr,
+                               int k, int64_t id_offset, int64_t *__restrict__ out_ids,
+                               float *__restrict__ out_scores, int *status) {
   extern __shared__ float sh[];
   float *sq = sh;                                  // [dim]
-  float *sc = sq + ((dim + 3) & ~3);               // [cap]
+  float *sa = sq + ((dim + 3) & ~3);               // [cap] screening scores (scratch)
+  float *sc = sa + cap;                            // [cap] exact scores
   int *sid = reinterpret_cast<int *>(sc + cap);    // [cap]
   __shared__ float red_s[32];
   __shared__ int red_i[32];
@@ -389,10 +461,34 @@ __global__ void rescore_kernel(const float *__restrict__ emb, int64_t ld_emb, in
     n = 0;  // results for this query are withheld (reported as overflow)
   }
   for (int i = tid; i < dim; i += blockDim.x) sq[i] = qn[(int64_t)q * dim + i];
+  for (int i = tid; i < n; i += blockDim.x) {
+    const int2 e = cand[(int64_t)q * cap + i];
+    sid[i] = e.x;
+    sa[i] = __int_as_float(e.y);
+  }
   __syncthreads();
+  float keep = -INFINITY;  // screening-score floor for exact rescoring
+  if (n > k) {
+    float bs;
+    int bi, bp;
+    for (int r = 0; r < k; ++r) {
+      block_argmax(sa, sid, n, bs, bi, bp, red_s, red_i, red_p);
+      if (tid == 0 && bp >= 0) sa[bp] = -INFINITY;
+      __syncthreads();
+      keep = bs;  // after k rounds: the k-th best screening score
+    }
+    const float dq = delta[q];
+    keep = isfinite(dq) ? keep - 2.f * dq : -INFINITY;
+    // restore the screening scores taken out
+    for (int i = tid; i < n; i += blockDim.x) sa[i] = __int_as_float(cand[(int64_t)q * cap + i].y);
+    __syncthreads();
+  }
   for (int i = warp; i < n; i += nwarps) {
-    const int j = cand[(int64_t)q * cap + i];
-    const float *e = emb + (int64_t)j * ld_emb;
+    if (sa[i] < keep) {  // NaN screening scores are always rescored
+      if (lane == 0) sc[i] = -INFINITY;
+      continue;
+    }
+    const float *e = emb + (int64_t)sid[i] * ld_emb;
     double acc = 0.0;
     for (int d = lane; d < dim; d += 32) acc = fma((double)sq[d], (double)e[d], acc);
 #pragma unroll
@@ -400,44 +496,18 @@ __global__ void rescore_kernel(const float *__restrict__ emb, int64_t ld_emb, in
     if (lane == 0) {
       const float s = (float)acc;
       sc[i] = s >= thr ? s : -INFINITY;
-      sid[i] = j;
     }
   }
   __syncthreads();
   for (int r = 0; r < k; ++r) {
-    float bs = -INFINITY;
-    int bi = INT_MAX, bp = -1;
-    for (int i = tid; i < n; i += blockDim.x) {
-      const float s = sc[i];
-      const int id = sid[i];
-      if (s > bs || (s == bs && s > -INFINITY && id < bi)) bs = s, bi = id, bp = i;
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float os = __shfl_xor_sync(0xffffffffu, bs, o);
-      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-      const int op = __shfl_xor_sync(0xffffffffu, bp, o);
-      if (os > bs || (os == bs && oi < bi)) bs = os, bi = oi, bp = op;
-    }
-    if (lane == 0) red_s[warp] = bs, red_i[warp] = bi, red_p[warp] = bp;
-    __syncthreads();
-    if (warp == 0) {
-      bs = lane < nwarps ? red_s[lane] : -INFINITY;
-      bi = lane < nwarps ? red_i[lane] : INT_MAX;
-      bp = lane < nwarps ? red_p[lane] : -1;
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        const float os = __shfl_xor_sync(0xffffffffu, bs, o);
-        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-        const int op = __shfl_xor_sync(0xffffffffu, bp, o);
-        if (os > bs || (os == bs && oi < bi)) bs = os, bi = oi, bp = op;
-      }
-      if (lane == 0) {
-        const bool hit = bs > -INFINITY;
-        out_ids[(int64_t)q * k + r] = hit ? (int64_t)bi + id_offset : -1;
-        out_scores[(int64_t)q * k + r] = hit ? bs : -INFINITY;
-        if (hit) sc[bp] = -INFINITY;
-      }
+    float bs;
+    int bi, bp;
+    block_argmax(sc, sid, n, bs, bi, bp, red_s, red_i, red_p);
+    if (tid == 0) {
+      const bool hit = bs > -INFINITY;
+      out_ids[(int64_t)q * k + r] = hit ? (int64_t)bi + id_offset : -1;
+      out_scores[(int64_t)q * k + r] = hit ? bs : -INFINITY;
+      if (hit) sc[bp] = -INFINITY;
     }
     __syncthreads();
   }
@@ -448,9 +518,10 @@ __global__ void fill_empty_kernel(int64_t *ids, float *scores, int64_t n) {
   if (i < n) ids[i] = -1, scores[i] = -INFINITY;
 }
 
-__global__ void prepare_rows_kernel(const float *__restrict__ emb, int64_t ld_emb, __nv_bfloat16 *__restrict__ eb,
-                                    int64_t ld_b, int dim, int dim_pad, const int64_t *__restrict__ rows,
-                                    int64_t row_begin, int64_t n, float *stats) {
+template <typename T>
+__global__ void prepare_rows_kernel(const float *__restrict__ emb, int64_t ld_emb, T *__restrict__ eb, int64_t ld_b,
+                                    int dim, int dim_pad, const int64_t *__restrict__ rows, int64_t row_begin,
+                                    int64_t n, float *stats) {
   const int64_t w = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) / 32;
   const int lane = threadIdx.x % 32;
   if (w >= n) return;
@@ -459,9 +530,9 @@ __global__ void prepare_rows_kernel(const float *__restrict__ emb, int64_t ld_em
   float nb = 0.f, nd = 0.f;
   for (int i = lane; i < dim_pad; i += 32) {
     const float v = i < dim ? e[i] : 0.f;
-    const __nv_bfloat16 b = __float2bfloat16_rn(v);
+    const T b = Half16<T>::from(v);
     eb[r * ld_b + i] = b;
-    const float bf = __bfloat162float(b);
+    const float bf = Half16<T>::to(b);
     nb = fmaf(bf, bf, nb);
     nd = fmaf(v - bf, v - bf, nd);
   }
@@ -471,9 +542,11 @@ __global__ void prepare_rows_kernel(const float *__restrict__ emb, int64_t ld_em
     nd += __shfl_xor_sync(0xffffffffu, nd, o);
   }
   if (lane == 0) {
-    // non-negative floats order like their bit patterns
-    atomicMax(reinterpret_cast<int *>(&stats[0]), __float_as_int(sqrtf(nd) * 1.0001f));
-    atomicMax(reinterpret_cast<int *>(&stats[1]), __float_as_int(sqrtf(nb) * 1.0001f));
+    // non-negative floats order like their bit patterns; a non-finite norm
+    // (a value outside the 16-bit range) poisons the bound to +inf
+    const float dn = sqrtf(nd) * 1.0001f, bn = sqrtf(nb) * 1.0001f;
+    atomicMax(reinterpret_cast<int *>(&stats[0]), __float_as_int(isfinite(dn) ? dn : INFINITY));
+    atomicMax(reinterpret_cast<int *>(&stats[1]), __float_as_int(isfinite(bn) ? bn : INFINITY));
   }
 }
 
@@ -513,8 +586,8 @@ inline int64_t align256(int64_t x) { return (x + 255) & ~int64_t(255); }
 struct Workspace {
   int *count, *lower;
   float *delta, *qn;
-  __nv_bfloat16 *qb;
-  int *cand;
+  void *qb;
+  int2 *cand;
   uint32_t *bits;
   int64_t bytes;
 };
@@ -532,8 +605,8 @@ Workspace carve(void *base, int nq, int dim, int dim_pad, int cap, int64_t n_row
   w.lower = reinterpret_cast<int *>(take(4LL * nq));
   w.delta = reinterpret_cast<float *>(take(4LL * nq));
   w.qn = reinterpret_cast<float *>(take(4LL * nq * dim));
-  w.qb = reinterpret_cast<__nv_bfloat16 *>(take(2LL * nq * dim_pad));
-  w.cand = reinterpret_cast<int *>(take(4LL * nq * cap));
+  w.qb = take(2LL * nq * dim_pad);
+  w.cand = reinterpret_cast<int2 *>(take(8LL * nq * cap));
   w.bits = reinterpret_cast<uint32_t *>(take(4LL * ((n_rows + 31) / 32 + 8)));
   w.bytes = off;
   return w;
@@ -563,17 +636,22 @@ int launch_screen(const CUtensorMap &tq, const CUtensorMap &te, const ScreenPara
 }  // namespace
 }  // namespace sb
 
-extern "C" SB_API int sb_search_prepare_rows(const float *emb, int64_t ld_emb, uint16_t *emb_bf16, int64_t ld_bf16,
-                                             int32_t dim, int32_t dim_pad, const int64_t *rows, int64_t row_begin,
-                                             int64_t n_rows, float *stats, void *stream) {
-  if (n_rows < 0 || dim <= 0 || dim_pad < dim || ld_emb < dim || ld_bf16 < dim_pad) return SB_ERR_INVALID_ARGUMENT;
+extern "C" SB_API int sb_search_prepare_rows(const float *emb, int64_t ld_emb, void *emb16, int64_t ld_16,
+                                             int32_t dim, int32_t dim_pad, int32_t shadow_dtype, const int64_t *rows,
+                                             int64_t row_begin, int64_t n_rows, float *stats, void *stream) {
+  if (n_rows < 0 || dim <= 0 || dim_pad < dim || ld_emb < dim || ld_16 < dim_pad) return SB_ERR_INVALID_ARGUMENT;
+  if (shadow_dtype != SB_DTYPE_F16 && shadow_dtype != SB_DTYPE_BF16) return SB_ERR_UNSUPPORTED;
   if (n_rows == 0) return SB_OK;
-  if (emb == nullptr || emb_bf16 == nullptr || stats == nullptr) return SB_ERR_INVALID_ARGUMENT;
+  if (emb == nullptr || emb16 == nullptr || stats == nullptr) return SB_ERR_INVALID_ARGUMENT;
   const int64_t threads = 256, warps_per_block = threads / 32;
   const int64_t blocks = (n_rows + warps_per_block - 1) / warps_per_block;
-  sb::prepare_rows_kernel<<<(unsigned)blocks, (unsigned)threads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      emb, ld_emb, reinterpret_cast<__nv_bfloat16 *>(emb_bf16), ld_bf16, dim, dim_pad, rows, row_begin, n_rows,
-      stats);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (shadow_dtype == SB_DTYPE_F16)
+    sb::prepare_rows_kernel<__half><<<(unsigned)blocks, (unsigned)threads, 0, st>>>(
+        emb, ld_emb, reinterpret_cast<__half *>(emb16), ld_16, dim, dim_pad, rows, row_begin, n_rows, stats);
+  else
+    sb::prepare_rows_kernel<__nv_bfloat16><<<(unsigned)blocks, (unsigned)threads, 0, st>>>(
+        emb, ld_emb, reinterpret_cast<__nv_bfloat16 *>(emb16), ld_16, dim, dim_pad, rows, row_begin, n_rows, stats);
   return sb::launch_status();
 }
 
@@ -583,23 +661,24 @@ extern "C" SB_API int64_t sb_cosine_topk_workspace_bytes(int32_t n_queries, int6
   return sb::carve(nullptr, n_queries, dim, dim_pad, capacity, n_rows).bytes;
 }
 
-extern "C" SB_API int sb_cosine_topk(const float *emb, int64_t ld_emb, const uint16_t *emb_bf16, int64_t ld_bf16,
-                                     const uint8_t *valid, int64_t n_rows, int32_t dim, int32_t dim_pad,
-                                     const float *stats, const float *queries, int64_t ld_q, int32_t n_queries,
-                                     int32_t k, float min_similarity, int64_t id_offset, int64_t *out_ids,
-                                     float *out_scores, int32_t capacity, void *workspace, int64_t workspace_bytes,
-                                     int32_t *status, void *stream) {
+extern "C" SB_API int sb_cosine_topk(const float *emb, int64_t ld_emb, const void *emb16, int64_t ld_16,
+                                     int32_t shadow_dtype, const uint8_t *valid, int64_t n_rows, int32_t dim,
+                                     int32_t dim_pad, const float *stats, const float *queries, int64_t ld_q,
+                                     int32_t n_queries, int32_t k, float min_similarity, int64_t id_offset,
+                                     int64_t *out_ids, float *out_scores, int32_t capacity, void *workspace,
+                                     int64_t workspace_bytes, int32_t *status, void *stream) {
   using namespace sb;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (n_queries < 0 || n_rows < 0 || k < 1 || k > 32 || dim <= 0) return SB_ERR_INVALID_ARGUMENT;
   if (dim_pad < dim || dim_pad % kBK != 0 || dim_pad > 512) return SB_ERR_UNSUPPORTED;
+  if (shadow_dtype != SB_DTYPE_F16 && shadow_dtype != SB_DTYPE_BF16) return SB_ERR_UNSUPPORTED;
   if (capacity < k || capacity > 16384) return SB_ERR_INVALID_ARGUMENT;
   if (n_rows > 0x7fffffffLL) return SB_ERR_TOO_LARGE;
   if (n_queries == 0) return SB_OK;
   if (queries == nullptr || out_ids == nullptr || out_scores == nullptr || status == nullptr || stats == nullptr)
     return SB_ERR_INVALID_ARGUMENT;
-  if (ld_q < dim || ld_emb < dim || ld_bf16 < dim_pad) return SB_ERR_INVALID_ARGUMENT;
-  if ((reinterpret_cast<uintptr_t>(emb_bf16) % 16) || ((ld_bf16 * 2) % 16)) return SB_ERR_INVALID_ARGUMENT;
+  if (ld_q < dim || ld_emb < dim || ld_16 < dim_pad) return SB_ERR_INVALID_ARGUMENT;
+  if ((reinterpret_cast<uintptr_t>(emb16) % 16) || ((ld_16 * 2) % 16)) return SB_ERR_INVALID_ARGUMENT;
   Workspace w = carve(workspace, n_queries, dim, dim_pad, capacity, n_rows);
   if (workspace == nullptr || workspace_bytes < w.bytes) return SB_ERR_WORKSPACE_TOO_SMALL;
   if (n_rows == 0) {
@@ -607,22 +686,30 @@ extern "C" SB_API int sb_cosine_topk(const float *emb, int64_t ld_emb, const uin
     fill_empty_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(out_ids, out_scores, n);
     return launch_status();
   }
-  if (emb == nullptr || emb_bf16 == nullptr) return SB_ERR_INVALID_ARGUMENT;
+  if (emb == nullptr || emb16 == nullptr) return SB_ERR_INVALID_ARGUMENT;
+  const bool f16 = shadow_dtype == SB_DTYPE_F16;
 
   const int64_t n_words = (n_rows + 31) / 32;
   {
     const int threads = 256;
     const int blocks = (n_queries * 32 + threads - 1) / threads;
-    query_prep_kernel<<<blocks, threads, 0, st>>>(queries, ld_q, n_queries, dim, dim_pad, stats, w.qn, w.qb,
-                                                  w.delta, w.count, w.lower);
+    if (f16)
+      query_prep_kernel<__half><<<blocks, threads, 0, st>>>(queries, ld_q, n_queries, dim, dim_pad, stats, w.qn,
+                                                            reinterpret_cast<__half *>(w.qb), w.delta, w.count,
+                                                            w.lower);
+    else
+      query_prep_kernel<__nv_bfloat16><<<blocks, threads, 0, st>>>(queries, ld_q, n_queries, dim, dim_pad, stats,
+                                                                   w.qn, reinterpret_cast<__nv_bfloat16 *>(w.qb),
+                                                                   w.delta, w.count, w.lower);
     valid_bits_kernel<<<(unsigned)((n_words + 255) / 256), 256, 0, st>>>(valid, n_rows, w.bits, n_words);
     int s = launch_status();
     if (s != SB_OK) return s;
   }
 
   CUtensorMap tq, te;
-  if (!make_tmap_bf16_2d(&tq, w.qb, dim_pad, n_queries, (uint64_t)dim_pad * 2, kBK, kBM) ||
-      !make_tmap_bf16_2d(&te, emb_bf16, dim_pad, n_rows, (uint64_t)ld_bf16 * 2, kBK, kBN))
+  const CUtensorMapDataType dt = f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  if (!make_tmap_16_2d(&tq, dt, w.qb, dim_pad, n_queries, (uint64_t)dim_pad * 2, kBK, kBM) ||
+      !make_tmap_16_2d(&te, dt, emb16, dim_pad, n_rows, (uint64_t)ld_16 * 2, kBK, kBN))
     return SB_ERR_CUDA;
 
   ScreenParams P;
@@ -635,6 +722,7 @@ extern "C" SB_API int sb_cosine_topk(const float *emb, int64_t ld_emb, const uin
   P.n_units = n_chunks * P.n_qtiles;
   P.thr = min_similarity;
   P.cap = capacity;
+  P.idesc = tc::idesc_f16(kBM, kBN, f16 ? 0u : 1u, 0u);
   P.valid_bits = w.bits;
   P.n_valid_words = n_words;
   P.delta = w.delta;
@@ -656,7 +744,7 @@ extern "C" SB_API int sb_cosine_topk(const float *emb, int64_t ld_emb, const uin
     s = launch_screen<32>(tq, te, P, grid, smem, st);
   if (s != SB_OK) return s;
 
-  const int rs_smem = (int)(((dim + 3) & ~3) * 4 + (int64_t)capacity * 8);
+  const int rs_smem = (int)(((dim + 3) & ~3) * 4 + (int64_t)capacity * 12);
   if (rs_smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(rescore_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, rs_smem);
     if (e != cudaSuccess) {
@@ -664,7 +752,7 @@ extern "C" SB_API int sb_cosine_topk(const float *emb, int64_t ld_emb, const uin
       return SB_ERR_CUDA;
     }
   }
-  rescore_kernel<<<n_queries, 256, rs_smem, st>>>(emb, ld_emb, dim, w.qn, w.count, w.cand, capacity,
+  rescore_kernel<<<n_queries, 256, rs_smem, st>>>(emb, ld_emb, dim, w.qn, w.delta, w.count, w.cand, capacity,
                                                   min_similarity, k, id_offset, out_ids, out_scores, status);
   return launch_status();
 }

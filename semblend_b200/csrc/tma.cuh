@@ -40,6 +40,22 @@ inline bool make_tmap_bf16_2d(CUtensorMap *map, const void *base, uint64_t cols,
   return r == CUDA_SUCCESS;
 }
 
+// 2-D row-major 16-bit matrix (bf16 or fp16, `dtype`), otherwise as
+// make_tmap_bf16_2d.
+inline bool make_tmap_16_2d(CUtensorMap *map, CUtensorMapDataType dtype, const void *base, uint64_t cols,
+                            uint64_t rows, uint64_t pitch_bytes, uint32_t box_cols, uint32_t box_rows) {
+  auto enc = tensor_map_encoder();
+  if (enc == nullptr) return false;
+  cuuint64_t gdim[2] = {cols, rows};
+  cuuint64_t gstride[1] = {pitch_bytes};
+  cuuint32_t box[2] = {box_cols, box_rows};
+  cuuint32_t estride[2] = {1, 1};
+  CUresult r = enc(map, dtype, 2, const_cast<void *>(base), gdim, gstride, box, estride,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 // 3-D bf16 tensor [d2, d1, cols] with pitches in bytes (dim 1 and dim 2),
 // boxes of box_cols x box_rows x 1, 128-byte swizzle, zero fill out of range.
 inline bool make_tmap_bf16_3d(CUtensorMap *map, const void *base, uint64_t cols, uint64_t d1, uint64_t d2,

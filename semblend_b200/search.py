@@ -2,7 +2,7 @@
 
 :class:`DeviceDonorMatrix` mirrors the reference DonorStore's row storage
 (``_embeddings [max_entries, dim]`` fp32 and ``_valid_mask``,
-semblend_core/donor_store.py:95-96) in HBM, plus the bf16 screening copy and
+semblend_core/donor_store.py:95-96) in HBM, plus the 16-bit screening copy and
 the rounding statistics the tensor-core search needs.  :meth:`search` runs
 ``sb_cosine_topk`` — the reference's per-query stage (normalise, cosine,
 threshold, top-k; donor_store.py:323-341) for a whole batch of queries.
@@ -30,9 +30,19 @@ def _pad64(d: int) -> int:
 
 
 class DeviceDonorMatrix:
-    """Fixed-capacity fp32 row matrix on one CUDA device with a bf16 shadow."""
+    """Fixed-capacity fp32 row matrix on one CUDA device with a 16-bit
+    screening copy.
 
-    def __init__(self, max_entries: int, dim: int, device: torch.device | str | int | None = None):
+    ``shadow_dtype`` is ``torch.float16`` (default: 10 mantissa bits, so the
+    proven screening error bound is 4x tighter than bf16 and fewer candidates
+    need exact rescoring; fine for embeddings with |value| < 65504, which
+    normalised sentence embeddings always are) or ``torch.bfloat16`` (any
+    range).  Results are exact either way; a row that overflows fp16 makes
+    the bound infinite (every row a candidate) rather than wrong.
+    """
+
+    def __init__(self, max_entries: int, dim: int, device: torch.device | str | int | None = None,
+                 shadow_dtype: torch.dtype = torch.float16):
         if device is None:
             device = torch.device("cuda", torch.cuda.current_device())
         self.device = torch.device(device) if not isinstance(device, int) else torch.device("cuda", device)
@@ -43,10 +53,13 @@ class DeviceDonorMatrix:
         self.dim_pad = _pad64(self.dim)
         if self.dim_pad > 512:
             raise ValueError(f"embedding dim {dim} > 512 is not supported by the search kernel")
+        if shadow_dtype not in (torch.float16, torch.bfloat16):
+            raise ValueError("shadow_dtype must be torch.float16 or torch.bfloat16")
+        self.shadow_dtype = shadow_dtype
         self.emb = torch.zeros(self.max_entries, self.dim, dtype=torch.float32, device=self.device)
-        self.emb_bf16 = torch.zeros(self.max_entries, self.dim_pad, dtype=torch.bfloat16, device=self.device)
+        self.emb16 = torch.zeros(self.max_entries, self.dim_pad, dtype=shadow_dtype, device=self.device)
         self.valid = torch.zeros(self.max_entries, dtype=torch.uint8, device=self.device)
-        # [max ||e - bf16(e)||, max ||bf16(e)||] over rows ever written (upper bounds)
+        # [max ||e - e16||, max ||e16||] over rows ever written (upper bounds)
         self.stats = torch.zeros(2, dtype=torch.float32, device=self.device)
         self._ws: torch.Tensor | None = None
         self._status = torch.zeros(1, dtype=torch.int32, device=self.device)
@@ -76,8 +89,9 @@ class DeviceDonorMatrix:
         lib = _lib.load()
         _lib.check(
             lib.sb_search_prepare_rows(
-                self.emb.data_ptr(), self.dim, self.emb_bf16.data_ptr(), self.dim_pad, self.dim, self.dim_pad,
-                None, begin, n, self.stats.data_ptr(), _lib.stream_ptr(self.device),
+                self.emb.data_ptr(), self.dim, self.emb16.data_ptr(), self.dim_pad, self.dim, self.dim_pad,
+                _lib.dtype_code(self.shadow_dtype), None, begin, n, self.stats.data_ptr(),
+                _lib.stream_ptr(self.device),
             ),
             "sb_search_prepare_rows",
         )
@@ -91,8 +105,9 @@ class DeviceDonorMatrix:
         lib = _lib.load()
         _lib.check(
             lib.sb_search_prepare_rows(
-                self.emb.data_ptr(), self.dim, self.emb_bf16.data_ptr(), self.dim_pad, self.dim, self.dim_pad,
-                rows_t.data_ptr(), 0, rows_t.shape[0], self.stats.data_ptr(), _lib.stream_ptr(self.device),
+                self.emb.data_ptr(), self.dim, self.emb16.data_ptr(), self.dim_pad, self.dim, self.dim_pad,
+                _lib.dtype_code(self.shadow_dtype), rows_t.data_ptr(), 0, rows_t.shape[0], self.stats.data_ptr(),
+                _lib.stream_ptr(self.device),
             ),
             "sb_search_prepare_rows",
         )
@@ -110,7 +125,7 @@ class DeviceDonorMatrix:
         q = q.to(device=self.device, dtype=torch.float32, non_blocking=True).contiguous()
         n_rows = self.max_entries if n_rows is None else int(n_rows)
         return cosine_topk(
-            self.emb, self.emb_bf16, self.valid, self.stats, q, k, min_similarity, n_rows=n_rows,
+            self.emb, self.emb16, self.valid, self.stats, q, k, min_similarity, n_rows=n_rows,
             id_offset=id_offset, capacity=capacity, status=self._status, workspace_owner=self,
         )
 
@@ -124,7 +139,7 @@ def _workspace(owner, nbytes: int, device: torch.device) -> torch.Tensor:
     return ws
 
 
-def cosine_topk_async(emb: torch.Tensor, emb_bf16: torch.Tensor, valid: torch.Tensor | None,
+def cosine_topk_async(emb: torch.Tensor, emb16: torch.Tensor, valid: torch.Tensor | None,
                       stats: torch.Tensor, queries: torch.Tensor, k: int, min_similarity: float, *,
                       n_rows: int | None = None, id_offset: int = 0, capacity: int = DEFAULT_CAPACITY,
                       status: torch.Tensor | None = None, workspace_owner=None,
@@ -135,19 +150,19 @@ def cosine_topk_async(emb: torch.Tensor, emb_bf16: torch.Tensor, valid: torch.Te
     before the results are trusted: bit 0 = a query overflowed ``capacity``
     (retry larger), values >= 2 = a kernel wait timed out.
     """
-    for t, name in ((emb, "emb"), (emb_bf16, "emb_bf16"), (queries, "queries"), (stats, "stats")):
+    for t, name in ((emb, "emb"), (emb16, "emb16"), (queries, "queries"), (stats, "stats")):
         _lib.require_cuda(t, name)
     dev = emb.device
     nq, dim = queries.shape
     n_rows = emb.shape[0] if n_rows is None else n_rows
-    dim_pad = emb_bf16.shape[1]
+    dim_pad = emb16.shape[1]
     k = int(k)
     if not 1 <= k <= 32:
         raise ValueError(f"k must be in [1, 32], got {k}")
     ld_q = queries.stride(0) if nq > 1 else dim  # a size-1 dim may carry any stride
     ld_e = emb.stride(0) if emb.shape[0] > 1 else dim
-    ld_b = emb_bf16.stride(0) if emb_bf16.shape[0] > 1 else dim_pad
-    if queries.stride(1) != 1 or emb.stride(1) != 1 or emb_bf16.stride(1) != 1:
+    ld_b = emb16.stride(0) if emb16.shape[0] > 1 else dim_pad
+    if queries.stride(1) != 1 or emb.stride(1) != 1 or emb16.stride(1) != 1:
         raise ValueError("queries and embedding rows must be contiguous along the embedding dimension")
     if out is None:
         ids = torch.empty(nq, k, dtype=torch.int64, device=dev)
@@ -164,7 +179,7 @@ def cosine_topk_async(emb: torch.Tensor, emb_bf16: torch.Tensor, valid: torch.Te
     ws = _workspace(workspace_owner, nbytes, dev)
     _lib.check(
         lib.sb_cosine_topk(
-            emb.data_ptr(), ld_e, emb_bf16.data_ptr(), ld_b,
+            emb.data_ptr(), ld_e, emb16.data_ptr(), ld_b, _lib.dtype_code(emb16.dtype),
             valid.data_ptr() if valid is not None else None, n_rows, dim, dim_pad, stats.data_ptr(),
             queries.data_ptr(), ld_q, nq, k, float(min_similarity), int(id_offset),
             ids.data_ptr(), scores.data_ptr(), cap, ws.data_ptr(), ws.numel(), status.data_ptr(),
@@ -175,7 +190,7 @@ def cosine_topk_async(emb: torch.Tensor, emb_bf16: torch.Tensor, valid: torch.Te
     return ids, scores, status
 
 
-def cosine_topk(emb: torch.Tensor, emb_bf16: torch.Tensor, valid: torch.Tensor | None, stats: torch.Tensor,
+def cosine_topk(emb: torch.Tensor, emb16: torch.Tensor, valid: torch.Tensor | None, stats: torch.Tensor,
                 queries: torch.Tensor, k: int, min_similarity: float, *, n_rows: int | None = None,
                 id_offset: int = 0, capacity: int = DEFAULT_CAPACITY, status: torch.Tensor | None = None,
                 workspace_owner=None) -> tuple[torch.Tensor, torch.Tensor]:
@@ -188,7 +203,7 @@ def cosine_topk(emb: torch.Tensor, emb_bf16: torch.Tensor, valid: torch.Tensor |
     cap = max(int(capacity), int(k))
     while True:
         ids, scores, st_t = cosine_topk_async(
-            emb, emb_bf16, valid, stats, queries, k, min_similarity, n_rows=n_rows, id_offset=id_offset,
+            emb, emb16, valid, stats, queries, k, min_similarity, n_rows=n_rows, id_offset=id_offset,
             capacity=cap, status=status, workspace_owner=workspace_owner)
         st = int(st_t.item())
         if st & ~1:

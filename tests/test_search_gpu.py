@@ -180,3 +180,25 @@ def test_donor_store_batch_add_matches_sequential():
     assert np.array_equal(a._embeddings, b._embeddings)
     assert np.array_equal(a._valid_mask, b._valid_mask)
     assert torch.equal(a.device_matrix.valid.cpu().bool(), torch.from_numpy(a._valid_mask))
+
+
+def test_bf16_shadow_vs_oracle():
+    E, centers, rng = clustered(8000, 384, 16, seed=11)
+    Q = queries_for(centers, rng, 200, 384)
+    m = DeviceDonorMatrix(E.shape[0], 384, DEV, shadow_dtype=torch.bfloat16)
+    m.write_range(0, torch.from_numpy(E).to(DEV))
+    ids, s = m.search(Q, 8, 0.6)
+    assert_topk_equivalent(E, np.ones(8000, bool), Q, 0.6, ids.cpu().numpy(), s.cpu().numpy(), 8)
+
+
+def test_fp16_overflow_rows_stay_exact():
+    rng = np.random.default_rng(12)
+    E = rng.standard_normal((3000, 64)).astype(np.float32)
+    E[17, 3] = 1e6  # beyond fp16 range: screening must fall back to rescoring everything
+    E[18, 5] = -1e6
+    Q = rng.standard_normal((5, 64)).astype(np.float32)
+    Q[0] = E[17] / np.linalg.norm(E[17])
+    m = build(E)
+    ids, s = m.search(Q, 4, -1e9)
+    assert_topk_equivalent(E, np.ones(3000, bool), Q, -1e9, ids.cpu().numpy(), s.cpu().numpy(), 4)
+    assert ids[0, 0].item() == 17
