@@ -1,0 +1,100 @@
+"""Host-side logic that needs no GPU: partial-attention plans against the
+reference's outputs, plan flattening, layout helpers, pair preprocessing and
+the module aliasing of ``semblend_b200.compat``."""
+
+from __future__ import annotations
+
+import json
+import sys
+
+import numpy as np
+import pytest
+import torch
+
+from semblend_b200 import _rows, compat
+from semblend_b200 import partial_attention as pa
+from semblend_b200.rope_correction import _host_pairs, _last_per_target
+from tests.helpers import GOLDEN
+
+
+@pytest.fixture(scope="module")
+def plans():
+    return json.loads((GOLDEN / "plans.json").read_text())
+
+
+def _build(entry):
+    a = entry["args"]
+    if entry["kind"] == "single":
+        return pa.build_attention_plan(a["donor_id"], a["target_len"], a["donor_len"], a["copy_positions"],
+                                       a["placeholder_positions"], a["slot_actions"], a["layer_hints"],
+                                       num_layers=a["num_layers"])
+    return pa.build_multi_donor_attention_plan(a["target_len"], a["slot_actions"], a["layer_hints"],
+                                               num_layers=a["num_layers"])
+
+
+def test_plans_match_reference(plans):
+    for entry in plans:
+        plan = _build(entry)
+        assert plan.num_reuse_positions == entry["num_reuse"]
+        assert plan.num_partial_positions == entry["num_partial"]
+        assert plan.num_full_layers == entry["num_full_layers"]
+        assert plan.computation_ratio == pytest.approx(entry["computation_ratio"], abs=0)
+        if entry["kind"] == "multi":
+            assert plan.donor_len == entry["donor_len"] and plan.donor_id == entry["donor_id"]
+            assert [list(x) for x in plan.donor_map] == entry["donor_map"]
+        for layer, (m, pairs) in enumerate(zip(entry["masks"], entry["pairs"])):
+            assert pa.compute_attention_mask(plan, layer).tolist() == m
+            assert [list(p) for p in pa.compute_donor_kv_indices(plan, layer)] == pairs
+
+
+def test_plan_arrays_agree_with_per_layer_functions(plans):
+    for entry in plans:
+        plan = _build(entry)
+        arr = pa.plan_arrays(plan)
+        for layer in range(len(plan.layer_masks)):
+            if arr.recompute_layers[layer]:
+                assert pa.compute_attention_mask(plan, layer).all()
+                assert pa.compute_donor_kv_indices(plan, layer) == []
+            else:
+                assert np.array_equal(pa.compute_attention_mask(plan, layer), arr.compute_mask)
+                got = list(zip(arr.donor_positions.tolist(), arr.target_positions.tolist()))
+                assert got == [tuple(p) for p in pa.compute_donor_kv_indices(plan, layer)]
+
+
+def test_layout_detection_and_geometry():
+    assert _rows.detect_layout(torch.empty(2, 100, 16, 4, 128)) == "vllm"
+    assert _rows.detect_layout(torch.empty(100, 2, 4, 16, 128)) == "canonical"
+    assert _rows.paged_geometry((2, 100, 16, 4, 128), "vllm") == (100, 4, 16, 128)
+    assert _rows.paged_geometry((100, 2, 16, 4, 128), "trtllm") == (100, 4, 16, 128)
+    with pytest.raises(ValueError):
+        _rows.paged_geometry((100, 3, 4, 16, 128), "canonical")
+    with pytest.raises(ValueError):
+        _rows.resolve_layout(torch.empty(1), "nonsense")
+
+
+def test_pair_preprocessing():
+    pairs = _host_pairs([(1, 5), (2, 6), (3, 5), (4, 7)])
+    assert pairs.shape == (4, 2)
+    kept = _last_per_target(pairs)
+    assert kept.tolist() == [[2, 6], [3, 5], [4, 7]]  # the last pair for target 5 wins, order kept
+    assert _host_pairs([]).shape == (0, 2)
+    with pytest.raises(ValueError):
+        _host_pairs([(1, 2, 3)])
+
+
+def test_compat_install_aliases_reference_names():
+    saved = {k: v for k, v in sys.modules.items() if k.split(".")[0] in compat.PARENTS}
+    try:
+        done = compat.install()
+        from semblend_core.rope_correction import rope_correct_scatter_paged
+        from synapse_kv_connector.donor_store import DonorStore
+
+        assert rope_correct_scatter_paged.__module__ == "semblend_b200.rope_correction"
+        assert DonorStore.__module__ == "semblend_b200.donor_store"
+        assert done["semblend_core.triton_kernels"] == "semblend_b200.triton_kernels"
+        compat.uninstall()
+        assert "semblend_core.rope_correction" not in sys.modules
+    finally:
+        for k in [k for k in sys.modules if k.split(".")[0] in compat.PARENTS]:
+            del sys.modules[k]
+        sys.modules.update(saved)
