@@ -170,6 +170,30 @@ SB_API int sb_permute_paged(const sb_rows *cache, const void *src_pos,
                             void *workspace, int64_t workspace_bytes,
                             uint64_t *err_counter, void *stream);
 
+/* Size of the fixed device scratch array used by sb_permute_paged_noalloc
+ * (32 MiB: for example one layer of 16384 pairs x 4 KV heads x head_dim 128
+ * in bf16). */
+#define SB_PERMUTE_NOALLOC_SCRATCH_BYTES (32LL << 20)
+
+/* sb_permute_paged for callers that cannot allocate device memory when they
+ * permute: an engine hook running inside the model's forward pass (whose
+ * memory pool was sized at start-up, or which is being captured into a CUDA
+ * graph), or a C / Go / Java caller without a caching allocator.  Same
+ * arguments and results as sb_permute_paged minus the workspace: the source
+ * rows are snapshotted into a fixed SB_PERMUTE_NOALLOC_SCRATCH_BYTES device
+ * array inside this library (held on every GPU that loads it until exit).
+ * Returns SB_ERR_TOO_LARGE, launching nothing, when
+ * sb_permute_workspace_bytes(...) exceeds that size.  It allocates nothing.
+ * The first call on a device resolves the array's device address, so make
+ * that call before any stream capture.  All calls share the one array: calls
+ * whose executions overlap on the GPU (other streams, other threads) race on
+ * it and must be serialised by the caller.  No counterpart in the reference
+ * (its permutation allocates with torch). */
+SB_API int sb_permute_paged_noalloc(const sb_rows *cache, const void *src_pos,
+                                    const void *dst_pos, int64_t n_pairs, int32_t pos_dtype,
+                                    const sb_inject_params *params, uint64_t *err_counter,
+                                    void *stream);
+
 /* ------------------------------------------------------------------------ */
 /* Donor search                                                             */
 /* ------------------------------------------------------------------------ */

@@ -31,6 +31,7 @@ SB_ANGLE_NONE, SB_ANGLE_DELTA, SB_ANGLE_NOPE, SB_ANGLE_CONST = 0, 1, 2, 3
 SB_ROW_AT_SRC_POS, SB_ROW_AT_DST_POS, SB_ROW_AT_PAIR = 0, 1, 2
 SB_KV_K, SB_KV_V, SB_KV_BOTH = 1, 2, 3
 SB_MAX_INJECT_DESC = 64
+SB_PERMUTE_NOALLOC_SCRATCH_BYTES = 32 << 20
 SB_DESC_CHECK_SRC_IN_DST = 1
 
 _DTYPES = {torch.float32: SB_DTYPE_F32, torch.float16: SB_DTYPE_F16, torch.bfloat16: SB_DTYPE_BF16}
@@ -105,6 +106,11 @@ _SIGNATURES: dict[str, tuple] = {
         ctypes.c_int,
         [_P(SbRows), ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int32, _P(SbInjectParams),
          ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p],
+    ),
+    "sb_permute_paged_noalloc": (
+        ctypes.c_int,
+        [_P(SbRows), ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int32, _P(SbInjectParams),
+         ctypes.c_void_p, ctypes.c_void_p],
     ),
     "sb_search_prepare_rows": (
         ctypes.c_int,

@@ -19,6 +19,7 @@
 // (rope_correction.py:117-129, triton_kernels.py:106-108, :246-260) and are
 // counted in a device error counter.
 #include <algorithm>
+#include <mutex>
 
 #include "common.cuh"
 #include "prof.cuh"
@@ -466,4 +467,65 @@ extern "C" SB_API int sb_permute_paged(const sb_rows *cache, const void *src_pos
   w.dst_row = SB_ROW_AT_DST_POS;
   w.flags = SB_DESC_CHECK_SRC_IN_DST;
   return sb::inject_dispatch(&w, 1, params, err_counter, st);
+}
+
+// ---------------------------------------------------------------------------
+// In-place permutation without any allocation.
+//
+// Some callers cannot allocate device memory at the moment they permute:
+// an inference engine's per-layer hook runs inside the model's forward pass,
+// where the engine has pre-sized its memory pool during start-up profiling
+// (an allocation there eats into the KV-cache budget or fails) or is capturing
+// the step into a CUDA graph; C, Go or Java callers that bind this library
+// directly have no caching allocator to borrow scratch space from.  For them
+// the source-row snapshot lives in this fixed device array instead of a
+// caller-provided workspace.  Every GPU that loads the library holds it until
+// the process exits.
+// ---------------------------------------------------------------------------
+static __device__ __align__(256) unsigned char g_permute_scratch[SB_PERMUTE_NOALLOC_SCRATCH_BYTES];
+
+namespace sb {
+namespace {
+std::mutex g_scratch_mu;
+void *g_scratch_ptr[64] = {};  // device address of g_permute_scratch, per device ordinal
+}  // namespace
+}  // namespace sb
+
+extern "C" SB_API int sb_permute_paged_noalloc(const sb_rows *cache, const void *src_pos, const void *dst_pos,
+                                               int64_t n_pairs, int32_t pos_dtype, const sb_inject_params *params,
+                                               uint64_t *err_counter, void *stream) {
+  if (cache == nullptr || params == nullptr || n_pairs < 0) return SB_ERR_INVALID_ARGUMENT;
+  if (n_pairs == 0) return SB_OK;
+  const int64_t need = sb_permute_workspace_bytes(n_pairs, params->n_layers, params->n_heads, params->head_dim,
+                                                  params->dtype);
+  if (need < 0) return SB_ERR_INVALID_ARGUMENT;
+  if (need > SB_PERMUTE_NOALLOC_SCRATCH_BYTES) return SB_ERR_TOO_LARGE;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) {
+    sb::set_last_cuda_error(e);
+    return SB_ERR_CUDA;
+  }
+  if (dev < 0 || dev >= 64) return SB_ERR_UNSUPPORTED;
+  void *scratch = nullptr;
+  {
+    // First call on this device: resolve the array's device address (the
+    // host-side symbol is only a stand-in and must never reach a kernel).
+    std::lock_guard<std::mutex> lk(sb::g_scratch_mu);
+    if (sb::g_scratch_ptr[dev] == nullptr) {
+      void *p = nullptr;
+      e = cudaGetSymbolAddress(&p, g_permute_scratch);
+      if (e != cudaSuccess || p == nullptr) {
+        sb::set_last_cuda_error(e);
+        return SB_ERR_CUDA;
+      }
+      sb::g_scratch_ptr[dev] = p;
+    }
+    scratch = sb::g_scratch_ptr[dev];
+  }
+  // Rows are snapshotted for every pair before any is read back, and pairs
+  // whose source was out of range are skipped rather than read, so the
+  // scratch needs no clearing between calls.
+  return sb_permute_paged(cache, src_pos, dst_pos, n_pairs, pos_dtype, params, scratch,
+                          SB_PERMUTE_NOALLOC_SCRATCH_BYTES, err_counter, stream);
 }
