@@ -458,6 +458,142 @@ def run_search(args, local: int) -> dict:
 
 
 # ---------------------------------------------------------------------------
+# Component: partial-prefill attention (configs[3], c4)
+# ---------------------------------------------------------------------------
+A_B, A_HQ, A_HKV, A_S, A_D, A_SPANS, A_TAIL, A_FRAC = 4, 28, 4, 32768, 128, 64, 512, 0.10
+
+
+def make_attention_mask(rng: np.random.Generator, S: int) -> np.ndarray:
+    """64 seeded contiguous recompute spans plus the final 512 tokens, 10 % of
+    positions in total."""
+    mask = np.zeros(S, bool)
+    tail = min(A_TAIL, S // 4)
+    mask[S - tail:] = True
+    budget = int(A_FRAC * S) - tail
+    starts = np.sort(rng.choice(S - tail, A_SPANS, replace=False))
+    lens = 1 + rng.multinomial(max(budget - A_SPANS, 0), np.ones(A_SPANS) / A_SPANS)
+    for a, ln in zip(starts, lens):
+        mask[a : min(a + ln, S - tail)] = True
+    return mask
+
+
+def attention_flops(masks: np.ndarray, n_q_heads: int, head_dim: int) -> float:
+    """4 * D * Hq * sum over compute rows of (p + 1): causal, inclusive, no padding."""
+    total = 0.0
+    for m in masks:
+        pos = np.nonzero(m)[0].astype(np.float64)
+        total += float((pos + 1).sum())
+    return 4.0 * head_dim * n_q_heads * total
+
+
+def run_attention(args, local: int) -> dict:
+    from oracle import attention as oatt
+    from semblend_b200 import _lib
+    from semblend_b200 import triton_kernels as tk
+
+    dev = torch.device("cuda", local)
+    B, S = args.attn_batch, args.attn_seq
+    rng = np.random.default_rng(SEED + 5)
+    masks = np.stack([make_attention_mask(rng, S) for _ in range(B)])
+    g = torch.Generator(device=dev).manual_seed(SEED + 5)
+    scale = 1.0 / np.sqrt(A_D)
+    q = (torch.randn(B, A_HQ, S, A_D, generator=g, device=dev) * scale).to(torch.bfloat16)
+    k = (torch.randn(B, A_HKV, S, A_D, generator=g, device=dev) * scale).to(torch.bfloat16)
+    v = (torch.randn(B, A_HKV, S, A_D, generator=g, device=dev) * scale).to(torch.bfloat16)
+    mask_d = torch.from_numpy(masks).to(dev)
+    rows, counts = tk.mask_to_rows(mask_d)
+    out = torch.zeros_like(q)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+
+    def step():
+        tk.gqa_partial_attention(q, k, v, rows, counts, out, max_rows=S, status=status)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    steps = max(5, args.steps // 10)
+    stream = torch.cuda.current_stream(dev)
+    clocks = ClockSampler(local)
+    clocks.start()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with _lib.KernelTimer(steps) as kt:
+        t0.record(stream)
+        for _ in range(steps):
+            step()
+        t1.record(stream)
+        torch.cuda.synchronize(dev)
+    clk = clocks.stop()
+    st = int(status.item())
+    ms = t0.elapsed_time(t1) / steps
+    flops = attention_flops(masks, A_HQ, A_D)
+
+    # end to end through the reference API: the step's compute mask from pinned
+    # host memory in, per-batch row counts and the kernel status out
+    hmask = torch.from_numpy(masks).pin_memory()
+    dmask = torch.empty_like(mask_d)
+    hres = torch.empty(B + 1, dtype=torch.int32).pin_memory()
+
+    def e2e_step():
+        dmask.copy_(hmask, non_blocking=True)
+        o = tk.partial_prefill_attention(q, k, v, dmask)
+        r, c = tk.mask_to_rows(dmask)
+        hres[:B].copy_(c, non_blocking=True)
+        return o
+
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    e2e_ms = e0.elapsed_time(e1) / steps
+
+    # CPU port on a seeded sample of rows of batch element 0 (GQA-expanded),
+    # also used to cross-check the GPU rows
+    pos0 = np.nonzero(masks[0])[0]
+    sample = np.sort(np.random.default_rng(SEED).choice(pos0, min(64, pos0.shape[0]), replace=False))
+    qc, kc, vc = q[0].float().cpu(), k[0].float().cpu(), v[0].float().cpu()
+    kk, vv = oatt.expand_kv_heads(kc, A_HQ), oatt.expand_kv_heads(vc, A_HQ)
+    torch.set_num_threads(os.cpu_count() or 1)
+    c0 = time.perf_counter()
+    want = oatt.partial_prefill_attention_blocked(qc, kk, vv, torch.from_numpy(sample), block=8)
+    cpu_s = time.perf_counter() - c0
+    got = out[0][:, torch.from_numpy(sample).to(dev), :].float().cpu()
+    max_err = float((got - want).abs().max())
+    cpu_flops = 4.0 * A_D * A_HQ * float((sample + 1).sum())
+    pk = peaks()
+    achieved = flops / (kt.mean_ms * 1e-3) / 1e12
+    return {
+        "metric": "partial-prefill attention TFLOP/s",
+        "value": round(flops / (ms * 1e-3) / 1e12, 2),
+        "unit": "TFLOP/s",
+        "ms_per_step": round(ms, 4),
+        "steps": steps,
+        "config": {"workload": f"c4{'' if (B, S) == (A_B, A_S) else ' (reduced)'}: batch {B}, 28 q heads / 4 KV "
+                               f"heads, head_dim 128, bf16, S={S}, compute rows = 64 seeded spans + final 512 "
+                               f"(10%), fp32 softmax", "compute_rows": int(masks.sum()),
+                   "flops_per_step": flops, "status": st},
+        "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+                     "frac": round(achieved / pk["bf16_tflops"], 4), "peak_source": pk["source"],
+                     "kernel": "attn_tc_kernel<bf16> (tcgen05, 4*D*Hq*sum(p+1) flops)",
+                     "kernel_ms": round(kt.mean_ms, 4), "traffic": None},
+        "e2e": {"value": round(flops / (e2e_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
+                "h2d_bytes_per_step": int(hmask.numel()), "d2h_bytes_per_step": 4 * B,
+                "api": "semblend_b200.triton_kernels.partial_prefill_attention"},
+        "gpu_launches": steps,
+        "clocks": clk,
+        "oracle_check": f"max |gpu - fp32 oracle| = {max_err:.2e} over {sample.shape[0]} sampled rows x 28 heads",
+        "cpu_baseline": {"value": round(cpu_flops / cpu_s / 1e12, 6), "unit": "TFLOP/s",
+                         "cores": torch.get_num_threads(), "kind": "port",
+                         "sample": f"{sample.shape[0]} seeded rows of batch element 0 through "
+                                   "oracle.attention (fp32, GQA-expanded); TFLOP/s by the same flop formula"},
+    }
+
+
+# ---------------------------------------------------------------------------
 # CPU baseline (oracle port of the reference's inject) — bounded sample
 # ---------------------------------------------------------------------------
 def cpu_baseline(steps: int = 1) -> dict:
@@ -520,8 +656,10 @@ def main() -> int:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-components", action="store_true", help="skip the search / attention components")
-    ap.add_argument("--only", choices=["all", "search"], default="all",
-                    help="'search': print only the donor-search component line")
+    ap.add_argument("--only", choices=["all", "search", "attention"], default="all",
+                    help="print only that component's line")
+    ap.add_argument("--attn-batch", type=int, default=A_B, help="attention batch (c4: 4)")
+    ap.add_argument("--attn-seq", type=int, default=A_S, help="attention context (c4: 32768)")
     ap.add_argument("--search-rows", type=int, default=S_ROWS, help="donor rows of the search (c3: 1048576)")
     ap.add_argument("--requests", type=int, default=N_REQ, help="requests per step (c2: 8)")
     ap.add_argument("--layers", type=int, default=N_LAYERS, help="layers (c2: 28)")
@@ -535,16 +673,17 @@ def main() -> int:
             print(json.dumps(line), flush=True)
         return 0
     world, rank, local = dist_setup(args.gpus)
-    if args.only == "search":
+    if args.only in ("search", "attention"):
         if rank == 0:
-            print(json.dumps(run_search(args, local)), flush=True)
+            fn = run_search if args.only == "search" else run_attention
+            print(json.dumps(fn(args, local)), flush=True)
         return 0
     line = run_ours(args, world, rank, local)
     if line is not None:
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(steps=3)
         if world == 1 and not args.no_components:
-            line["components"] = {"search": run_search(args, local)}
+            line["components"] = {"search": run_search(args, local), "attention": run_attention(args, local)}
         print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist
