@@ -457,6 +457,59 @@ def run_search(args, local: int) -> dict:
     }
 
 
+def run_search_sharded(args, world: int, rank: int, local: int) -> dict | None:
+    """c3 with the donor rows split across `world` GPUs (strong scaling): each
+    rank searches its shard, NCCL all-gathers the per-shard top-8 and merges."""
+    from semblend_b200 import _lib
+    from semblend_b200.sharded_search import ShardedDonorMatrix
+
+    dev = torch.device("cuda", local)
+    n_rows = args.search_rows
+    emb, queries = make_search_inputs(dev, SEED + 3, n_rows=n_rows)
+    m = ShardedDonorMatrix(n_rows, S_DIM, device=dev)
+    m.write_range(0, emb)
+    del emb
+    torch.cuda.empty_cache()
+    for _ in range(args.warmup):
+        m.search(queries, S_K, S_THR)
+    torch.cuda.synchronize(dev)
+    steps = max(5, args.steps // 10)
+    barrier(world)
+    stream = torch.cuda.current_stream(dev)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with _lib.KernelTimer(steps) as kt:
+        t0.record(stream)
+        for _ in range(steps):
+            ids, sc = m.search(queries, S_K, S_THR)
+        t1.record(stream)
+        torch.cuda.synchronize(dev)
+    barrier(world)
+    ms = max_over_ranks(t0.elapsed_time(t1) / steps, world)
+    kms = max_over_ranks(kt.mean_ms, world)
+    if rank != 0:
+        return None
+    pk = peaks()
+    flops_rank = 2.0 * (m.row_end - m.row_begin) * S_QUERIES * S_DIM
+    return {
+        "metric": "donor search q/s",
+        "value": round(S_QUERIES / (ms * 1e-3), 1),
+        "unit": "q/s",
+        "n_gpus": world,
+        "scaling": "strong",
+        "ms_per_step": round(ms, 4),
+        "steps": steps,
+        "config": {"workload": f"c3: {n_rows:,} x 384 donors split over {world} GPUs, 4096 queries, top-8, "
+                               "threshold 0.60; per-shard exact top-8, NCCL all_gather_into_tensor, k-way merge",
+                   "fill": round(float((ids >= 0).float().mean().item()), 4)},
+        "roofline": {"bound": "tensor", "achieved": round(flops_rank / (kms * 1e-3) / 1e12, 1),
+                     "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+                     "frac": round(flops_rank / (kms * 1e-3) / 1e12 / pk["bf16_tflops"], 4),
+                     "peak_source": pk["source"], "kernel": "screen_kernel<8> per rank (slowest rank)",
+                     "kernel_ms": round(kms, 4)},
+        "gpu_launches": steps * 4,
+    }
+
+
 # ---------------------------------------------------------------------------
 # Component: partial-prefill attention (configs[3], c4)
 # ---------------------------------------------------------------------------
@@ -674,9 +727,19 @@ def main() -> int:
         return 0
     world, rank, local = dist_setup(args.gpus)
     if args.only in ("search", "attention"):
-        if rank == 0:
-            fn = run_search if args.only == "search" else run_attention
-            print(json.dumps(fn(args, local)), flush=True)
+        if args.only == "search" and world > 1:
+            res = run_search_sharded(args, world, rank, local)
+        elif rank == 0:
+            res = run_search(args, local) if args.only == "search" else run_attention(args, local)
+        else:
+            res = None
+        if res is not None:
+            print(json.dumps(res), flush=True)
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.barrier()
+            dist.destroy_process_group()
         return 0
     line = run_ours(args, world, rank, local)
     if line is not None:
@@ -684,6 +747,11 @@ def main() -> int:
             line["cpu_baseline"] = cpu_baseline(steps=3)
         if world == 1 and not args.no_components:
             line["components"] = {"search": run_search(args, local), "attention": run_attention(args, local)}
+    if world > 1 and not args.no_components:
+        comp = run_search_sharded(args, world, rank, local)
+        if line is not None:
+            line["components"] = {"search": comp}
+    if line is not None:
         print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist

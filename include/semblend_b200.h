@@ -288,6 +288,29 @@ SB_API int sb_partial_attention(sb_attn_tensor q, sb_attn_tensor k, sb_attn_tens
                                 int32_t *status, void *stream);
 
 /* ------------------------------------------------------------------------ */
+/* Masked QKV projection                                                    */
+/* ------------------------------------------------------------------------ */
+/* Workspace bytes sb_masked_linear needs (the compacted rows of x; 0 for fp32). */
+SB_API int64_t sb_masked_linear_workspace_bytes(int32_t n_rows, int32_t in_features, int32_t dtype);
+
+/* out[rows[i], :] = x[rows[i], :] @ w^T (+ bias) for i < n_rows, with fp32
+ * accumulation and one rounding to the element type; other rows of out are
+ * not written (zero them first for the reference's output).  x [*, ldx],
+ * w [out_features, ldw], out [*, ldo], bias [out_features] or NULL, all of
+ * `dtype`; rows device int32.  bf16 / fp16 with 16-byte aligned rows
+ * (in_features, ldx, ldw, ldo multiples of 8) run a tcgen05 GEMM over the
+ * compacted rows only; fp32 and other 16-bit shapes run on CUDA cores.
+ * *status (device int32, zeroed by the caller)
+ * receives a value >= 2 if a kernel wait timed out.
+ *
+ * Replaces masked_qkv_projection (semblend_core/triton_kernels.py:451-522;
+ * kernel :366-448), which computes every row and then zeroes the reuse rows. */
+SB_API int sb_masked_linear(const void *x, int64_t ldx, const void *w, int64_t ldw, const void *bias,
+                            const int32_t *rows, int32_t n_rows, int32_t out_features,
+                            int32_t in_features, void *out, int64_t ldo, int32_t dtype,
+                            void *workspace, int64_t workspace_bytes, int32_t *status, void *stream);
+
+/* ------------------------------------------------------------------------ */
 /* Miscellaneous                                                            */
 /* ------------------------------------------------------------------------ */
 SB_API const char *sb_status_string(int status);
@@ -298,7 +321,8 @@ SB_API int sb_last_cuda_error(void);
 
 /* Timing of the dominant kernel of each later call (inject_kernel for
  * sb_inject / sb_permute_paged, the tensor-core screening kernel for
- * sb_cosine_topk, the attention kernel for sb_partial_attention): CUDA events are recorded on the launch stream around each
+ * sb_cosine_topk, the attention kernel for sb_partial_attention, the GEMM for
+ * sb_masked_linear): CUDA events are recorded on the launch stream around each
  * of the next max_launches such launches.  sb_profile_stop synchronises on
  * them, reports the summed milliseconds and the number of launches timed, and
  * turns timing off. */

@@ -74,3 +74,37 @@ def masked_qkv_projection(hidden_states, qkv_weight, compute_mask, qkv_bias=None
         hidden_states.float(), qkv_weight.float(), qkv_bias.float() if qkv_bias is not None else None
     )
     return (projected * compute_mask.unsqueeze(1).float()).to(hidden_states.dtype)
+
+
+def partial_prefill(hidden_states, donor_kv, qkv_weight, output_projection, donor_positions,
+                    target_positions, compute_mask, num_heads, head_dim, qkv_bias=None,
+                    output_bias=None, scale=None):
+    """triton_kernels.py:769-923 on CPU: scatter, masked projection, layer-0
+    merge in fp32, fp32 partial attention, fp32 output projection, reuse rows
+    zeroed, new K/V written into every layer.  Returns ``(output, kv_cache)``."""
+    from .rope import scatter_donor_kv
+
+    S = hidden_states.shape[0]
+    L = donor_kv.shape[0]
+    if scale is None:
+        scale = 1.0 / math.sqrt(head_dim)
+    target = torch.zeros((L, 2, num_heads, S, head_dim), dtype=hidden_states.dtype)
+    target = scatter_donor_kv(target, donor_kv.to(target.dtype), donor_positions, target_positions)
+    qkv = masked_qkv_projection(hidden_states, qkv_weight, compute_mask, qkv_bias)
+    qkv = qkv.float().view(S, 3, num_heads, head_dim)
+    q_new, k_new, v_new = (qkv[:, i].permute(1, 0, 2) for i in range(3))
+    comp = torch.where(compute_mask)[0]
+    merged_k = target[0, 0].float().clone()
+    merged_v = target[0, 1].float().clone()
+    merged_k[:, comp] = k_new[:, comp]
+    merged_v[:, comp] = v_new[:, comp]
+    attn = partial_prefill_attention(q_new.contiguous(), merged_k, merged_v, compute_mask, scale)
+    final = torch.nn.functional.linear(
+        attn.permute(1, 0, 2).reshape(S, num_heads * head_dim), output_projection.float(),
+        output_bias.float() if output_bias is not None else None,
+    ).to(hidden_states.dtype)
+    final[~compute_mask] = 0.0
+    for layer in range(L):
+        target[layer, 0][:, comp] = k_new[:, comp].to(target.dtype)
+        target[layer, 1][:, comp] = v_new[:, comp].to(target.dtype)
+    return final, target

@@ -143,6 +143,13 @@ _SIGNATURES: dict[str, tuple] = {
          ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
          ctypes.c_float, ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p],
     ),
+    "sb_masked_linear_workspace_bytes": (ctypes.c_int64, [ctypes.c_int32, ctypes.c_int32, ctypes.c_int32]),
+    "sb_masked_linear": (
+        ctypes.c_int,
+        [ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p,
+         ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int32,
+         ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p],
+    ),
     "sb_profile_start": (ctypes.c_int, [ctypes.c_int32]),
     "sb_profile_stop": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p]),
     "sb_selftest_wait_timeout": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p]),

@@ -10,6 +10,7 @@ runs a hand-written sm_100a kernel of ``libsemblend_b200``.  CPU tensors raise
 from __future__ import annotations
 
 import math
+from dataclasses import dataclass
 
 import torch
 
@@ -214,8 +215,145 @@ def partial_prefill_attention(
     return output if batched else output[0]
 
 
+def masked_qkv_projection(
+    hidden_states: torch.Tensor,
+    qkv_weight: torch.Tensor,
+    compute_mask: torch.Tensor,
+    qkv_bias: torch.Tensor | None = None,
+    status: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """``hidden_states @ qkv_weight^T (+ qkv_bias)`` at compute-mask rows; reuse rows are zero.
+
+    Mirrors semblend_core/triton_kernels.py:451-522 (fp32 accumulation, one
+    rounding to the input dtype), but multiplies only the compute rows: bf16 /
+    fp16 run a tcgen05 GEMM over the compacted rows (``sb_masked_linear``),
+    fp32 (and 16-bit hidden sizes that are not a multiple of 8) a CUDA-core
+    kernel.  ``status`` (device int32) receives a value >= 2 if a kernel wait
+    timed out.
+    """
+    _lib.require_cuda(hidden_states, "hidden_states")
+    S, K = hidden_states.shape
+    N = qkv_weight.shape[0]
+    if qkv_weight.shape[1] != K:
+        raise ValueError(f"qkv_weight {tuple(qkv_weight.shape)} does not match hidden_states {tuple(hidden_states.shape)}")
+    dt = hidden_states.dtype
+    w = qkv_weight.to(dt).contiguous()
+    b = qkv_bias.to(dt).contiguous() if qkv_bias is not None else None
+    x = hidden_states if hidden_states.stride(1) == 1 else hidden_states.contiguous()
+    out = torch.zeros(S, N, dtype=dt, device=x.device)
+    if S == 0:
+        return out
+    rows, counts = mask_to_rows(compute_mask.reshape(-1)[:S].to(x.device))
+    n = int(counts[0].item())
+    if n == 0:
+        return out
+    lib = _lib.load()
+    code = _lib.dtype_code(dt)
+    ws_bytes = lib.sb_masked_linear_workspace_bytes(n, K, code)
+    ws = torch.empty(max(ws_bytes, 16), dtype=torch.uint8, device=x.device)
+    if status is None:
+        status = torch.zeros(1, dtype=torch.int32, device=x.device)
+    ldx = x.stride(0) if S > 1 else K
+    _lib.check(
+        lib.sb_masked_linear(x.data_ptr(), ldx, w.data_ptr(), K, b.data_ptr() if b is not None else None,
+                             rows.data_ptr(), n, N, K, out.data_ptr(), N, code, ws.data_ptr(), ws_bytes,
+                             status.data_ptr(), _lib.stream_ptr(x.device)),
+        "sb_masked_linear",
+    )
+    return out
+
+
+@dataclass
+class PartialPrefillResult:
+    """Result of :func:`partial_prefill` (semblend_core/triton_kernels.py:742-766)."""
+
+    output: torch.Tensor
+    kv_cache: torch.Tensor
+    positions_computed: int
+    positions_reused: int
+    computation_ratio: float
+    scatter_time_ms: float
+    projection_time_ms: float
+    attention_time_ms: float
+    total_time_ms: float
+
+
+def partial_prefill(
+    hidden_states: torch.Tensor,
+    donor_kv: torch.Tensor,
+    qkv_weight: torch.Tensor,
+    output_projection: torch.Tensor,
+    donor_positions: torch.Tensor,
+    target_positions: torch.Tensor,
+    compute_mask: torch.Tensor,
+    num_heads: int,
+    head_dim: int,
+    qkv_bias: torch.Tensor | None = None,
+    output_bias: torch.Tensor | None = None,
+    scale: float | None = None,
+) -> PartialPrefillResult:
+    """Scatter donor KV, project only the compute rows, attend, project out.
+
+    Mirrors the reference orchestrator (semblend_core/triton_kernels.py:769-923)
+    step for step: a zero target cache ``[L, 2, H, S, D]``, donor rows
+    scattered into it, the masked QKV projection, layer 0's K/V merged with
+    the new rows in fp32, causal attention at the compute rows (fp32), the
+    output projection in fp32 (a plain library GEMM: outside the kernels this
+    package replaces), reuse rows zeroed, and the new K/V written into every
+    layer; CUDA-event timings per stage.
+    """
+    _lib.require_cuda(hidden_states, "hidden_states")
+    seq_len = hidden_states.shape[0]
+    num_layers = donor_kv.shape[0]
+    device = hidden_states.device
+    if scale is None:
+        scale = 1.0 / math.sqrt(head_dim)
+    target_kv = torch.zeros((num_layers, 2, num_heads, seq_len, head_dim), dtype=hidden_states.dtype, device=device)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
+    ev[0].record()
+    scatter_donor_kv(target_kv, donor_kv.to(target_kv.dtype), donor_positions, target_positions)
+    ev[1].record()
+    qkv = masked_qkv_projection(hidden_states, qkv_weight, compute_mask, qkv_bias)
+    qkv = qkv.float().view(seq_len, 3, num_heads, head_dim)
+    q_new = qkv[:, 0].permute(1, 0, 2)
+    k_new = qkv[:, 1].permute(1, 0, 2)
+    v_new = qkv[:, 2].permute(1, 0, 2)
+    ev[2].record()
+    compute_indices = torch.where(compute_mask)[0]
+    merged_k = target_kv[0, 0].float().clone()
+    merged_v = target_kv[0, 1].float().clone()
+    if compute_indices.numel() > 0:
+        merged_k[:, compute_indices, :] = k_new[:, compute_indices, :]
+        merged_v[:, compute_indices, :] = v_new[:, compute_indices, :]
+    attn = partial_prefill_attention(q_new.contiguous(), merged_k, merged_v, compute_mask, scale)
+    ev[3].record()
+    final = torch.nn.functional.linear(
+        attn.permute(1, 0, 2).reshape(seq_len, num_heads * head_dim), output_projection.float(),
+        output_bias.float() if output_bias is not None else None,
+    ).to(hidden_states.dtype)
+    reuse_indices = torch.where(~compute_mask)[0]
+    if reuse_indices.numel() > 0:
+        final[reuse_indices] = 0.0
+    if compute_indices.numel() > 0:
+        for layer in range(num_layers):
+            target_kv[layer, 0, :, compute_indices, :] = k_new[:, compute_indices, :].to(target_kv.dtype)
+            target_kv[layer, 1, :, compute_indices, :] = v_new[:, compute_indices, :].to(target_kv.dtype)
+    ev[4].record()
+    torch.cuda.synchronize(device)
+    n_comp = int(compute_mask.sum().item())
+    return PartialPrefillResult(
+        output=final, kv_cache=target_kv, positions_computed=n_comp, positions_reused=seq_len - n_comp,
+        computation_ratio=n_comp / seq_len if seq_len > 0 else 1.0,
+        scatter_time_ms=ev[0].elapsed_time(ev[1]), projection_time_ms=ev[1].elapsed_time(ev[2]),
+        attention_time_ms=ev[2].elapsed_time(ev[3]), total_time_ms=ev[0].elapsed_time(ev[4]),
+    )
+
+
 __all__ = [
     "HAS_TRITON",
+    "PartialPrefillResult",
+    "masked_qkv_projection",
+    "partial_prefill",
     "gqa_partial_attention",
     "mask_to_rows",
     "partial_prefill_attention",
