@@ -459,37 +459,93 @@ def run_search(args, local: int) -> dict:
 
 def run_search_sharded(args, world: int, rank: int, local: int) -> dict | None:
     """c3 with the donor rows split across `world` GPUs (strong scaling): each
-    rank searches its shard, NCCL all-gathers the per-shard top-8 and merges."""
+    rank searches its shard exactly, one NCCL all_gather_into_tensor exchanges
+    the per-shard top-8 records, every rank merges."""
     from semblend_b200 import _lib
+    from semblend_b200.search import cosine_topk_async
     from semblend_b200.sharded_search import ShardedDonorMatrix
 
     dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
     n_rows = args.search_rows
+    # every rank generates the same matrix and keeps its shard (seeded on the device)
     emb, queries = make_search_inputs(dev, SEED + 3, n_rows=n_rows)
     m = ShardedDonorMatrix(n_rows, S_DIM, device=dev)
     m.write_range(0, emb)
     del emb
     torch.cuda.empty_cache()
+
+    def step(q):
+        return m.search_async(q, S_K, S_THR)
+
     for _ in range(args.warmup):
-        m.search(queries, S_K, S_THR)
+        step(queries)
     torch.cuda.synchronize(dev)
     steps = max(5, args.steps // 10)
-    barrier(world)
     stream = torch.cuda.current_stream(dev)
+    clocks = ClockSampler(local) if rank == 0 else None
+    if clocks:
+        clocks.start()
+    barrier(world)
+    torch.cuda.synchronize(dev)
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with _lib.KernelTimer(steps) as kt:
         t0.record(stream)
         for _ in range(steps):
-            ids, sc = m.search(queries, S_K, S_THR)
+            ids, sc, status = step(queries)
         t1.record(stream)
         torch.cuda.synchronize(dev)
     barrier(world)
+    clk = clocks.stop() if clocks else None
+    st = 0
+    for v in status.reshape(-1).tolist():
+        st |= int(v)
     ms = max_over_ranks(t0.elapsed_time(t1) / steps, world)
     kms = max_over_ranks(kt.mean_ms, world)
+
+    # the shard search alone (no exchange, no merge), for the overhead split
+    lm = m.local
+    lo = (torch.empty(S_QUERIES, S_K, dtype=torch.int64, device=dev),
+          torch.empty(S_QUERIES, S_K, dtype=torch.float32, device=dev))
+    lst = torch.zeros(1, dtype=torch.int32, device=dev)
+    l0, l1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    l0.record(stream)
+    for _ in range(steps):
+        cosine_topk_async(lm.emb, lm.emb16, lm.valid, lm.stats, queries, S_K, S_THR, n_rows=m.n_local,
+                          id_offset=m.row_begin, status=lst, workspace_owner=lm, out=lo)
+    l1.record(stream)
+    torch.cuda.synchronize(dev)
+    local_ms = max_over_ranks(l0.elapsed_time(l1) / steps, world)
+
+    # end to end: pinned host queries in, merged ids + scores out (every rank)
+    hq = queries.cpu().pin_memory()
+    dq = torch.empty_like(queries)
+    hi = torch.empty(S_QUERIES, S_K, dtype=torch.int64).pin_memory()
+    hs = torch.empty(S_QUERIES, S_K, dtype=torch.float32).pin_memory()
+
+    def e2e_step():
+        dq.copy_(hq, non_blocking=True)
+        i, s_, _ = step(dq)
+        hi.copy_(i, non_blocking=True)
+        hs.copy_(s_, non_blocking=True)
+
+    for _ in range(3):
+        e2e_step()
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / steps, world)
+    fill = float((ids >= 0).float().mean().item())
     if rank != 0:
         return None
     pk = peaks()
     flops_rank = 2.0 * (m.row_end - m.row_begin) * S_QUERIES * S_DIM
+    achieved = flops_rank / (kms * 1e-3) / 1e12
     return {
         "metric": "donor search q/s",
         "value": round(S_QUERIES / (ms * 1e-3), 1),
@@ -499,14 +555,19 @@ def run_search_sharded(args, world: int, rank: int, local: int) -> dict | None:
         "ms_per_step": round(ms, 4),
         "steps": steps,
         "config": {"workload": f"c3: {n_rows:,} x 384 donors split over {world} GPUs, 4096 queries, top-8, "
-                               "threshold 0.60; per-shard exact top-8, NCCL all_gather_into_tensor, k-way merge",
-                   "fill": round(float((ids >= 0).float().mean().item()), 4)},
-        "roofline": {"bound": "tensor", "achieved": round(flops_rank / (kms * 1e-3) / 1e12, 1),
-                     "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
-                     "frac": round(flops_rank / (kms * 1e-3) / 1e12 / pk["bf16_tflops"], 4),
-                     "peak_source": pk["source"], "kernel": "screen_kernel<8> per rank (slowest rank)",
-                     "kernel_ms": round(kms, 4)},
-        "gpu_launches": steps * 4,
+                               "threshold 0.60; per-shard exact top-8, one NCCL all_gather_into_tensor of "
+                               "the shard records, k-way merge on every rank",
+                   "fill": round(fill, 4), "status": st,
+                   "shard_search_ms": round(local_ms, 4),
+                   "exchange_and_merge_ms": round(ms - local_ms, 4)},
+        "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": pk["bf16_tflops"],
+                     "unit": "TFLOP/s", "frac": round(achieved / pk["bf16_tflops"], 4),
+                     "peak_source": pk["source"], "kernel": "screen_kernel<8> on the slowest rank's shard",
+                     "kernel_ms": round(kms, 4), "traffic": None},
+        "e2e": {"value": round(S_QUERIES / (e2e_ms * 1e-3), 1), "unit": "q/s",
+                "h2d_bytes_per_step": hq.numel() * 4, "d2h_bytes_per_step": S_QUERIES * S_K * 12},
+        "gpu_launches": steps * (4 if world == 1 else 5),
+        "clocks": clk,
     }
 
 

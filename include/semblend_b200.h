@@ -241,13 +241,16 @@ SB_API int sb_cosine_topk(const float *emb, int64_t ld_emb, const void *emb16, i
                           int32_t capacity, void *workspace, int64_t workspace_bytes,
                           int32_t *status, void *stream);
 
-/* Merge n_lists (<= 16) per-query sorted top-k lists [n_lists][n_queries][k]
- * into one [n_queries][k] by (score desc, id asc); ids < 0 are empty.  Used
- * after an all-gather of per-shard sb_cosine_topk results (no reference
- * counterpart: the reference searches one process's matrix). */
-SB_API int sb_topk_merge(const int64_t *ids, const float *scores, int32_t n_lists,
-                         int32_t n_queries, int32_t k, int64_t *out_ids, float *out_scores,
-                         void *stream);
+/* Merge n_lists (<= 16) per-query sorted top-k lists into one
+ * [n_queries][k] by (score desc, id asc); ids < 0 are empty.  List l is
+ * [n_queries][k] at ids + l * ids_list_stride (elements; >= n_queries * k)
+ * and scores + l * scores_list_stride, so the lists can sit inside the
+ * per-shard records of one all-gather.  Used after an all-gather of
+ * per-shard sb_cosine_topk results (no reference counterpart: the reference
+ * searches one process's matrix). */
+SB_API int sb_topk_merge(const int64_t *ids, int64_t ids_list_stride, const float *scores,
+                         int64_t scores_list_stride, int32_t n_lists, int32_t n_queries, int32_t k,
+                         int64_t *out_ids, float *out_scores, void *stream);
 
 /* ------------------------------------------------------------------------ */
 /* Partial-prefill attention                                                */

@@ -129,8 +129,8 @@ _SIGNATURES: dict[str, tuple] = {
     ),
     "sb_topk_merge": (
         ctypes.c_int,
-        [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_void_p,
-         ctypes.c_void_p, ctypes.c_void_p],
+        [ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int32, ctypes.c_int32,
+         ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p],
     ),
     "sb_mask_to_rows": (
         ctypes.c_int,

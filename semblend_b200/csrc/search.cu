@@ -50,7 +50,7 @@ constexpr int kBK = 64;              // K elements per shared-memory stage (128 
 constexpr int kQBlockBytes = kBM * 128;
 constexpr int kEStageBytes = kBN * 128;
 constexpr int kThreads = 320;        // warp 0 TMA, warp 1 MMA, warps 2-9 epilogue
-constexpr int kTilesPerChunk = 32;   // donor tiles per work unit
+constexpr int kMaxTilesPerChunk = 32;  // donor tiles per work unit (chosen per launch, <= this)
 constexpr int kMaxStages = 6;
 constexpr int kSmemLimit = 232448;
 constexpr long long kWaitCycles = 2000000000LL;  // ~1 s at 1.9 GHz
@@ -63,6 +63,7 @@ struct ScreenParams {
   int64_t n_rows;
   int64_t n_ntiles;
   int64_t n_units;
+  int tiles_per_chunk;
   float thr;
   int cap;
   uint32_t idesc;
@@ -85,10 +86,38 @@ template <> struct Half16<__half> {
   static __device__ __forceinline__ float to(__half x) { return __half2float(x); }
 };
 
+// Bit-pack the row validity of word w (all rows valid when `valid` is null);
+// bits at or past n_rows are cleared.
+__device__ __forceinline__ void valid_bits_word(const uint8_t *__restrict__ valid, int64_t n_rows,
+                                                uint32_t *__restrict__ bits, int64_t w) {
+  uint32_t v = 0;
+  const int64_t j0 = w * 32;
+  if (valid != nullptr && j0 + 32 <= n_rows && (reinterpret_cast<uintptr_t>(valid) % 16) == 0) {
+    const uint4 *p = reinterpret_cast<const uint4 *>(valid + j0);
+    const uint4 a = __ldg(p), b = __ldg(p + 1);
+    const uint32_t wd[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v |= (((wd[i / 4] >> (8 * (i % 4))) & 0xffu) != 0 ? 1u : 0u) << i;
+  } else {
+    for (int i = 0; i < 32; ++i) {
+      const int64_t j = j0 + i;
+      if (j < n_rows && (valid == nullptr || valid[j])) v |= 1u << i;
+    }
+  }
+  bits[w] = v;
+}
+
 template <typename T>
 __global__ void query_prep_kernel(const float *__restrict__ q, int64_t ld_q, int nq, int dim, int dim_pad,
                                   const float *__restrict__ stats, float *__restrict__ qn, T *__restrict__ qb,
-                                  float *__restrict__ delta, int *__restrict__ count, int *__restrict__ lower) {
+                                  float *__restrict__ delta, int *__restrict__ count, int *__restrict__ lower,
+                                  int q_blocks, const uint8_t *__restrict__ valid, int64_t n_rows,
+                                  uint32_t *__restrict__ bits, int64_t n_words) {
+  if ((int)blockIdx.x >= q_blocks) {  // trailing blocks: the row-validity bitmask
+    const int64_t w = (int64_t)(blockIdx.x - q_blocks) * blockDim.x + threadIdx.x;
+    if (w < n_words) valid_bits_word(valid, n_rows, bits, w);
+    return;
+  }
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) / 32;
   const int lane = threadIdx.x % 32;
   if (warp >= nq) return;
@@ -126,20 +155,6 @@ __global__ void query_prep_kernel(const float *__restrict__ q, int64_t ld_q, int
     count[warp] = 0;
     lower[warp] = tc::float_to_ordered(-INFINITY);
   }
-}
-
-// Bit-pack the row validity (all rows valid when `valid` is null); bits at
-// or past n_rows are cleared.
-__global__ void valid_bits_kernel(const uint8_t *__restrict__ valid, int64_t n_rows, uint32_t *__restrict__ bits,
-                                  int64_t n_words) {
-  const int64_t w = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (w >= n_words) return;
-  uint32_t v = 0;
-  for (int i = 0; i < 32; ++i) {
-    const int64_t j = w * 32 + i;
-    if (j < n_rows && (valid == nullptr || valid[j])) v |= 1u << i;
-  }
-  bits[w] = v;
 }
 
 // Descending insertion into a register-resident sorted list.
@@ -207,8 +222,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       for (int64_t u = blockIdx.x; u < P.n_units && ok; u += gridDim.x) {
         const int qt = (int)(u % P.n_qtiles);
-        const int64_t t0 = (u / P.n_qtiles) * kTilesPerChunk;
-        const int64_t t1 = min(t0 + kTilesPerChunk, P.n_ntiles);
+        const int64_t t0 = (u / P.n_qtiles) * P.tiles_per_chunk;
+        const int64_t t1 = min(t0 + P.tiles_per_chunk, P.n_ntiles);
         if (qi > 0 && !tc::mbar_wait(q_empty, (qi - 1) & 1, ab, 2, kWaitCycles)) break;
         tc::mbar_arrive_expect_tx(q_full, P.k_blocks * kQBlockBytes);
         for (int kb = 0; kb < P.k_blocks; ++kb)
@@ -249,8 +264,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t it = 0, qi = 0, ai = 0;
       bool ok = true;
       for (int64_t u = blockIdx.x; u < P.n_units && ok; u += gridDim.x) {
-        const int64_t t0 = (u / P.n_qtiles) * kTilesPerChunk;
-        const int64_t t1 = min(t0 + kTilesPerChunk, P.n_ntiles);
+        const int64_t t0 = (u / P.n_qtiles) * P.tiles_per_chunk;
+        const int64_t t1 = min(t0 + P.tiles_per_chunk, P.n_ntiles);
         if (!tc::mbar_wait(q_full, qi & 1, ab, 3, kWaitCycles)) break;
         tc::fence_after_sync();
         for (int64_t t = t0; t < t1 && ok; ++t) {
@@ -302,8 +317,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool ok = true;
     for (int64_t u = blockIdx.x; u < P.n_units && ok; u += gridDim.x) {
       const int qt = (int)(u % P.n_qtiles);
-      const int64_t t0 = (u / P.n_qtiles) * kTilesPerChunk;
-      const int64_t t1 = min(t0 + kTilesPerChunk, P.n_ntiles);
+      const int64_t t0 = (u / P.n_qtiles) * P.tiles_per_chunk;
+      const int64_t t1 = min(t0 + P.tiles_per_chunk, P.n_ntiles);
       const int q = qt * kBM + row;
       const bool active = q < P.nq;
       const float dq = active ? P.delta[q] : 0.f;
@@ -404,112 +419,196 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) tc::tmem_dealloc(tmem, 512);
 }
 
-// Block-wide argmax over (score desc, id asc) of n entries; returns the
-// winner's position in `pos` (or -1) to every thread.
-__device__ __forceinline__ void block_argmax(const float *sc, const int *sid, int n, float &bs, int &bi, int &bp,
-                                             float *red_s, int *red_i, int *red_p) {
-  const int tid = threadIdx.x, lane = tid % 32, warp = tid / 32, nwarps = blockDim.x / 32;
-  bs = -INFINITY, bi = INT_MAX, bp = -1;
-  for (int i = tid; i < n; i += blockDim.x) {
-    const float s = sc[i];
-    const int id = sid[i];
-    if (s > bs || (s == bs && s > -INFINITY && id < bi)) bs = s, bi = id, bp = i;
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    const float os = __shfl_xor_sync(0xffffffffu, bs, o);
-    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-    const int op = __shfl_xor_sync(0xffffffffu, bp, o);
-    if (os > bs || (os == bs && oi < bi)) bs = os, bi = oi, bp = op;
-  }
-  if (lane == 0) red_s[warp] = bs, red_i[warp] = bi, red_p[warp] = bp;
-  __syncthreads();
-  bs = lane < nwarps ? red_s[lane] : -INFINITY;
-  bi = lane < nwarps ? red_i[lane] : INT_MAX;
-  bp = lane < nwarps ? red_p[lane] : -1;
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    const float os = __shfl_xor_sync(0xffffffffu, bs, o);
-    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-    const int op = __shfl_xor_sync(0xffffffffu, bp, o);
-    if (os > bs || (os == bs && oi < bi)) bs = os, bi = oi, bp = op;
-  }
-  __syncthreads();
+// Per query (one warp each): the exact k-th best screening score A_k over the
+// candidates, exact rescoring (fp64 accumulation of the fp32 vectors) of the
+// candidates with screening score >= A_k - 2 delta, threshold and top-k
+// selection by (score desc, row asc).
+//
+// The kernel is latency-bound (a query rescored ~10-30 rows here), so every
+// stage keeps several loads in flight per lane.  A_k: every lane keeps a
+// sorted register list of the best KT screening scores of its strided share
+// of the candidates (read 8 per lane at a time); k rounds of a warp max over
+// the list heads pop the k best.  Candidates that pass the A_k filter are
+// queued in shared memory and rescored a few rows at a time, each row split
+// over the warp (T 16-byte loads per lane per row, T = ceil(dim / 128)), all
+// loads of those rows in flight together.  The result list is spread over
+// the warp: lane j holds the j-th best (score, row) so far, and an insertion
+// is one ballot plus one shuffle.
+constexpr int kRescoreWarps = 8;
+constexpr int kMaxDim = 512;
+constexpr int kCandPerLane = 8;                 // candidates read per lane and pass
+constexpr int kQueue = 32 * kCandPerLane + 32;  // passing candidates queued per warp
+
+__device__ __forceinline__ bool better(float s, int id, float s2, int id2) {
+  return s > s2 || (s == s2 && id < id2);
 }
 
-// Per query: the exact k-th best screening score A_k over the candidates,
-// exact fp32 rescoring of candidates with screening score >= A_k - 2 delta,
-// threshold and top-k selection by (score desc, row asc).
-__global__ void rescore_kernel(const float *__restrict__ emb, int64_t ld_emb, int dim,
-                               const float *__restrict__ qn, const float *__restrict__ delta,
-                               const int *__restrict__ count, const int2 *__restrict__ cand, int cap, float thr,
-                               int k, int64_t id_offset, int64_t *__restrict__ out_ids,
-                               float *__restrict__ out_scores, int *status) {
-  extern __shared__ float sh[];
-  float *sq = sh;                                  // [dim]
-  float *sa = sq + ((dim + 3) & ~3);               // [cap] screening scores (scratch)
-  float *sc = sa + cap;                            // [cap] exact scores
-  int *sid = reinterpret_cast<int *>(sc + cap);    // [cap]
-  __shared__ float red_s[32];
-  __shared__ int red_i[32];
-  __shared__ int red_p[32];
-  const int q = blockIdx.x;
-  const int tid = threadIdx.x, lane = tid % 32, warp = tid / 32, nwarps = blockDim.x / 32;
+template <int KT, int T>
+__global__ void __launch_bounds__(kRescoreWarps * 32, 4)
+    rescore_kernel(const float *__restrict__ emb, int64_t ld_emb, int dim, const float *__restrict__ qn,
+                   const float *__restrict__ delta, const int *__restrict__ count, const int2 *__restrict__ cand,
+                   int cap, float thr, int k, int nq, int64_t id_offset, int64_t *__restrict__ out_ids,
+                   float *__restrict__ out_scores, int *status) {
+  __shared__ __align__(16) float sq_all[kRescoreWarps][kMaxDim];
+  __shared__ int queue_all[kRescoreWarps][kQueue];
+  const int lane = threadIdx.x % 32, wib = threadIdx.x / 32;
+  const int q = blockIdx.x * kRescoreWarps + wib;
+  if (q >= nq) return;
+  float *qv = sq_all[wib];
+  int *queue = queue_all[wib];
   int n = count[q];
   if (n > cap) {
-    if (tid == 0) atomicOr(status, 1);
+    if (lane == 0) atomicOr(status, 1);
     n = 0;  // results for this query are withheld (reported as overflow)
   }
-  for (int i = tid; i < dim; i += blockDim.x) sq[i] = qn[(int64_t)q * dim + i];
-  for (int i = tid; i < n; i += blockDim.x) {
-    const int2 e = cand[(int64_t)q * cap + i];
-    sid[i] = e.x;
-    sa[i] = __int_as_float(e.y);
-  }
-  __syncthreads();
+  const int2 *cq = cand + (int64_t)q * cap;
+  const int *cq_score = reinterpret_cast<const int *>(cq) + 1;  // .y of each entry
+  for (int d = lane; d < dim; d += 32) qv[d] = qn[(int64_t)q * dim + d];
+
   float keep = -INFINITY;  // screening-score floor for exact rescoring
   if (n > k) {
-    float bs;
-    int bi, bp;
-    for (int r = 0; r < k; ++r) {
-      block_argmax(sa, sid, n, bs, bi, bp, red_s, red_i, red_p);
-      if (tid == 0 && bp >= 0) sa[bp] = -INFINITY;
-      __syncthreads();
-      keep = bs;  // after k rounds: the k-th best screening score
-    }
-    const float dq = delta[q];
-    keep = isfinite(dq) ? keep - 2.f * dq : -INFINITY;
-    // restore the screening scores taken out
-    for (int i = tid; i < n; i += blockDim.x) sa[i] = __int_as_float(cand[(int64_t)q * cap + i].y);
-    __syncthreads();
-  }
-  for (int i = warp; i < n; i += nwarps) {
-    if (sa[i] < keep) {  // NaN screening scores are always rescored
-      if (lane == 0) sc[i] = -INFINITY;
-      continue;
-    }
-    const float *e = emb + (int64_t)sid[i] * ld_emb;
-    double acc = 0.0;
-    for (int d = lane; d < dim; d += 32) acc = fma((double)sq[d], (double)e[d], acc);
+    float tk[KT];
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-    if (lane == 0) {
-      const float s = (float)acc;
-      sc[i] = s >= thr ? s : -INFINITY;
+    for (int i = 0; i < KT; ++i) tk[i] = -INFINITY;
+    for (int base = 0; base < n; base += 32 * kCandPerLane) {
+      float v[kCandPerLane];
+#pragma unroll
+      for (int j = 0; j < kCandPerLane; ++j) {
+        const int i = base + 32 * j + lane;
+        v[j] = i < n ? __int_as_float(__ldcg(cq_score + 2 * (int64_t)i)) : -INFINITY;
+      }
+#pragma unroll
+      for (int j = 0; j < kCandPerLane; ++j)
+        if (v[j] > tk[KT - 1]) topk_insert<KT>(tk, v[j]);  // NaN never enters
     }
+    int popped = INT_MIN;
+    for (int r = 0; r < k; ++r) {
+      const int head = tc::float_to_ordered(tk[0]);
+      popped = __reduce_max_sync(0xffffffffu, head);
+      const uint32_t holders = __ballot_sync(0xffffffffu, head == popped);
+      if (lane == __ffs(holders) - 1) {
+#pragma unroll
+        for (int i = 0; i < KT - 1; ++i) tk[i] = tk[i + 1];
+        tk[KT - 1] = -INFINITY;
+      }
+    }
+    const float ak = tc::ordered_to_float(popped);  // -inf if fewer than k finite scores
+    const float dq = delta[q];
+    keep = isfinite(dq) ? ak - 2.f * dq : -INFINITY;
   }
-  __syncthreads();
-  for (int r = 0; r < k; ++r) {
-    float bs;
-    int bi, bp;
-    block_argmax(sc, sid, n, bs, bi, bp, red_s, red_i, red_p);
-    if (tid == 0) {
-      const bool hit = bs > -INFINITY;
-      out_ids[(int64_t)q * k + r] = hit ? (int64_t)bi + id_offset : -1;
-      out_scores[(int64_t)q * k + r] = hit ? bs : -INFINITY;
-      if (hit) sc[bp] = -INFINITY;
+  __syncwarp();
+
+  // warp-spread result list: lane j < k holds the j-th best so far
+  float ls = -INFINITY;
+  int li = INT_MAX;
+  const bool vec4 = (dim % 4 == 0) && (ld_emb % 4 == 0) && (reinterpret_cast<uintptr_t>(emb) % 16 == 0);
+  const float4 *qv4 = reinterpret_cast<const float4 *>(qv);
+
+  // insert (s, id) (warp-uniform) into the list
+  auto insert = [&](float ns, int ni) {
+    if (!(ns >= thr) || ns == -INFINITY) return;
+    const uint32_t ahead = __ballot_sync(0xffffffffu, lane < k && better(ls, li, ns, ni));
+    const int pos = __popc(ahead);
+    const float us = __shfl_up_sync(0xffffffffu, ls, 1);
+    const int ui = __shfl_up_sync(0xffffffffu, li, 1);
+    if (pos < k) {
+      if (lane > pos) ls = us, li = ui;
+      if (lane == pos) ls = ns, li = ni;
     }
-    __syncthreads();
+  };
+
+  // exact scores of the rows queue[off, off + cnt): the warp splits each row's
+  // dims (16 bytes per lane), ROWS rows with all their loads in flight at once
+  auto flush = [&](int off, int cnt) {
+    constexpr int ROWS = T <= 2 ? 4 : 2;
+    for (int r0 = 0; r0 < cnt; r0 += ROWS) {
+      int id[ROWS];
+      double acc[ROWS];
+      float4 v[ROWS][T];
+#pragma unroll
+      for (int j = 0; j < ROWS; ++j) {
+        id[j] = r0 + j < cnt ? queue[off + r0 + j] : -1;
+        const float *row = emb + (int64_t)max(id[j], 0) * ld_emb;
+#pragma unroll
+        for (int t = 0; t < T; ++t) {
+          const int c = lane + 32 * t;
+          float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (id[j] >= 0 && 4 * c < dim) {
+            if (vec4) {
+              x = __ldg(reinterpret_cast<const float4 *>(row) + c);
+            } else {  // rows not 16-byte aligned: element loads
+              x.x = __ldg(row + 4 * c);
+              if (4 * c + 1 < dim) x.y = __ldg(row + 4 * c + 1);
+              if (4 * c + 2 < dim) x.z = __ldg(row + 4 * c + 2);
+              if (4 * c + 3 < dim) x.w = __ldg(row + 4 * c + 3);
+            }
+          }
+          v[j][t] = x;
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < ROWS; ++j) {
+        double a = 0.0;
+#pragma unroll
+        for (int t = 0; t < T; ++t) {
+          const int c = lane + 32 * t;
+          const float4 w = 4 * c < dim ? qv4[c] : make_float4(0.f, 0.f, 0.f, 0.f);
+          a = fma((double)w.x, (double)v[j][t].x, a);
+          a = fma((double)w.y, (double)v[j][t].y, a);
+          a = fma((double)w.z, (double)v[j][t].z, a);
+          a = fma((double)w.w, (double)v[j][t].w, a);
+        }
+        acc[j] = a;
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+        for (int j = 0; j < ROWS; ++j) acc[j] += __shfl_xor_sync(0xffffffffu, acc[j], o);
+#pragma unroll
+      for (int j = 0; j < ROWS; ++j)
+        if (id[j] >= 0) insert((float)acc[j], id[j]);
+    }
+  };
+
+  int queued = 0;  // warp-uniform, < 32 between passes
+  for (int base = 0;; base += 32 * kCandPerLane) {
+    const bool last = base + 32 * kCandPerLane >= n;
+    if (base < n) {
+      int2 e[kCandPerLane];
+#pragma unroll
+      for (int j = 0; j < kCandPerLane; ++j) {
+        const int i = base + 32 * j + lane;
+        e[j] = i < n ? __ldcg(cq + i) : make_int2(0, 0);
+      }
+#pragma unroll
+      for (int j = 0; j < kCandPerLane; ++j) {
+        const int i = base + 32 * j + lane;
+        const bool pass = i < n && !(__int_as_float(e[j].y) < keep);  // NaN screening scores are always rescored
+        const uint32_t m = __ballot_sync(0xffffffffu, pass);
+        if (pass) queue[queued + __popc(m & ((1u << lane) - 1))] = e[j].x;
+        queued += __popc(m);
+      }
+      __syncwarp();
+    }
+    // full batches now; the remainder after the last pass
+    int off = 0;
+    while (queued - off >= 32 || (last && queued - off > 0)) {
+      const int cnt = min(32, queued - off);
+      flush(off, cnt);
+      off += cnt;
+    }
+    if (last) break;
+    const int rest = queued - off;  // < 32: move to the front
+    const int moved = lane < rest ? queue[off + lane] : 0;
+    __syncwarp();
+    if (lane < rest) queue[lane] = moved;
+    __syncwarp();
+    queued = rest;
+  }
+  if (lane < k) {
+    const bool hit = ls > -INFINITY;
+    out_ids[(int64_t)q * k + lane] = hit ? (int64_t)li + id_offset : -1;
+    out_scores[(int64_t)q * k + lane] = hit ? ls : -INFINITY;
   }
 }
 
@@ -551,34 +650,87 @@ __global__ void prepare_rows_kernel(const float *__restrict__ emb, int64_t ld_em
 }
 
 // Merge n_lists sorted top-k lists per query (shards of a row-partitioned
-// search) into one, by (score desc, id asc).
-__global__ void topk_merge_kernel(const int64_t *__restrict__ ids, const float *__restrict__ scores, int n_lists,
-                                  int nq, int k, int64_t *__restrict__ out_ids, float *__restrict__ out_scores) {
-  const int q = blockIdx.x * blockDim.x + threadIdx.x;
+// search) into one, by (score desc, id asc).  One warp per query: lane l holds
+// list l in registers; k rounds of a warp argmax over the list heads, the
+// winning lane shifts its list.
+constexpr int kMergeWarps = 8;
+
+template <int KT>
+__global__ void __launch_bounds__(kMergeWarps * 32)
+    topk_merge_kernel(const int64_t *__restrict__ ids, int64_t ids_stride, const float *__restrict__ scores,
+                      int64_t scores_stride, int n_lists, int nq, int k, int64_t *__restrict__ out_ids,
+                      float *__restrict__ out_scores) {
+  const int lane = threadIdx.x % 32;
+  const int q = blockIdx.x * kMergeWarps + threadIdx.x / 32;
   if (q >= nq) return;
-  int head[16];
-  for (int l = 0; l < n_lists; ++l) head[l] = 0;
-  for (int r = 0; r < k; ++r) {
-    int best = -1;
-    float bs = -INFINITY;
-    int64_t bi = INT64_MAX;
-    for (int l = 0; l < n_lists; ++l) {
-      if (head[l] >= k) continue;
-      const int64_t off = ((int64_t)l * nq + q) * k + head[l];
-      const int64_t id = ids[off];
-      const float s = scores[off];
-      if (id < 0) continue;
-      if (s > bs || (s == bs && id < bi)) bs = s, bi = id, best = l;
-    }
-    if (best < 0) {
-      out_ids[(int64_t)q * k + r] = -1;
-      out_scores[(int64_t)q * k + r] = -INFINITY;
-    } else {
-      out_ids[(int64_t)q * k + r] = bi;
-      out_scores[(int64_t)q * k + r] = bs;
-      ++head[best];
+  float ls[KT];
+  int64_t li[KT];
+#pragma unroll
+  for (int j = 0; j < KT; ++j) {
+    ls[j] = -INFINITY;
+    li[j] = -1;
+    if (lane < n_lists && j < k) {
+      const int64_t off = (int64_t)q * k + j;
+      li[j] = ids[lane * ids_stride + off];
+      ls[j] = li[j] >= 0 ? scores[lane * scores_stride + off] : -INFINITY;
     }
   }
+  for (int r = 0; r < k; ++r) {
+    float bs = li[0] >= 0 ? ls[0] : -INFINITY;
+    int64_t bi = li[0] >= 0 ? li[0] : INT64_MAX;
+    int bl = lane;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float os = __shfl_xor_sync(0xffffffffu, bs, o);
+      const int64_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      const int ol = __shfl_xor_sync(0xffffffffu, bl, o);
+      if (os > bs || (os == bs && (oi < bi || (oi == bi && ol < bl)))) bs = os, bi = oi, bl = ol;
+    }
+    const bool hit = bi != INT64_MAX;
+    if (lane == bl && hit) {
+#pragma unroll
+      for (int j = 0; j < KT - 1; ++j) ls[j] = ls[j + 1], li[j] = li[j + 1];
+      ls[KT - 1] = -INFINITY, li[KT - 1] = -1;
+    }
+    if (lane == 0) {
+      out_ids[(int64_t)q * k + r] = hit ? bi : -1;
+      out_scores[(int64_t)q * k + r] = hit ? bs : -INFINITY;
+    }
+  }
+}
+
+template <int KT>
+void launch_rescore_kt(int t, unsigned grid, cudaStream_t st, const float *emb, int64_t ld_emb, int dim,
+                       const float *qn, const float *delta, const int *count, const int2 *cand, int cap, float thr,
+                       int k, int nq, int64_t id_offset, int64_t *out_ids, float *out_scores, int *status) {
+  const dim3 block(kRescoreWarps * 32);
+  if (t == 1)
+    rescore_kernel<KT, 1><<<grid, block, 0, st>>>(emb, ld_emb, dim, qn, delta, count, cand, cap, thr, k, nq,
+                                                  id_offset, out_ids, out_scores, status);
+  else if (t == 2)
+    rescore_kernel<KT, 2><<<grid, block, 0, st>>>(emb, ld_emb, dim, qn, delta, count, cand, cap, thr, k, nq,
+                                                  id_offset, out_ids, out_scores, status);
+  else if (t == 3)
+    rescore_kernel<KT, 3><<<grid, block, 0, st>>>(emb, ld_emb, dim, qn, delta, count, cand, cap, thr, k, nq,
+                                                  id_offset, out_ids, out_scores, status);
+  else
+    rescore_kernel<KT, 4><<<grid, block, 0, st>>>(emb, ld_emb, dim, qn, delta, count, cand, cap, thr, k, nq,
+                                                  id_offset, out_ids, out_scores, status);
+}
+
+void launch_rescore(int kt, unsigned grid, cudaStream_t st, const float *emb, int64_t ld_emb, int dim,
+                    const float *qn, const float *delta, const int *count, const int2 *cand, int cap, float thr,
+                    int k, int nq, int64_t id_offset, int64_t *out_ids, float *out_scores, int *status) {
+  const int t = (dim + 127) / 128;  // 16-byte loads per lane per row (dim <= 512)
+  if (kt == 8)
+    launch_rescore_kt<8>(t, grid, st, emb, ld_emb, dim, qn, delta, count, cand, cap, thr, k, nq, id_offset, out_ids,
+                         out_scores, status);
+  else if (kt == 16)
+    launch_rescore_kt<16>(t, grid, st, emb, ld_emb, dim, qn, delta, count, cand, cap, thr, k, nq, id_offset,
+                          out_ids, out_scores, status);
+  else
+    launch_rescore_kt<32>(t, grid, st, emb, ld_emb, dim, qn, delta, count, cand, cap, thr, k, nq, id_offset,
+                          out_ids, out_scores, status);
 }
 
 inline int64_t align256(int64_t x) { return (x + 255) & ~int64_t(255); }
@@ -692,16 +844,16 @@ extern "C" SB_API int sb_cosine_topk(const float *emb, int64_t ld_emb, const voi
   const int64_t n_words = (n_rows + 31) / 32;
   {
     const int threads = 256;
-    const int blocks = (n_queries * 32 + threads - 1) / threads;
+    const int q_blocks = (n_queries * 32 + threads - 1) / threads;
+    const int blocks = q_blocks + (int)((n_words + threads - 1) / threads);
     if (f16)
       query_prep_kernel<__half><<<blocks, threads, 0, st>>>(queries, ld_q, n_queries, dim, dim_pad, stats, w.qn,
                                                             reinterpret_cast<__half *>(w.qb), w.delta, w.count,
-                                                            w.lower);
+                                                            w.lower, q_blocks, valid, n_rows, w.bits, n_words);
     else
-      query_prep_kernel<__nv_bfloat16><<<blocks, threads, 0, st>>>(queries, ld_q, n_queries, dim, dim_pad, stats,
-                                                                   w.qn, reinterpret_cast<__nv_bfloat16 *>(w.qb),
-                                                                   w.delta, w.count, w.lower);
-    valid_bits_kernel<<<(unsigned)((n_words + 255) / 256), 256, 0, st>>>(valid, n_rows, w.bits, n_words);
+      query_prep_kernel<__nv_bfloat16><<<blocks, threads, 0, st>>>(
+          queries, ld_q, n_queries, dim, dim_pad, stats, w.qn, reinterpret_cast<__nv_bfloat16 *>(w.qb), w.delta,
+          w.count, w.lower, q_blocks, valid, n_rows, w.bits, n_words);
     int s = launch_status();
     if (s != SB_OK) return s;
   }
@@ -718,8 +870,20 @@ extern "C" SB_API int sb_cosine_topk(const float *emb, int64_t ld_emb, const voi
   P.n_qtiles = (n_queries + kBM - 1) / kBM;
   P.n_rows = n_rows;
   P.n_ntiles = (n_rows + kBN - 1) / kBN;
-  const int64_t n_chunks = (P.n_ntiles + kTilesPerChunk - 1) / kTilesPerChunk;
-  P.n_units = n_chunks * P.n_qtiles;
+  // Work unit = one query tile x a chunk of donor tiles; the query tiles of a
+  // chunk are consecutive units, so concurrent CTAs share each chunk through
+  // L2.  The chunk length balances the last wave of units across the SMs
+  // (one tile-equivalent charged per unit for its query-tile load).
+  {
+    const int sms = sm_count();
+    int64_t best_cost = INT64_MAX;
+    for (int tpc = kMaxTilesPerChunk; tpc >= 8; tpc /= 2) {
+      const int64_t units = (P.n_ntiles + tpc - 1) / tpc * P.n_qtiles;
+      const int64_t g = std::min<int64_t>(sms, units);
+      const int64_t cost = (units + g - 1) / g * (tpc + 1);
+      if (cost < best_cost) best_cost = cost, P.tiles_per_chunk = tpc, P.n_units = units;
+    }
+  }
   P.thr = min_similarity;
   P.cap = capacity;
   P.idesc = tc::idesc_f16(kBM, kBN, f16 ? 0u : 1u, 0u);
@@ -744,25 +908,33 @@ extern "C" SB_API int sb_cosine_topk(const float *emb, int64_t ld_emb, const voi
     s = launch_screen<32>(tq, te, P, grid, smem, st);
   if (s != SB_OK) return s;
 
-  const int rs_smem = (int)(((dim + 3) & ~3) * 4 + (int64_t)capacity * 12);
-  if (rs_smem > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(rescore_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, rs_smem);
-    if (e != cudaSuccess) {
-      set_last_cuda_error(e);
-      return SB_ERR_CUDA;
-    }
-  }
-  rescore_kernel<<<n_queries, 256, rs_smem, st>>>(emb, ld_emb, dim, w.qn, w.delta, w.count, w.cand, capacity,
-                                                  min_similarity, k, id_offset, out_ids, out_scores, status);
+  const unsigned rs_grid = (unsigned)((n_queries + kRescoreWarps - 1) / kRescoreWarps);
+  const int kt = k <= 8 ? 8 : (k <= 16 ? 16 : 32);
+  launch_rescore(kt, rs_grid, st, emb, ld_emb, dim, w.qn, w.delta, w.count, w.cand, capacity, min_similarity, k,
+                 n_queries, id_offset, out_ids, out_scores, status);
   return launch_status();
 }
 
-extern "C" SB_API int sb_topk_merge(const int64_t *ids, const float *scores, int32_t n_lists, int32_t n_queries,
-                                    int32_t k, int64_t *out_ids, float *out_scores, void *stream) {
+extern "C" SB_API int sb_topk_merge(const int64_t *ids, int64_t ids_list_stride, const float *scores,
+                                    int64_t scores_list_stride, int32_t n_lists, int32_t n_queries, int32_t k,
+                                    int64_t *out_ids, float *out_scores, void *stream) {
   if (n_lists < 1 || n_lists > 16 || n_queries < 0 || k < 1) return SB_ERR_INVALID_ARGUMENT;
+  if (ids_list_stride < (int64_t)n_queries * k || scores_list_stride < (int64_t)n_queries * k)
+    return SB_ERR_INVALID_ARGUMENT;
   if (n_queries == 0) return SB_OK;
   if (!ids || !scores || !out_ids || !out_scores) return SB_ERR_INVALID_ARGUMENT;
-  sb::topk_merge_kernel<<<(n_queries + 127) / 128, 128, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      ids, scores, n_lists, n_queries, k, out_ids, out_scores);
+  if (k > 32) return SB_ERR_INVALID_ARGUMENT;
+  const unsigned grid = (unsigned)((n_queries + sb::kMergeWarps - 1) / sb::kMergeWarps);
+  const dim3 block(sb::kMergeWarps * 32);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (k <= 8)
+    sb::topk_merge_kernel<8><<<grid, block, 0, st>>>(ids, ids_list_stride, scores, scores_list_stride, n_lists,
+                                                     n_queries, k, out_ids, out_scores);
+  else if (k <= 16)
+    sb::topk_merge_kernel<16><<<grid, block, 0, st>>>(ids, ids_list_stride, scores, scores_list_stride, n_lists,
+                                                      n_queries, k, out_ids, out_scores);
+  else
+    sb::topk_merge_kernel<32><<<grid, block, 0, st>>>(ids, ids_list_stride, scores, scores_list_stride, n_lists,
+                                                      n_queries, k, out_ids, out_scores);
   return sb::launch_status();
 }

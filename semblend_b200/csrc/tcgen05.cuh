@@ -1,5 +1,5 @@
 // Blackwell (sm_100a) primitives as inline PTX: mbarriers with bounded waits,
-// TMA tensor loads (no multicast), TMEM allocation, tcgen05.mma (bf16 inputs,
+// TMA tensor loads (each into its own CTA only), TMEM allocation, tcgen05.mma (bf16 inputs,
 // fp32 accumulation in TMEM) and tcgen05.ld.
 //
 // Every wait is bounded by a clock deadline: when it expires the waiter
@@ -70,7 +70,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, const 
 }
 
 // ---------------------------------------------------------------------------
-// TMA (tiled tensor loads into shared memory; no cluster multicast)
+// TMA (tiled tensor loads into this CTA's shared memory only)
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap *map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");

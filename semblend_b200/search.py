@@ -218,15 +218,26 @@ def cosine_topk(emb: torch.Tensor, emb16: torch.Tensor, valid: torch.Tensor | No
 
 def merge_topk(ids: torch.Tensor, scores: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
     """Merge per-shard sorted lists ``[n_lists, Q, k]`` into ``[Q, k]`` by
-    (score desc, id asc) with ``sb_topk_merge``."""
+    (score desc, id asc) with ``sb_topk_merge``.  Each list must be contiguous
+    (``[Q, k]`` row-major); the lists themselves may be strided (views into
+    all-gathered shard records are read in place)."""
     _lib.require_cuda(ids, "ids")
     n_lists, nq, k = ids.shape
-    ids_c, scores_c = ids.contiguous(), scores.to(torch.float32).contiguous()
+    if scores.dtype != torch.float32:
+        scores = scores.to(torch.float32)
+    if ids.dtype != torch.int64:
+        ids = ids.to(torch.int64)
+
+    def lists(t):
+        return t if t.stride(2) == 1 and t.stride(1) == k else t.contiguous()
+
+    ids_c, scores_c = lists(ids), lists(scores)
     out_i = torch.empty(nq, k, dtype=torch.int64, device=ids.device)
     out_s = torch.empty(nq, k, dtype=torch.float32, device=ids.device)
     lib = _lib.load()
     _lib.check(
-        lib.sb_topk_merge(ids_c.data_ptr(), scores_c.data_ptr(), n_lists, nq, k,
+        lib.sb_topk_merge(ids_c.data_ptr(), ids_c.stride(0) if n_lists > 1 else nq * k, scores_c.data_ptr(),
+                          scores_c.stride(0) if n_lists > 1 else nq * k, n_lists, nq, k,
                           out_i.data_ptr(), out_s.data_ptr(), _lib.stream_ptr(ids.device)),
         "sb_topk_merge",
     )

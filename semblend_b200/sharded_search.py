@@ -3,9 +3,9 @@
 Each rank holds a contiguous slice of the donor rows in its own
 :class:`~semblend_b200.search.DeviceDonorMatrix` and searches it exactly
 (global row ids = local row + the shard's first row); one
-``all_gather_into_tensor`` of the per-shard ``[Q, k]`` ids and similarities
-(NCCL over NVLink on GPUs) and a k-way merge by (similarity desc, row asc)
-give every rank the global top-k.  The merged result equals a single-device
+``all_gather_into_tensor`` of a byte record per shard holding its ``[Q, k]``
+ids, similarities and kernel status (NCCL over NVLink on GPUs) and a k-way
+merge by (similarity desc, row asc) give every rank the global top-k.  The merged result equals a single-device
 search over all rows.  The reference searches one process's matrix
 (semblend_core/donor_store.py:323-341); this is the multi-GPU form of that
 stage.
@@ -18,7 +18,8 @@ from collections.abc import Callable
 import torch
 import torch.distributed as dist
 
-from .search import DEFAULT_CAPACITY, DeviceDonorMatrix, cosine_topk, merge_topk
+from ._lib import NativeLibraryError
+from .search import DEFAULT_CAPACITY, DeviceDonorMatrix, cosine_topk_async, merge_topk
 
 
 def shard_bounds(n_rows: int, world: int) -> list[tuple[int, int]]:
@@ -60,23 +61,77 @@ class ShardedDonorMatrix:
         if a < b and self.local is not None:
             self.local.write_range(a - self.row_begin, values[a - begin : b - begin])
 
-    def search(self, queries: torch.Tensor, k: int, min_similarity: float,
-               capacity: int = DEFAULT_CAPACITY) -> tuple[torch.Tensor, torch.Tensor]:
-        """Global top-``k`` (ids, similarities) ``[Q, k]``, identical on every rank."""
+    def _record_bytes(self, nq: int, k: int) -> int:
+        # per-rank record: ids int64 [Q, k] | scores fp32 [Q, k] | status int32, padded to 16 bytes
+        return (12 * nq * k + 4 + 15) // 16 * 16
+
+    def search_async(self, queries: torch.Tensor, k: int, min_similarity: float,
+                     capacity: int = DEFAULT_CAPACITY) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+        """Global top-``k`` without a host synchronisation: ``(ids, scores, status [W])``.
+
+        Each rank writes its shard's ids, similarities and kernel status into
+        one byte record; a single ``all_gather_into_tensor`` exchanges the
+        records, so every rank holds every shard's status and makes the same
+        retry decision (keeping the ranks' collectives in step).
+        """
+        nq, kk = queries.shape[0], int(k)
+        qk = nq * kk
+        rec = self._record_bytes(nq, kk)
+        dev = queries.device if self._local_search is not None else self.local.device
+        if self.world == 1:
+            send = torch.empty(rec, dtype=torch.uint8, device=dev)
+        else:
+            # exchange buffers are reused across calls: the collective is stream-ordered
+            # before the next call's writes, and the merged results are fresh tensors
+            key = (nq, kk, str(dev))
+            if getattr(self, "_bufs_key", None) != key:
+                self._bufs = (torch.empty(rec, dtype=torch.uint8, device=dev),
+                              torch.empty(self.world * rec, dtype=torch.uint8, device=dev))
+                self._bufs_key = key
+            send, recv = self._bufs
+        ids_v = send[: 8 * qk].view(torch.int64).view(nq, kk)
+        sc_v = send[8 * qk : 12 * qk].view(torch.float32).view(nq, kk)
+        st_v = send[12 * qk : 12 * qk + 4].view(torch.int32)
         if self._local_search is not None:
-            ids, scores = self._local_search(queries, k, min_similarity, self.row_begin)
+            ids, scores = self._local_search(queries, kk, min_similarity, self.row_begin)
+            ids_v.copy_(ids)
+            sc_v.copy_(scores)
+            st_v.zero_()
         else:
             m = self.local
             q = queries.to(device=m.device, dtype=torch.float32).contiguous()
-            ids, scores = cosine_topk(m.emb, m.emb16, m.valid, m.stats, q, k, min_similarity,
-                                      n_rows=self.n_local, id_offset=self.row_begin, capacity=capacity,
-                                      status=m._status, workspace_owner=m)
+            cosine_topk_async(m.emb, m.emb16, m.valid, m.stats, q, kk, min_similarity, n_rows=self.n_local,
+                              id_offset=self.row_begin, capacity=capacity, status=st_v, workspace_owner=m,
+                              out=(ids_v, sc_v))
         if self.world == 1:
+            return ids_v, sc_v, st_v
+        dist.all_gather_into_tensor(recv, send, group=self.group)
+        table = recv.view(self.world, rec)
+        all_ids = table[:, : 8 * qk].view(torch.int64).view(self.world, nq, kk)
+        all_sc = table[:, 8 * qk : 12 * qk].view(torch.float32).view(self.world, nq, kk)
+        status = table[:, 12 * qk : 12 * qk + 4].view(torch.int32).reshape(self.world)
+        ids, scores = self._merge(all_ids, all_sc)
+        return ids, scores, status
+
+    def search(self, queries: torch.Tensor, k: int, min_similarity: float,
+               capacity: int = DEFAULT_CAPACITY) -> tuple[torch.Tensor, torch.Tensor]:
+        """Global top-``k`` (ids, similarities) ``[Q, k]``, identical on every rank.
+
+        Reads every shard's status: retries all ranks together with a 4x
+        larger candidate capacity if any shard overflowed it, raises if a
+        kernel wait timed out on any shard.
+        """
+        cap = max(int(capacity), int(k))
+        while True:
+            ids, scores, status = self.search_async(queries, k, min_similarity, capacity=cap)
+            st = 0
+            for v in status.reshape(-1).tolist():
+                st |= int(v)
+            if st & ~1:
+                raise NativeLibraryError(f"sharded search: kernel wait timed out (code {st})")
+            if st & 1 and cap < 16384:
+                cap = min(cap * 4, 16384)
+                continue
+            if st & 1:
+                raise NativeLibraryError("sharded search: more than 16384 screening candidates for a query")
             return ids, scores
-        nq, kk = ids.shape
-        # dim-0 concatenation [W * Q, k] (the form every backend accepts), viewed as [W, Q, k]
-        all_ids = torch.empty((self.world * nq, kk), dtype=ids.dtype, device=ids.device)
-        all_sc = torch.empty((self.world * nq, kk), dtype=scores.dtype, device=scores.device)
-        dist.all_gather_into_tensor(all_ids, ids.contiguous(), group=self.group)
-        dist.all_gather_into_tensor(all_sc, scores.contiguous(), group=self.group)
-        return self._merge(all_ids.view(self.world, nq, kk), all_sc.view(self.world, nq, kk))

@@ -207,3 +207,42 @@ def test_fp16_overflow_rows_stay_exact():
     ids, s = m.search(Q, 4, -1e9)
     assert_topk_equivalent(E, np.ones(3000, bool), Q, -1e9, ids.cpu().numpy(), s.cpu().numpy(), 4)
     assert ids[0, 0].item() == 17
+
+
+def _merge_reference(ids, scores):
+    """k-way merge by (score desc, id asc) of [L, Q, k] lists, -1 ids empty."""
+    L, Q, k = ids.shape
+    out_i = torch.full((Q, k), -1, dtype=torch.int64)
+    out_s = torch.full((Q, k), -float("inf"))
+    for q in range(Q):
+        ent = [(float(scores[l, q, j]), int(ids[l, q, j])) for l in range(L) for j in range(k) if ids[l, q, j] >= 0]
+        ent.sort(key=lambda e: (-e[0], e[1]))
+        for r, (s, i) in enumerate(ent[:k]):
+            out_i[q, r], out_s[q, r] = i, s
+    return out_i, out_s
+
+
+@pytest.mark.parametrize("n_lists,k", [(1, 8), (5, 8), (16, 3), (3, 16), (2, 32)])
+def test_merge_strided_lists_with_ties_and_empties(n_lists, k):
+    g = torch.Generator().manual_seed(n_lists * 100 + k)
+    Q = 300
+    ids = torch.full((n_lists, Q, k), -1, dtype=torch.int64)
+    sc = torch.full((n_lists, Q, k), -float("inf"))
+    for l in range(n_lists):
+        for q in range(Q):
+            n = int(torch.randint(0, k + 1, (1,), generator=g))
+            s = torch.randint(0, 6, (n,), generator=g).float() / 8  # many ties across lists
+            i = torch.randperm(100000, generator=g)[:n] * n_lists + l  # ids unique across lists
+            order = sorted(range(n), key=lambda j: (-float(s[j]), int(i[j])))
+            ids[l, q, :n] = i[order]
+            sc[l, q, :n] = s[order]
+    want_i, want_s = _merge_reference(ids, sc)
+    # lists as strided views into larger per-list records (as after an all-gather)
+    rec_i = torch.zeros(n_lists, Q * k + 40, dtype=torch.int64)
+    rec_s = torch.zeros(n_lists, Q * k + 24)
+    rec_i[:, : Q * k] = ids.reshape(n_lists, -1)
+    rec_s[:, : Q * k] = sc.reshape(n_lists, -1)
+    di, ds_ = rec_i.to(DEV), rec_s.to(DEV)
+    got_i, got_s = merge_topk(di[:, : Q * k].view(n_lists, Q, k), ds_[:, : Q * k].view(n_lists, Q, k))
+    assert torch.equal(got_i.cpu(), want_i)
+    assert torch.equal(got_s.cpu(), want_s)
