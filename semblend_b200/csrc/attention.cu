@@ -23,6 +23,7 @@
 // CUDA-core path: any head_dim <= 256 and fp32 (the reference's own dtype in
 // its tests), one CTA per (row, head), fp32 online softmax with expf.
 #include <algorithm>
+#include <cmath>
 
 #include "common.cuh"
 #include "prof.cuh"
@@ -35,14 +36,38 @@ namespace {
 constexpr int kBM = 128;
 constexpr int kBN = 128;
 constexpr int kD = 128;
-constexpr int kThreads = 192;
-constexpr int kStages = 3;
+// One pair of exponentials in every SB_ATTN_POLY_EVERY is evaluated as a
+// polynomial on the FMA pipe instead of MUFU (0: all on MUFU).
+#ifndef SB_ATTN_POLY_EVERY
+#define SB_ATTN_POLY_EVERY 0
+#endif
+constexpr int kPolyEvery = SB_ATTN_POLY_EVERY;
+// S columns read from TMEM per wait when turning S into P (32 or 64).
+#ifndef SB_ATTN_PCHUNK
+#define SB_ATTN_PCHUNK 32
+#endif
+constexpr int kPChunk = SB_ATTN_PCHUNK;
+// Packed fp32x2 arithmetic for the scale-subtract and the row sum.
+#ifndef SB_ATTN_PACKED
+#define SB_ATTN_PACKED 1
+#endif
+constexpr int kThreads = 320;  // warp 0 TMA, warp 1 MMA, warps 2-5 softmax of tile 0, warps 6-9 of tile 1
+constexpr int kStages = 2;     // K and V rings
 constexpr int kTileBytes = 128 * 128 * 2;  // one [128 x 128] 16-bit operand tile (two 64-column boxes)
 constexpr int kHalfTile = kTileBytes / 2;
-constexpr int kSmemBytes = 1024 + kTileBytes * (1 + 2 * kStages) + 256;
+constexpr int kSmemBytes = 1024 + kTileBytes * (2 + 2 * kStages) + 256;
 constexpr long long kWaitCycles = 2000000000LL;
-constexpr uint32_t kTmemS = 0;    // two S / P buffers: columns [0, 128) and [128, 256)
-constexpr uint32_t kTmemO = 256;  // O accumulator: columns [256, 384)
+// TMEM columns: tile t has S (P packed over its first half) at [256 t, 256 t + 128)
+// and its O accumulator at [256 t + 128, 256 t + 256).
+__host__ __device__ constexpr uint32_t tmem_s(int t) { return 256u * t; }
+__host__ __device__ constexpr uint32_t tmem_o(int t) { return 256u * t + 128u; }
+
+#if SB_ATTN_TRACE
+__device__ long long g_trace[16 * 512];
+#define SB_TRACE(slot, idx) do { if (blockIdx.x == 0 && (idx) < 512) g_trace[(slot) * 512 + (idx)] = clock64(); } while (0)
+#else
+#define SB_TRACE(slot, idx) do { } while (0)
+#endif
 
 struct AttnParams {
   const void *q;
@@ -52,30 +77,34 @@ struct AttnParams {
   const int32_t *rows;
   int64_t rows_sb;
   const int32_t *counts;
-  int B, Hq, Hkv, S, G, Pt, T_max;
+  int B, Hq, Hkv, S, G, Pt, T_max;  // T_max: row-tile pairs of the longest batch element
   int64_t n_units;
   float scale_log2;
   int *status;
 };
 
+// A work unit is two consecutive row tiles of one (batch element, KV group).
 struct Unit {
-  int b, g, t, r0, n_rows;
-  int pos_max;
-  int nblk;
+  int b, g, r0;
+  int n_rows[2];
+  int nblk[2];
 };
 
 __device__ __forceinline__ bool decode_unit(const AttnParams &P, int64_t u, Unit &w) {
   const int64_t bg_all = (int64_t)P.B * P.Hkv;
-  w.t = P.T_max - 1 - (int)(u / bg_all);
+  const int tp = P.T_max - 1 - (int)(u / bg_all);  // longest units first
   const int bg = (int)(u % bg_all);
   w.b = bg / P.Hkv;
   w.g = bg % P.Hkv;
-  w.r0 = w.t * P.Pt;
+  w.r0 = tp * 2 * P.Pt;
   const int cnt = P.counts[w.b];
   if (w.r0 >= cnt) return false;
-  w.n_rows = min(P.Pt, cnt - w.r0);
-  w.pos_max = P.rows[(int64_t)w.b * P.rows_sb + w.r0 + w.n_rows - 1];
-  w.nblk = w.pos_max / kBN + 1;
+#pragma unroll
+  for (int t = 0; t < 2; ++t) {
+    const int first = w.r0 + t * P.Pt;
+    w.n_rows[t] = max(0, min(P.Pt, cnt - first));
+    w.nblk[t] = w.n_rows[t] > 0 ? P.rows[(int64_t)w.b * P.rows_sb + first + w.n_rows[t] - 1] / kBN + 1 : 0;
+  }
   return true;
 }
 
@@ -93,42 +122,52 @@ template <> struct Pack2<__half> {
   }
 };
 
+// Two query tiles per CTA, processed in ping-pong: while the softmax warps of
+// one tile turn its S block into P, the tensor cores run the other tile's
+// P.V and next Q.K^T.  PV_t(j) is issued before S_t(j + 1), so the barrier
+// that signals S_t(j + 1) also certifies that O_t holds blocks <= j.
+// Registers are split per SM sub-partition: with 10 warps, three share one
+// quarter of the register file, so a thread has at most 168.  The softmax
+// therefore reads each S block from TMEM twice (row max, then P) instead of
+// holding all 128 scores in registers.
 template <typename T>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
                    const AttnParams P) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t *sQ = smem;
-  uint8_t *sK = sQ + kTileBytes;               // [kStages]
+  uint8_t *sQ = smem;                          // [2] query tiles
+  uint8_t *sK = sQ + 2 * kTileBytes;           // [kStages]
   uint8_t *sV = sK + kStages * kTileBytes;     // [kStages]
   uint64_t *bars = reinterpret_cast<uint64_t *>(sV + kStages * kTileBytes);
-  uint64_t *k_full = bars;                     // [3]
-  uint64_t *v_full = bars + 3;                 // [3]
-  uint64_t *kv_empty = bars + 6;               // [3]
-  uint64_t *q_full = bars + 9;
+  uint64_t *k_full = bars;                     // [kStages]
+  uint64_t *k_empty = bars + 2;                // [kStages]
+  uint64_t *v_full = bars + 4;                 // [kStages]
+  uint64_t *v_empty = bars + 6;                // [kStages]
+  uint64_t *q_full = bars + 8;                 // [2]
   uint64_t *q_empty = bars + 10;
   uint64_t *s_full = bars + 11;                // [2]
   uint64_t *p_full = bars + 13;                // [2]
-  uint64_t *pv_done = bars + 15;
-  uint64_t *final_bar = bars + 16;
-  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 17);
-  volatile int *abort_flag = reinterpret_cast<volatile int *>(bars + 18);
+  uint64_t *o_final = bars + 15;               // [2]
+  uint64_t *final_bar = bars + 17;
+  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 18);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(bars + 19);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
       tc::mbar_init(&k_full[s], 1);
+      tc::mbar_init(&k_empty[s], 1);
       tc::mbar_init(&v_full[s], 1);
-      tc::mbar_init(&kv_empty[s], 1);
+      tc::mbar_init(&v_empty[s], 1);
     }
-    tc::mbar_init(q_full, 4);
+    for (int t = 0; t < 2; ++t) {
+      tc::mbar_init(&q_full[t], 4);
+      tc::mbar_init(&s_full[t], 1);
+      tc::mbar_init(&p_full[t], 4);
+      tc::mbar_init(&o_final[t], 1);
+    }
     tc::mbar_init(q_empty, 1);
-    tc::mbar_init(&s_full[0], 1);
-    tc::mbar_init(&s_full[1], 1);
-    tc::mbar_init(&p_full[0], 4);
-    tc::mbar_init(&p_full[1], 4);
-    tc::mbar_init(pv_done, 1);
     tc::mbar_init(final_bar, 1);
     *abort_flag = 0;
     tc::fence_mbar_init();
@@ -155,23 +194,30 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int64_t u = blockIdx.x; u < P.n_units && ok; u += gridDim.x) {
         Unit w;
         if (!decode_unit(P, u, w)) continue;
-        for (int j = 0; j < w.nblk; ++j) {
+        const int nb = max(w.nblk[0], w.nblk[1]);
+        for (int j = 0; j < nb; ++j) {
           const uint32_t st = gl % kStages, ph = (gl / kStages) & 1;
-          if (!tc::mbar_wait(&kv_empty[st], ph ^ 1, ab, 2, kWaitCycles)) {
+          if (!tc::mbar_wait(&k_empty[st], ph ^ 1, ab, 2, kWaitCycles)) {
             ok = false;
             break;
           }
           uint8_t *k_dst = sK + st * kTileBytes;
-          uint8_t *v_dst = sV + st * kTileBytes;
           tc::mbar_arrive_expect_tx(&k_full[st], kTileBytes);
           tc::tma_load_4d(k_dst, &tmK, &k_full[st], 0, j * kBN, w.g, w.b);
           tc::tma_load_4d(k_dst + kHalfTile, &tmK, &k_full[st], 64, j * kBN, w.g, w.b);
+          if (!tc::mbar_wait(&v_empty[st], ph ^ 1, ab, 2, kWaitCycles)) {
+            ok = false;
+            ++gl;  // K of this block is in flight: drain it below
+            break;
+          }
+          uint8_t *v_dst = sV + st * kTileBytes;
           tc::mbar_arrive_expect_tx(&v_full[st], kTileBytes);
           tc::tma_load_4d(v_dst, &tmV, &v_full[st], 0, j * kBN, w.g, w.b);
           tc::tma_load_4d(v_dst + kHalfTile, &tmV, &v_full[st], 64, j * kBN, w.g, w.b);
           ++gl;
         }
       }
+      // every load this thread issued lands before the CTA can exit
       const uint32_t n_out = gl < (uint32_t)kStages ? gl : (uint32_t)kStages;
       for (uint32_t i = gl - n_out; i < gl; ++i) {
         tc::mbar_wait(&k_full[i % kStages], (i / kStages) & 1, drain, 0, kWaitCycles);
@@ -184,202 +230,313 @@ __global__ void __launch_bounds__(kThreads, 1)
       constexpr uint32_t fmt = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
       constexpr uint32_t idesc_qk = tc::idesc_f16(kBM, kBN, fmt, 0);
       constexpr uint32_t idesc_pv = tc::idesc_f16(kBM, kD, fmt, 1);
-      uint32_t gl = 0, gb = 0, qi = 0;
+      uint32_t gl = 0, qi = 0;
+      uint32_t pc[2] = {0, 0};  // P blocks consumed per tile
       bool ok = true;
-      auto issue_pv = [&](uint32_t st, uint32_t glx, uint32_t gbx, bool first) -> bool {
-        if (!tc::mbar_wait(&p_full[gbx & 1], (gbx >> 1) & 1, ab, 3, kWaitCycles)) return false;
-        if (!tc::mbar_wait(&v_full[st], (glx / kStages) & 1, ab, 3, kWaitCycles)) return false;
-        tc::fence_after_sync();
-        const uint32_t p_tmem = tmem + kTmemS + (gbx & 1) * kBN;
+      auto issue_s = [&](int t, uint32_t st) {
+        const uint32_t s_tmem = tmem + tmem_s(t);
 #pragma unroll
-        for (int kk = 0; kk < kBN / 16; ++kk) {
-          const uint64_t dv = tc::desc_mnmajor_sw128(sV + st * kTileBytes, kk * 2048, kHalfTile);
-          tc::mma_bf16_ts(tmem + kTmemO, p_tmem + kk * 8, dv, idesc_pv, (first && kk == 0) ? 0u : 1u);
-        }
-        tc::mma_commit(&kv_empty[st]);
-        tc::mma_commit(pv_done);
-        return true;
+        for (int kb = 0; kb < 2; ++kb)
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            const uint64_t dq = tc::desc_kmajor_sw128(sQ + t * kTileBytes + kb * kHalfTile, kk * 32);
+            const uint64_t dk = tc::desc_kmajor_sw128(sK + st * kTileBytes + kb * kHalfTile, kk * 32);
+            tc::mma_bf16_ss(s_tmem, dq, dk, idesc_qk, (kb | kk) != 0);
+          }
+        tc::mma_commit(&s_full[t]);
       };
       for (int64_t u = blockIdx.x; u < P.n_units && ok; u += gridDim.x) {
         Unit w;
         if (!decode_unit(P, u, w)) continue;
-        if (!tc::mbar_wait(q_full, qi & 1, ab, 3, kWaitCycles)) break;
+        const int nb = max(w.nblk[0], w.nblk[1]);
+        if (!tc::mbar_wait(&q_full[0], qi & 1, ab, 3, kWaitCycles) ||
+            !tc::mbar_wait(&q_full[1], qi & 1, ab, 3, kWaitCycles))
+          break;
         tc::fence_after_sync();
-        uint32_t prev_st = 0, prev_gl = 0, prev_gb = 0;
-        for (int j = 0; j < w.nblk && ok; ++j) {
+        // S of block 0 for both tiles
+        {
           const uint32_t st = gl % kStages;
-          if (!tc::mbar_wait(&k_full[st], (gl / kStages) & 1, ab, 3, kWaitCycles)) {
-            ok = false;
-            break;
-          }
+          if (!tc::mbar_wait(&k_full[st], (gl / kStages) & 1, ab, 3, kWaitCycles)) break;
           tc::fence_after_sync();
-          const uint32_t s_tmem = tmem + kTmemS + (gb & 1) * kBN;
-#pragma unroll
-          for (int kb = 0; kb < 2; ++kb)
-#pragma unroll
-            for (int kk = 0; kk < 4; ++kk) {
-              const uint64_t dq = tc::desc_kmajor_sw128(sQ + kb * kHalfTile, kk * 32);
-              const uint64_t dk = tc::desc_kmajor_sw128(sK + st * kTileBytes + kb * kHalfTile, kk * 32);
-              tc::mma_bf16_ss(s_tmem, dq, dk, idesc_qk, (kb | kk) != 0);
+          for (int t = 0; t < 2; ++t)
+            if (w.nblk[t] > 0) issue_s(t, st);
+          tc::mma_commit(&k_empty[st]);
+        }
+        for (int j = 0; j < nb && ok; ++j) {
+          const uint32_t st = (gl + j) % kStages, ph = ((gl + j) / kStages) & 1;
+          const uint32_t st1 = (gl + j + 1) % kStages, ph1 = ((gl + j + 1) / kStages) & 1;
+          bool v_ready = false, k_ready = false;
+          for (int t = 0; t < 2 && ok; ++t) {
+            if (j >= w.nblk[t]) continue;
+            if (!tc::mbar_wait(&p_full[t], pc[t] & 1, ab, 3, kWaitCycles)) {
+              ok = false;
+              break;
             }
-          tc::mma_commit(&s_full[gb & 1]);
-          if (j > 0 && !issue_pv(prev_st, prev_gl, prev_gb, j == 1)) {
-            ok = false;
-            break;
+            SB_TRACE(t, pc[t]);
+            ++pc[t];
+            if (!v_ready) {
+              if (!tc::mbar_wait(&v_full[st], ph, ab, 3, kWaitCycles)) {
+                ok = false;
+                break;
+              }
+              v_ready = true;
+            }
+            tc::fence_after_sync();
+            const uint32_t p_tmem = tmem + tmem_s(t);
+#pragma unroll
+            for (int kk = 0; kk < kBN / 16; ++kk) {
+              const uint64_t dv = tc::desc_mnmajor_sw128(sV + st * kTileBytes, kk * 2048, kHalfTile);
+              tc::mma_bf16_ts(tmem + tmem_o(t), p_tmem + kk * 8, dv, idesc_pv, (j == 0 && kk == 0) ? 0u : 1u);
+            }
+            if (j == w.nblk[t] - 1) tc::mma_commit(&o_final[t]);
+            if (j + 1 < w.nblk[t]) {
+              if (!k_ready) {
+                if (!tc::mbar_wait(&k_full[st1], ph1, ab, 3, kWaitCycles)) {
+                  ok = false;
+                  break;
+                }
+                tc::fence_after_sync();
+                k_ready = true;
+              }
+              issue_s(t, st1);
+            }
           }
-          prev_st = st, prev_gl = gl, prev_gb = gb;
-          ++gl, ++gb;
+          if (!ok) break;
+          tc::mma_commit(&v_empty[st]);
+          if (j + 1 < nb) tc::mma_commit(&k_empty[st1]);
         }
         if (!ok) break;
+        gl += nb;
         tc::mma_commit(q_empty);
         ++qi;
-        if (!issue_pv(prev_st, prev_gl, prev_gb, w.nblk == 1)) break;
       }
       tc::mma_commit(final_bar);
       tc::mbar_wait(final_bar, 0, drain, 0, kWaitCycles);
     }
   } else {
     // ------------------------------ softmax / epilogue ------------------------------
+    const int t = (warp - 2) >> 2;  // query tile of this warp group
     const int quarter = warp & 3;
     const int m = quarter * 32 + lane;  // tile row == TMEM lane
     const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
-    uint32_t gb = 0, qi = 0;
-    int64_t pv_known = -1;  // every PV group with global index <= pv_known has completed
+    uint32_t sc = 0, oc = 0, qi = 0;  // S blocks seen, O finals seen, units seen
     bool ok = true;
-    auto wait_pv_through = [&](int64_t idx) -> bool {
-      while (pv_known < idx) {
-        ++pv_known;
-        if (!tc::mbar_wait(pv_done, (uint32_t)(pv_known & 1), ab, 4, kWaitCycles)) return false;
-      }
-      return true;
-    };
+    const bool neg_scale = P.scale_log2 < 0.f;
     for (int64_t u = blockIdx.x; u < P.n_units && ok; u += gridDim.x) {
       Unit w;
       if (!decode_unit(P, u, w)) continue;
       const int hh = m / P.Pt, pi = m - hh * P.Pt;
-      const bool valid = hh < P.G && pi < w.n_rows;
-      const int pos = valid ? P.rows[(int64_t)w.b * P.rows_sb + w.r0 + pi] : -1;
+      const bool valid = hh < P.G && pi < w.n_rows[t];
+      const int pos = valid ? P.rows[(int64_t)w.b * P.rows_sb + w.r0 + t * P.Pt + pi] : -1;
       const int head = w.g * P.G + hh;
-      // gather this row of Q into the 128-byte-swizzled K-major tile
+      // gather this row of Q into the 128-byte-swizzled K-major tile (zeros for unused rows)
       if (qi > 0 && !tc::mbar_wait(q_empty, (qi - 1) & 1, ab, 4, kWaitCycles)) break;
       {
+        uint8_t *q_tile = sQ + t * kTileBytes;
         const uint4 *src = reinterpret_cast<const uint4 *>(
             reinterpret_cast<const T *>(P.q) + (valid ? (int64_t)w.b * P.q_sb + (int64_t)head * P.q_sh +
                                                             (int64_t)pos * P.q_ss
                                                       : 0));
+        uint4 v[16];
+#pragma unroll
+        for (int c = 0; c < 16; ++c) v[c] = valid ? src[c] : make_uint4(0, 0, 0, 0);
 #pragma unroll
         for (int c = 0; c < 16; ++c) {
-          const uint4 v = valid ? src[c] : make_uint4(0, 0, 0, 0);
           const int kb = c >> 3, cc = c & 7;
-          *reinterpret_cast<uint4 *>(sQ + kb * kHalfTile + m * 128 + ((cc ^ (m & 7)) << 4)) = v;
+          *reinterpret_cast<uint4 *>(q_tile + kb * kHalfTile + m * 128 + ((cc ^ (m & 7)) << 4)) = v[c];
         }
       }
       tc::fence_proxy_async_smem();
       __syncwarp();
-      if (lane == 0) tc::mbar_arrive(q_full);
+      if (lane == 0) tc::mbar_arrive(&q_full[t]);
+      ++qi;
 
+      const int nb = w.nblk[t];
       float m_used = -INFINITY, l = 0.f;
-      for (int j = 0; j < w.nblk; ++j) {
-        if (!tc::mbar_wait(&s_full[gb & 1], (gb >> 1) & 1, ab, 4, kWaitCycles)) {
+      const uint32_t s_addr = tmem + lane_addr + tmem_s(t);
+      for (int j = 0; j < nb; ++j) {
+        if (!tc::mbar_wait(&s_full[t], sc & 1, ab, 4, kWaitCycles)) {
           ok = false;
           break;
         }
+        if (quarter == 2 && lane == 0) SB_TRACE(2 + t, sc);
+        ++sc;
         tc::fence_after_sync();
-        // S for this block proves every PV group issued before it has completed
-        pv_known = max(pv_known, (int64_t)gb - (j == 0 ? 1 : 2));
-        const uint32_t s_addr = tmem + lane_addr + kTmemS + (gb & 1) * kBN;
-        float s[kBN];
-        {
-          uint32_t r[32];
+        const int key0 = j * kBN;
+        // keys past this row are masked; unused rows (zero Q) are left unmasked and never stored
+        const bool diag = valid && key0 + kBN - 1 > pos;
+        const bool any_diag = __any_sync(0xffffffffu, diag);
+        const float masked = neg_scale ? INFINITY : -INFINITY;
+        float mx;
+        if (!any_diag) {
+          // every key of the block is visible to every row of this warp
+          float a0 = masked, a1 = masked, a2 = masked, a3 = masked;
 #pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            tc::tmem_ld32(s_addr + c * 32, r);
+          for (int h = 0; h < 2; ++h) {
+            uint32_t r[2][32];
+            tc::tmem_ld32(s_addr + h * 64, r[0]);
+            tc::tmem_ld32(s_addr + h * 64 + 32, r[1]);
             tc::tmem_ld_wait();
 #pragma unroll
-            for (int i = 0; i < 32; ++i) s[c * 32 + i] = __uint_as_float(r[i]);
+            for (int c = 0; c < 64; c += 8) {
+#define SB_X(i) __uint_as_float(r[(c + (i)) >> 5][(c + (i)) & 31])
+              if (!neg_scale) {
+                a0 = tc::max3(a0, SB_X(0), SB_X(1)), a1 = tc::max3(a1, SB_X(2), SB_X(3));
+                a2 = tc::max3(a2, SB_X(4), SB_X(5)), a3 = tc::max3(a3, SB_X(6), SB_X(7));
+              } else {
+                a0 = tc::min3(a0, SB_X(0), SB_X(1)), a1 = tc::min3(a1, SB_X(2), SB_X(3));
+                a2 = tc::min3(a2, SB_X(4), SB_X(5)), a3 = tc::min3(a3, SB_X(6), SB_X(7));
+              }
+#undef SB_X
+            }
           }
-        }
-        const int key0 = j * kBN;
-        float mx = -INFINITY;
+          mx = neg_scale ? fminf(fminf(a0, a1), fminf(a2, a3)) : fmaxf(fmaxf(a0, a1), fmaxf(a2, a3));
+        } else {
+          float a0 = masked, a1 = masked, a2 = masked, a3 = masked;
 #pragma unroll
-        for (int c = 0; c < kBN; ++c) {
-          const float x = (key0 + c <= pos) ? s[c] * P.scale_log2 : -INFINITY;
-          s[c] = x;
-          mx = fmaxf(mx, x);
+          for (int h = 0; h < 2; ++h) {
+            uint32_t r[2][32];
+            tc::tmem_ld32(s_addr + h * 64, r[0]);
+            tc::tmem_ld32(s_addr + h * 64 + 32, r[1]);
+            tc::tmem_ld_wait();
+#pragma unroll
+            for (int c = 0; c < 64; c += 4) {
+              float x[4];
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                x[i] = __uint_as_float(r[(c + i) >> 5][(c + i) & 31]);
+                if (key0 + h * 64 + c + i > pos) x[i] = masked;
+              }
+              if (!neg_scale)
+                a0 = fmaxf(a0, x[0]), a1 = fmaxf(a1, x[1]), a2 = fmaxf(a2, x[2]), a3 = fmaxf(a3, x[3]);
+              else
+                a0 = fminf(a0, x[0]), a1 = fminf(a1, x[1]), a2 = fminf(a2, x[2]), a3 = fminf(a3, x[3]);
+            }
+          }
+          mx = neg_scale ? fminf(fminf(a0, a1), fminf(a2, a3)) : fmaxf(fmaxf(a0, a1), fmaxf(a2, a3));
         }
+        if (quarter == 2 && lane == 0) SB_TRACE(4 + t, sc);
+        const float mx_s = mx * P.scale_log2;  // row max of the scaled logits (log2 domain)
         float m_new = m_used;
         bool need = false;
-        if (mx > -INFINITY && (m_used == -INFINITY || mx > m_used + 8.f)) {
+        if (mx_s > -INFINITY && (m_used == -INFINITY || mx_s > m_used + 8.f)) {
           need = m_used != -INFINITY;
-          m_new = mx;
+          m_new = mx_s;
         }
         if (__any_sync(0xffffffffu, need)) {
-          if (!wait_pv_through((int64_t)gb - 1)) {
-            ok = false;
-            break;
-          }
-          tc::fence_after_sync();
+          // O_t holds blocks < j (certified by this S block's barrier): rescale it in TMEM
           const float alpha = need ? tc::ex2_approx(m_used - m_new) : 1.f;
-          const uint32_t o_addr = tmem + lane_addr + kTmemO;
+          const uint32_t o_addr = tmem + lane_addr + tmem_o(t);
 #pragma unroll 1
-          for (int c = 0; c < kD; c += 16) {
-            uint32_t r[16];
-            tc::tmem_ld16(o_addr + c, r);
+          for (int c = 0; c < kD; c += 32) {
+            uint32_t r[32];
+            tc::tmem_ld32(o_addr + c, r);
             tc::tmem_ld_wait();
 #pragma unroll
-            for (int i = 0; i < 16; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
-            tc::tmem_st16(o_addr + c, r);
+            for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
+            tc::tmem_st16(o_addr + c, *reinterpret_cast<const uint32_t(*)[16]>(r));
+            tc::tmem_st16(o_addr + c + 16, *reinterpret_cast<const uint32_t(*)[16]>(r + 16));
           }
           tc::tmem_st_wait();
           l *= alpha;
         }
         m_used = m_new;
-        float sum = 0.f;
-        const uint32_t p_addr = tmem + lane_addr + kTmemS + (gb & 1) * kBN;
+        // P = 2^(s * scale_log2 - m_used); rows with no visible key yet give 0
+        const float neg_m = m_used != -INFINITY ? -m_used : -INFINITY;
+        const float2 cc = make_float2(P.scale_log2, P.scale_log2), nm = make_float2(neg_m, neg_m);
+        float2 sum2 = make_float2(0.f, 0.f);
+        // exponentials on MUFU, one pair in kPolyEvery as a polynomial on the FMA pipe
+        // one pair of scores -> probabilities: MUFU, or (one pair in kPolyEvery) the FMA-pipe polynomial
+        auto exp_pair = [&](uint32_t a0, uint32_t a1, int i) -> float2 {
+#if SB_ATTN_PACKED
+          const float2 e = tc::fma2(make_float2(__uint_as_float(a0), __uint_as_float(a1)), cc, nm);
+#else
+          const float2 e = make_float2(fmaf(__uint_as_float(a0), cc.x, nm.x), fmaf(__uint_as_float(a1), cc.y, nm.y));
+#endif
+          if (kPolyEvery > 0 && i % (kPolyEvery > 0 ? kPolyEvery : 1) == kPolyEvery - 1) return tc::exp2_poly2(e);
+          return make_float2(tc::ex2_approx(e.x), tc::ex2_approx(e.y));
+        };
+        auto accumulate = [&](float2 pp) {
+#if SB_ATTN_PACKED
+          sum2 = tc::add2(sum2, pp);
+#else
+          sum2.x += pp.x;
+          sum2.y += pp.y;
+#endif
+        };
+        if (!any_diag) {
+#pragma unroll 1
+          for (int c = 0; c < kBN; c += kPChunk) {
+            uint32_t x[kPChunk / 32][32];
 #pragma unroll
-        for (int c = 0; c < kBN; c += 32) {
-          uint32_t r[16];
+            for (int hh = 0; hh < kPChunk / 32; ++hh) tc::tmem_ld32(s_addr + c + hh * 32, x[hh]);
+            tc::tmem_ld_wait();
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const float p0 = m_used == -INFINITY ? 0.f : tc::ex2_approx(s[c + 2 * i] - m_used);
-            const float p1 = m_used == -INFINITY ? 0.f : tc::ex2_approx(s[c + 2 * i + 1] - m_used);
-            sum += p0 + p1;
-            r[i] = Pack2<T>::pack(p0, p1);
+            for (int hh = 0; hh < kPChunk / 32; ++hh) {
+              uint32_t r[16];
+#pragma unroll
+              for (int i = 0; i < 16; ++i) {
+                const float2 pp = exp_pair(x[hh][2 * i], x[hh][2 * i + 1], i);
+                accumulate(pp);
+                r[i] = Pack2<T>::pack(pp.x, pp.y);
+              }
+              tc::tmem_st16(s_addr + (c + hh * 32) / 2, r);
+            }
           }
-          tc::tmem_st16(p_addr + c / 2, r);
+        } else {
+#pragma unroll 1
+          for (int c = 0; c < kBN; c += 32) {
+            uint32_t x[32];
+            tc::tmem_ld32(s_addr + c, x);
+            tc::tmem_ld_wait();
+            uint32_t r[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              float2 pp = exp_pair(x[2 * i], x[2 * i + 1], i);
+              const int k0 = key0 + c + 2 * i;
+              if (k0 > pos) pp.x = 0.f;
+              if (k0 + 1 > pos) pp.y = 0.f;
+              accumulate(pp);
+              r[i] = Pack2<T>::pack(pp.x, pp.y);
+            }
+            tc::tmem_st16(s_addr + c / 2, r);
+          }
         }
+        const float sum0 = sum2.x, sum1 = sum2.y;
         tc::tmem_st_wait();
-        l += sum;
+        l += sum0 + sum1;
         tc::fence_before_sync();
         __syncwarp();
-        if (lane == 0) tc::mbar_arrive(&p_full[gb & 1]);
-        ++gb;
+        if (quarter == 2 && lane == 0) SB_TRACE(6 + t, sc);
+        if (lane == 0) SB_TRACE(8 + 4 * t + quarter, sc);
+        if (lane == 0) tc::mbar_arrive(&p_full[t]);
       }
       if (!ok) break;
+      if (nb == 0) continue;
       // epilogue: O / l for this row
-      if (!wait_pv_through((int64_t)gb - 1)) break;
+      if (!tc::mbar_wait(&o_final[t], oc & 1, ab, 4, kWaitCycles)) break;
+      ++oc;
       tc::fence_after_sync();
       const float inv = l > 0.f ? 1.f / l : 0.f;
       uint4 *dst = reinterpret_cast<uint4 *>(
           reinterpret_cast<T *>(P.out) +
           (valid ? (int64_t)w.b * P.o_sb + (int64_t)head * P.o_sh + (int64_t)pos * P.o_ss : 0));
-      const uint32_t o_addr = tmem + lane_addr + kTmemO;
+      const uint32_t o_addr = tmem + lane_addr + tmem_o(t);
 #pragma unroll 1
-      for (int c = 0; c < kD; c += 16) {
-        uint32_t r[16];
-        tc::tmem_ld16(o_addr + c, r);
+      for (int c = 0; c < kD; c += 32) {
+        uint32_t r[32];
+        tc::tmem_ld32(o_addr + c, r);
         tc::tmem_ld_wait();
         if (valid) {
-          uint32_t pk[8];
+          uint32_t pk[16];
 #pragma unroll
-          for (int i = 0; i < 8; ++i)
+          for (int i = 0; i < 16; ++i)
             pk[i] = Pack2<T>::pack(__uint_as_float(r[2 * i]) * inv, __uint_as_float(r[2 * i + 1]) * inv);
-          dst[c / 8] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-          dst[c / 8 + 1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) dst[c / 8 + i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
         }
       }
       tc::fence_before_sync();
-      ++qi;
     }
   }
 
@@ -532,6 +689,12 @@ bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 
 }  // namespace
 }  // namespace sb
 
+#if SB_ATTN_TRACE
+extern "C" SB_API int sb_attn_trace_read(long long *dst) {
+  return cudaMemcpyFromSymbol(dst, sb::g_trace, sizeof(long long) * 16 * 512) == cudaSuccess ? 0 : -3;
+}
+#endif
+
 extern "C" SB_API int sb_mask_to_rows(const uint8_t *mask, int64_t mask_stride, int32_t batch, int32_t seq_len,
                                       int32_t *rows, int64_t rows_stride, int32_t *counts, void *stream) {
   if (batch < 0 || seq_len < 0) return SB_ERR_INVALID_ARGUMENT;
@@ -568,7 +731,8 @@ extern "C" SB_API int sb_partial_attention(sb_attn_tensor q, sb_attn_tensor k, s
   P.G = n_q_heads / n_kv_heads;
   P.status = status;
   const int es = elem_bytes(dtype);
-  const bool tc_ok = dtype != SB_DTYPE_F32 && head_dim == kD && P.G <= kBM && aligned16(q.data) &&
+  const bool tc_ok = dtype != SB_DTYPE_F32 && head_dim == kD && P.G <= kBM && std::isfinite(scale) && scale != 0.f &&
+                     aligned16(q.data) &&
                      aligned16(out.data) && aligned16(k.data) && aligned16(v.data) && (q.stride_seq * es) % 16 == 0 &&
                      (q.stride_head * es) % 16 == 0 && (q.stride_batch * es) % 16 == 0 &&
                      (out.stride_seq * es) % 16 == 0 && (out.stride_head * es) % 16 == 0 &&
@@ -578,7 +742,7 @@ extern "C" SB_API int sb_partial_attention(sb_attn_tensor q, sb_attn_tensor k, s
                      (v.stride_batch * es) % 16 == 0;
   if (tc_ok) {
     P.Pt = kBM / P.G;
-    P.T_max = (max_rows + P.Pt - 1) / P.Pt;
+    P.T_max = (max_rows + 2 * P.Pt - 1) / (2 * P.Pt);
     P.n_units = (int64_t)P.T_max * batch * n_kv_heads;
     P.scale_log2 = scale * 1.4426950408889634f;
     if (dtype == SB_DTYPE_BF16) return launch_tc<__nv_bfloat16>(k, v, P, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, st);

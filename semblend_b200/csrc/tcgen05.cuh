@@ -45,6 +45,25 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
   return ok != 0;
 }
 
+#ifndef SB_WAIT_SLEEP
+#define SB_WAIT_SLEEP 0
+#endif
+
+// As mbar_try_wait, but the thread may be suspended in hardware (up to about
+// a millisecond) until the phase completes, instead of returning at once:
+// waiting warps then take no issue slots from the warps doing the work.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t *bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, 1000000;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 // Shared abort state of one CTA: a flag every bounded wait polls, and the
 // global error word the first failing wait records its code in.
 struct Abort {
@@ -59,7 +78,11 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, const 
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
   while (true) {
+#if SB_WAIT_SLEEP
+    if (mbar_try_wait_sleep(bar, parity)) return true;
+#else
     if (mbar_try_wait(bar, parity)) return true;
+#endif
     if (*ab.flag) return false;
     if (clock64() - t0 > max_cycles) {
       *ab.flag = 1;
@@ -158,6 +181,58 @@ __device__ __forceinline__ float ex2_approx(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// Three-input maximum / minimum (sm_100).
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+__device__ __forceinline__ float min3(float a, float b, float c) {
+  float d;
+  asm("min.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// Packed fp32 pairs (sm_100): one instruction for two lanes' worth of work.
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
+__device__ __forceinline__ float2 add2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+
+// 2^x for a pair of floats on the FMA pipe (no MUFU): x = j + f with
+// j = rint(x) (by the 1.5 * 2^23 rounding constant) and f in [-0.5, 0.5];
+// 2^f = 1 + f (c1 + f (c2 + f c3)) with coefficients fitted to 2^f on
+// Chebyshev nodes of [-0.5, 0.5] (relative error 1.0e-4, far below a bf16
+// ulp); 2^j enters as j added to the exponent field.  x below -127 gives a
+// value below 2^-126 (effectively zero); x must be below 128.
+__device__ __forceinline__ float2 exp2_poly2(float2 x) {
+  constexpr float kRound = 12582912.f;  // 1.5 * 2^23
+  x.x = fmaxf(x.x, -127.f);
+  x.y = fmaxf(x.y, -127.f);
+  const float2 t = add2(x, make_float2(kRound, kRound));
+  const float2 r = add2(t, make_float2(-kRound, -kRound));
+  const float2 f = fma2(r, make_float2(-1.f, -1.f), x);
+  float2 p = fma2(f, make_float2(0.05500893f, 0.05500893f), make_float2(0.24221095f, 0.24221095f));
+  p = fma2(f, p, make_float2(0.6932829f, 0.6932829f));
+  p = fma2(f, p, make_float2(1.f, 1.f));
+  return make_float2(__int_as_float(__float_as_int(p.x) + (__float_as_int(t.x) << 23)),
+                     __int_as_float(__float_as_int(p.y) + (__float_as_int(t.y) << 23)));
 }
 
 __device__ __forceinline__ void tma_load_4d(void *dst, const CUtensorMap *map, uint64_t *bar, int x, int y, int z,

@@ -137,3 +137,36 @@ def test_long_context_rows_sample():
     vv = oatt.expand_kv_heads(v[0].float(), Hq)
     want = oatt.partial_prefill_attention_blocked(q[0].float(), kk, vv, pick)
     torch.testing.assert_close(out[0][:, pick.to(DEV), :].float().cpu(), want, atol=2e-2, rtol=0)
+
+
+@pytest.mark.parametrize("scale", [-0.06, 0.4])
+def test_tensor_core_negative_and_large_scale(scale):
+    """A negative scale (row minimum becomes the reference) and a large one
+    (logit spreads that force many rescales of the running output)."""
+    g = torch.Generator().manual_seed(11)
+    B, Hq, Hkv, S, D = 1, 8, 2, 900, 128
+    q = torch.randn(B, Hq, S, D, generator=g).to(torch.bfloat16)
+    k = torch.randn(B, Hkv, S, D, generator=g).to(torch.bfloat16)
+    v = torch.randn(B, Hkv, S, D, generator=g).to(torch.bfloat16)
+    mask = _spans_mask(S, 6, 40, 0.2, 4).unsqueeze(0)
+    out = tk.partial_prefill_attention(q.to(DEV), k.to(DEV), v.to(DEV), mask.to(DEV), scale)
+    rows = torch.where(mask[0])[0]
+    kk = oatt.expand_kv_heads(k[0].float(), Hq)
+    vv = oatt.expand_kv_heads(v[0].float(), Hq)
+    want = oatt.partial_prefill_attention_blocked(q[0].float(), kk, vv, rows, scale=scale)
+    torch.testing.assert_close(out[0][:, rows.to(DEV), :].float().cpu(), want, atol=2e-2, rtol=0)
+
+
+@pytest.mark.parametrize("count", [1, 10, 18, 19, 36, 37])
+def test_row_tile_pair_boundaries(count):
+    """Row counts around the two-tile unit (G = 7 -> 18 rows per tile): second
+    tile empty, partly filled, full, and a unit with a single row."""
+    g = torch.Generator().manual_seed(count)
+    B, Hq, Hkv, S, D = 1, 28, 4, 600, 128
+    q = (torch.randn(B, Hq, S, D, generator=g) / math.sqrt(D)).to(torch.bfloat16)
+    k = (torch.randn(B, Hkv, S, D, generator=g) / math.sqrt(D)).to(torch.bfloat16)
+    v = torch.randn(B, Hkv, S, D, generator=g).to(torch.bfloat16)
+    mask = torch.zeros(B, S, dtype=torch.bool)
+    mask[0, torch.randperm(S, generator=g)[:count]] = True
+    out = tk.partial_prefill_attention(q.to(DEV), k.to(DEV), v.to(DEV), mask.to(DEV))
+    _check_rows(out, q, k, v, mask, atol=2e-2)
