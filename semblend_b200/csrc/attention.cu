@@ -39,23 +39,27 @@ constexpr int kD = 128;
 // One pair of exponentials in every SB_ATTN_POLY_EVERY is evaluated as a
 // polynomial on the FMA pipe instead of MUFU (0: all on MUFU).
 #ifndef SB_ATTN_POLY_EVERY
-#define SB_ATTN_POLY_EVERY 0
+#define SB_ATTN_POLY_EVERY 4
 #endif
 constexpr int kPolyEvery = SB_ATTN_POLY_EVERY;
-// S columns read from TMEM per wait when turning S into P (32 or 64).
-#ifndef SB_ATTN_PCHUNK
-#define SB_ATTN_PCHUNK 32
+
+// warps 0-3 softmax of tile 0, warps 4-7 softmax of tile 1 (warpgroups 0 and 1),
+// warp 8 TMA, warp 9 MMA, warps 10-11 idle (warpgroup 2).  Launched with 168
+// registers a thread (384 x 168 fill the register file); warpgroup 2 gives
+// registers up (setmaxnreg) so the softmax warpgroups can hold a whole S row:
+// 2 x 128 x kSoftmaxRegs + 128 x kControlRegs = 384 x 168.
+constexpr int kThreads = 384;
+constexpr int kSoftmaxRegs = 200;
+constexpr int kControlRegs = 104;
+static_assert(2 * 128 * kSoftmaxRegs + 128 * kControlRegs == kThreads * 168, "register split");
+#ifndef SB_ATTN_K_STAGES
+#define SB_ATTN_K_STAGES 2
 #endif
-constexpr int kPChunk = SB_ATTN_PCHUNK;
-// Packed fp32x2 arithmetic for the scale-subtract and the row sum.
-#ifndef SB_ATTN_PACKED
-#define SB_ATTN_PACKED 1
-#endif
-constexpr int kThreads = 320;  // warp 0 TMA, warp 1 MMA, warps 2-5 softmax of tile 0, warps 6-9 of tile 1
-constexpr int kStages = 2;     // K and V rings
+constexpr int kKStages = SB_ATTN_K_STAGES;  // K ring (K is needed one MMA group before V)
+constexpr int kVStages = 2;    // V ring
 constexpr int kTileBytes = 128 * 128 * 2;  // one [128 x 128] 16-bit operand tile (two 64-column boxes)
 constexpr int kHalfTile = kTileBytes / 2;
-constexpr int kSmemBytes = 1024 + kTileBytes * (2 + 2 * kStages) + 256;
+constexpr int kSmemBytes = 1024 + kTileBytes * (2 + kKStages + kVStages) + 256;
 constexpr long long kWaitCycles = 2000000000LL;
 // TMEM columns: tile t has S (P packed over its first half) at [256 t, 256 t + 128)
 // and its O accumulator at [256 t + 128, 256 t + 256).
@@ -63,7 +67,7 @@ __host__ __device__ constexpr uint32_t tmem_s(int t) { return 256u * t; }
 __host__ __device__ constexpr uint32_t tmem_o(int t) { return 256u * t + 128u; }
 
 #if SB_ATTN_TRACE
-__device__ long long g_trace[16 * 512];
+__device__ long long g_trace[24 * 512];
 #define SB_TRACE(slot, idx) do { if (blockIdx.x == 0 && (idx) < 512) g_trace[(slot) * 512 + (idx)] = clock64(); } while (0)
 #else
 #define SB_TRACE(slot, idx) do { } while (0)
@@ -126,10 +130,6 @@ template <> struct Pack2<__half> {
 // one tile turn its S block into P, the tensor cores run the other tile's
 // P.V and next Q.K^T.  PV_t(j) is issued before S_t(j + 1), so the barrier
 // that signals S_t(j + 1) also certifies that O_t holds blocks <= j.
-// Registers are split per SM sub-partition: with 10 warps, three share one
-// quarter of the register file, so a thread has at most 168.  The softmax
-// therefore reads each S block from TMEM twice (row max, then P) instead of
-// holding all 128 scores in registers.
 template <typename T>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
@@ -137,34 +137,37 @@ __global__ void __launch_bounds__(kThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t *sQ = smem;                          // [2] query tiles
-  uint8_t *sK = sQ + 2 * kTileBytes;           // [kStages]
-  uint8_t *sV = sK + kStages * kTileBytes;     // [kStages]
-  uint64_t *bars = reinterpret_cast<uint64_t *>(sV + kStages * kTileBytes);
-  uint64_t *k_full = bars;                     // [kStages]
-  uint64_t *k_empty = bars + 2;                // [kStages]
-  uint64_t *v_full = bars + 4;                 // [kStages]
-  uint64_t *v_empty = bars + 6;                // [kStages]
-  uint64_t *q_full = bars + 8;                 // [2]
-  uint64_t *q_empty = bars + 10;
-  uint64_t *s_full = bars + 11;                // [2]
-  uint64_t *p_full = bars + 13;                // [2]
-  uint64_t *o_final = bars + 15;               // [2]
-  uint64_t *final_bar = bars + 17;
-  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 18);
-  volatile int *abort_flag = reinterpret_cast<volatile int *>(bars + 19);
+  uint8_t *sK = sQ + 2 * kTileBytes;           // [kKStages]
+  uint8_t *sV = sK + kKStages * kTileBytes;    // [kVStages]
+  uint64_t *bars = reinterpret_cast<uint64_t *>(sV + kVStages * kTileBytes);
+  uint64_t *k_full = bars;                     // [kKStages <= 3]
+  uint64_t *k_empty = bars + 3;                // [kKStages <= 3]
+  uint64_t *v_full = bars + 6;                 // [kVStages]
+  uint64_t *v_empty = bars + 8;                // [kVStages]
+  uint64_t *q_full = bars + 10;                // [2]
+  uint64_t *q_empty = bars + 12;
+  uint64_t *s_full = bars + 13;                // [2]
+  uint64_t *p_full = bars + 15;                // [2 tiles][2 key halves]
+  uint64_t *o_final = bars + 19;               // [2]
+  uint64_t *final_bar = bars + 21;
+  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 22);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(bars + 23);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) {
+    for (int s = 0; s < kKStages; ++s) {
       tc::mbar_init(&k_full[s], 1);
       tc::mbar_init(&k_empty[s], 1);
+    }
+    for (int s = 0; s < kVStages; ++s) {
       tc::mbar_init(&v_full[s], 1);
       tc::mbar_init(&v_empty[s], 1);
     }
     for (int t = 0; t < 2; ++t) {
       tc::mbar_init(&q_full[t], 4);
       tc::mbar_init(&s_full[t], 1);
-      tc::mbar_init(&p_full[t], 4);
+      tc::mbar_init(&p_full[2 * t], 4);
+      tc::mbar_init(&p_full[2 * t + 1], 4);
       tc::mbar_init(&o_final[t], 1);
     }
     tc::mbar_init(q_empty, 1);
@@ -172,7 +175,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     *abort_flag = 0;
     tc::fence_mbar_init();
   }
-  if (warp == 1) {
+  if (warp == 9) {
     tc::tmem_alloc(tmem_holder, 512);
     tc::tmem_relinquish();
   }
@@ -184,47 +187,53 @@ __global__ void __launch_bounds__(kThreads, 1)
   volatile int never = 0;
   const tc::Abort drain{&never, nullptr};
 
-  if (warp == 0) {
+  if (warp >= 8) {
+   asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kControlRegs));
+   if (warp == 8) {
     if (lane == 0) {
       // ------------------------------ TMA producer ------------------------------
       tc::tma_prefetch_desc(&tmK);
       tc::tma_prefetch_desc(&tmV);
       uint32_t gl = 0;
-      bool ok = true;
+      bool ok = true, vfail = false;
       for (int64_t u = blockIdx.x; u < P.n_units && ok; u += gridDim.x) {
         Unit w;
         if (!decode_unit(P, u, w)) continue;
         const int nb = max(w.nblk[0], w.nblk[1]);
         for (int j = 0; j < nb; ++j) {
-          const uint32_t st = gl % kStages, ph = (gl / kStages) & 1;
-          if (!tc::mbar_wait(&k_empty[st], ph ^ 1, ab, 2, kWaitCycles)) {
+          const uint32_t ks = gl % kKStages, kph = (gl / kKStages) & 1;
+          const uint32_t vs = gl % kVStages, vph = (gl / kVStages) & 1;
+          if (!tc::mbar_wait(&k_empty[ks], kph ^ 1, ab, 2, kWaitCycles)) {
             ok = false;
             break;
           }
-          uint8_t *k_dst = sK + st * kTileBytes;
-          tc::mbar_arrive_expect_tx(&k_full[st], kTileBytes);
-          tc::tma_load_4d(k_dst, &tmK, &k_full[st], 0, j * kBN, w.g, w.b);
-          tc::tma_load_4d(k_dst + kHalfTile, &tmK, &k_full[st], 64, j * kBN, w.g, w.b);
-          if (!tc::mbar_wait(&v_empty[st], ph ^ 1, ab, 2, kWaitCycles)) {
+          uint8_t *k_dst = sK + ks * kTileBytes;
+          tc::mbar_arrive_expect_tx(&k_full[ks], kTileBytes);
+          tc::tma_load_4d(k_dst, &tmK, &k_full[ks], 0, j * kBN, w.g, w.b);
+          tc::tma_load_4d(k_dst + kHalfTile, &tmK, &k_full[ks], 64, j * kBN, w.g, w.b);
+          ++gl;  // the K load of this block is in flight from here on
+          if (!tc::mbar_wait(&v_empty[vs], vph ^ 1, ab, 2, kWaitCycles)) {
             ok = false;
-            ++gl;  // K of this block is in flight: drain it below
+            vfail = true;
             break;
           }
-          uint8_t *v_dst = sV + st * kTileBytes;
-          tc::mbar_arrive_expect_tx(&v_full[st], kTileBytes);
-          tc::tma_load_4d(v_dst, &tmV, &v_full[st], 0, j * kBN, w.g, w.b);
-          tc::tma_load_4d(v_dst + kHalfTile, &tmV, &v_full[st], 64, j * kBN, w.g, w.b);
-          ++gl;
+          uint8_t *v_dst = sV + vs * kTileBytes;
+          tc::mbar_arrive_expect_tx(&v_full[vs], kTileBytes);
+          tc::tma_load_4d(v_dst, &tmV, &v_full[vs], 0, j * kBN, w.g, w.b);
+          tc::tma_load_4d(v_dst + kHalfTile, &tmV, &v_full[vs], 64, j * kBN, w.g, w.b);
         }
       }
-      // every load this thread issued lands before the CTA can exit
-      const uint32_t n_out = gl < (uint32_t)kStages ? gl : (uint32_t)kStages;
-      for (uint32_t i = gl - n_out; i < gl; ++i) {
-        tc::mbar_wait(&k_full[i % kStages], (i / kStages) & 1, drain, 0, kWaitCycles);
-        tc::mbar_wait(&v_full[i % kStages], (i / kStages) & 1, drain, 0, kWaitCycles);
-      }
+      // every load this thread issued lands before the CTA can exit (the V load
+      // of the last counted block is missing when its slot wait gave up)
+      const uint32_t nk = gl < (uint32_t)kKStages ? gl : (uint32_t)kKStages;
+      for (uint32_t i = gl - nk; i < gl; ++i)
+        tc::mbar_wait(&k_full[i % kKStages], (i / kKStages) & 1, drain, 0, kWaitCycles);
+      const uint32_t gv = vfail ? gl - 1 : gl;
+      const uint32_t nv = gv < (uint32_t)kVStages ? gv : (uint32_t)kVStages;
+      for (uint32_t i = gv - nv; i < gv; ++i)
+        tc::mbar_wait(&v_full[i % kVStages], (i / kVStages) & 1, drain, 0, kWaitCycles);
     }
-  } else if (warp == 1) {
+  } else if (warp == 9) {
     if (lane == 0) {
       // ------------------------------ MMA issuer ------------------------------
       constexpr uint32_t fmt = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
@@ -233,16 +242,20 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t gl = 0, qi = 0;
       uint32_t pc[2] = {0, 0};  // P blocks consumed per tile
       bool ok = true;
+      // descriptors advance in 16-byte units of the start address (no carry out of its 14 bits)
+      const uint64_t dq0 = tc::desc_kmajor_sw128(sQ);
+      const uint64_t dk0 = tc::desc_kmajor_sw128(sK);
+      const uint64_t dv0 = tc::desc_mnmajor_sw128(sV, 0, kHalfTile);
+      constexpr uint32_t kTileUnits = kTileBytes >> 4, kHalfUnits = kHalfTile >> 4;
       auto issue_s = [&](int t, uint32_t st) {
         const uint32_t s_tmem = tmem + tmem_s(t);
+        const uint64_t dq = dq0 + t * kTileUnits, dk = dk0 + st * kTileUnits;
 #pragma unroll
         for (int kb = 0; kb < 2; ++kb)
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk) {
-            const uint64_t dq = tc::desc_kmajor_sw128(sQ + t * kTileBytes + kb * kHalfTile, kk * 32);
-            const uint64_t dk = tc::desc_kmajor_sw128(sK + st * kTileBytes + kb * kHalfTile, kk * 32);
-            tc::mma_bf16_ss(s_tmem, dq, dk, idesc_qk, (kb | kk) != 0);
-          }
+          for (int kk = 0; kk < 4; ++kk)
+            tc::mma_bf16_ss(s_tmem, dq + kb * kHalfUnits + kk * 2, dk + kb * kHalfUnits + kk * 2, idesc_qk,
+                            (kb | kk) != 0);
         tc::mma_commit(&s_full[t]);
       };
       for (int64_t u = blockIdx.x; u < P.n_units && ok; u += gridDim.x) {
@@ -255,55 +268,68 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc::fence_after_sync();
         // S of block 0 for both tiles
         {
-          const uint32_t st = gl % kStages;
-          if (!tc::mbar_wait(&k_full[st], (gl / kStages) & 1, ab, 3, kWaitCycles)) break;
+          const uint32_t ks = gl % kKStages;
+          if (!tc::mbar_wait(&k_full[ks], (gl / kKStages) & 1, ab, 3, kWaitCycles)) break;
           tc::fence_after_sync();
           for (int t = 0; t < 2; ++t)
-            if (w.nblk[t] > 0) issue_s(t, st);
-          tc::mma_commit(&k_empty[st]);
+            if (w.nblk[t] > 0) issue_s(t, ks);
+          tc::mma_commit(&k_empty[ks]);
         }
         for (int j = 0; j < nb && ok; ++j) {
-          const uint32_t st = (gl + j) % kStages, ph = ((gl + j) / kStages) & 1;
-          const uint32_t st1 = (gl + j + 1) % kStages, ph1 = ((gl + j + 1) / kStages) & 1;
+          const uint32_t g = gl + j;
+          const uint32_t vs = g % kVStages, vph = (g / kVStages) & 1;
+          const uint32_t ks1 = (g + 1) % kKStages, kph1 = ((g + 1) / kKStages) & 1;
           bool v_ready = false, k_ready = false;
           for (int t = 0; t < 2 && ok; ++t) {
             if (j >= w.nblk[t]) continue;
-            if (!tc::mbar_wait(&p_full[t], pc[t] & 1, ab, 3, kWaitCycles)) {
+            // P.V in two halves of 64 keys: the first runs while the softmax writes the second
+            if (!tc::mbar_wait(&p_full[2 * t], pc[t] & 1, ab, 3, kWaitCycles)) {
               ok = false;
               break;
             }
             SB_TRACE(t, pc[t]);
-            ++pc[t];
             if (!v_ready) {
-              if (!tc::mbar_wait(&v_full[st], ph, ab, 3, kWaitCycles)) {
+              if (!tc::mbar_wait(&v_full[vs], vph, ab, 3, kWaitCycles)) {
                 ok = false;
                 break;
               }
               v_ready = true;
             }
+            SB_TRACE(20 + t, pc[t]);
             tc::fence_after_sync();
             const uint32_t p_tmem = tmem + tmem_s(t);
+            const uint64_t dv = dv0 + vs * kTileUnits;
 #pragma unroll
-            for (int kk = 0; kk < kBN / 16; ++kk) {
-              const uint64_t dv = tc::desc_mnmajor_sw128(sV + st * kTileBytes, kk * 2048, kHalfTile);
-              tc::mma_bf16_ts(tmem + tmem_o(t), p_tmem + kk * 8, dv, idesc_pv, (j == 0 && kk == 0) ? 0u : 1u);
+            for (int kk = 0; kk < kBN / 32; ++kk)
+              tc::mma_bf16_ts(tmem + tmem_o(t), p_tmem + kk * 8, dv + kk * (2048 >> 4), idesc_pv,
+                              (j == 0 && kk == 0) ? 0u : 1u);
+            if (!tc::mbar_wait(&p_full[2 * t + 1], pc[t] & 1, ab, 3, kWaitCycles)) {
+              ok = false;
+              break;
             }
+            SB_TRACE(16 + t, pc[t]);
+            ++pc[t];
+            tc::fence_after_sync();
+#pragma unroll
+            for (int kk = kBN / 32; kk < kBN / 16; ++kk)
+              tc::mma_bf16_ts(tmem + tmem_o(t), p_tmem + kk * 8, dv + kk * (2048 >> 4), idesc_pv, 1u);
             if (j == w.nblk[t] - 1) tc::mma_commit(&o_final[t]);
             if (j + 1 < w.nblk[t]) {
               if (!k_ready) {
-                if (!tc::mbar_wait(&k_full[st1], ph1, ab, 3, kWaitCycles)) {
+                if (!tc::mbar_wait(&k_full[ks1], kph1, ab, 3, kWaitCycles)) {
                   ok = false;
                   break;
                 }
                 tc::fence_after_sync();
                 k_ready = true;
               }
-              issue_s(t, st1);
+              issue_s(t, ks1);
             }
+            SB_TRACE(18 + t, pc[t] - 1);
           }
           if (!ok) break;
-          tc::mma_commit(&v_empty[st]);
-          if (j + 1 < nb) tc::mma_commit(&k_empty[st1]);
+          tc::mma_commit(&v_empty[vs]);
+          if (j + 1 < nb) tc::mma_commit(&k_empty[ks1]);
         }
         if (!ok) break;
         gl += nb;
@@ -313,9 +339,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc::mma_commit(final_bar);
       tc::mbar_wait(final_bar, 0, drain, 0, kWaitCycles);
     }
+   }
   } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kSoftmaxRegs));
     // ------------------------------ softmax / epilogue ------------------------------
-    const int t = (warp - 2) >> 2;  // query tile of this warp group
+    const int t = warp >> 2;  // query tile of this warpgroup
     const int quarter = warp & 3;
     const int m = quarter * 32 + lane;  // tile row == TMEM lane
     const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
@@ -367,51 +395,30 @@ __global__ void __launch_bounds__(kThreads, 1)
         const bool diag = valid && key0 + kBN - 1 > pos;
         const bool any_diag = __any_sync(0xffffffffu, diag);
         const float masked = neg_scale ? INFINITY : -INFINITY;
+        // the whole S row of this thread, read from TMEM once
+        uint32_t sr[kBN];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) tc::tmem_ld32(s_addr + c * 32, *reinterpret_cast<uint32_t(*)[32]>(sr + c * 32));
+        tc::tmem_ld_wait();
+        if (any_diag) {
+#pragma unroll
+          for (int c = 0; c < kBN; ++c)
+            if (key0 + c > pos) sr[c] = __float_as_uint(masked);
+        }
         float mx;
-        if (!any_diag) {
-          // every key of the block is visible to every row of this warp
+        {
           float a0 = masked, a1 = masked, a2 = masked, a3 = masked;
 #pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            uint32_t r[2][32];
-            tc::tmem_ld32(s_addr + h * 64, r[0]);
-            tc::tmem_ld32(s_addr + h * 64 + 32, r[1]);
-            tc::tmem_ld_wait();
-#pragma unroll
-            for (int c = 0; c < 64; c += 8) {
-#define SB_X(i) __uint_as_float(r[(c + (i)) >> 5][(c + (i)) & 31])
-              if (!neg_scale) {
-                a0 = tc::max3(a0, SB_X(0), SB_X(1)), a1 = tc::max3(a1, SB_X(2), SB_X(3));
-                a2 = tc::max3(a2, SB_X(4), SB_X(5)), a3 = tc::max3(a3, SB_X(6), SB_X(7));
-              } else {
-                a0 = tc::min3(a0, SB_X(0), SB_X(1)), a1 = tc::min3(a1, SB_X(2), SB_X(3));
-                a2 = tc::min3(a2, SB_X(4), SB_X(5)), a3 = tc::min3(a3, SB_X(6), SB_X(7));
-              }
+          for (int c = 0; c < kBN; c += 8) {
+#define SB_X(i) __uint_as_float(sr[c + (i)])
+            if (!neg_scale) {
+              a0 = tc::max3(a0, SB_X(0), SB_X(1)), a1 = tc::max3(a1, SB_X(2), SB_X(3));
+              a2 = tc::max3(a2, SB_X(4), SB_X(5)), a3 = tc::max3(a3, SB_X(6), SB_X(7));
+            } else {
+              a0 = tc::min3(a0, SB_X(0), SB_X(1)), a1 = tc::min3(a1, SB_X(2), SB_X(3));
+              a2 = tc::min3(a2, SB_X(4), SB_X(5)), a3 = tc::min3(a3, SB_X(6), SB_X(7));
+            }
 #undef SB_X
-            }
-          }
-          mx = neg_scale ? fminf(fminf(a0, a1), fminf(a2, a3)) : fmaxf(fmaxf(a0, a1), fmaxf(a2, a3));
-        } else {
-          float a0 = masked, a1 = masked, a2 = masked, a3 = masked;
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            uint32_t r[2][32];
-            tc::tmem_ld32(s_addr + h * 64, r[0]);
-            tc::tmem_ld32(s_addr + h * 64 + 32, r[1]);
-            tc::tmem_ld_wait();
-#pragma unroll
-            for (int c = 0; c < 64; c += 4) {
-              float x[4];
-#pragma unroll
-              for (int i = 0; i < 4; ++i) {
-                x[i] = __uint_as_float(r[(c + i) >> 5][(c + i) & 31]);
-                if (key0 + h * 64 + c + i > pos) x[i] = masked;
-              }
-              if (!neg_scale)
-                a0 = fmaxf(a0, x[0]), a1 = fmaxf(a1, x[1]), a2 = fmaxf(a2, x[2]), a3 = fmaxf(a3, x[3]);
-              else
-                a0 = fminf(a0, x[0]), a1 = fminf(a1, x[1]), a2 = fminf(a2, x[2]), a3 = fminf(a3, x[3]);
-            }
           }
           mx = neg_scale ? fminf(fminf(a0, a1), fminf(a2, a3)) : fmaxf(fmaxf(a0, a1), fmaxf(a2, a3));
         }
@@ -441,75 +448,37 @@ __global__ void __launch_bounds__(kThreads, 1)
           l *= alpha;
         }
         m_used = m_new;
-        // P = 2^(s * scale_log2 - m_used); rows with no visible key yet give 0
+        // P = 2^(s * scale_log2 - m_used): masked keys (+-inf) and rows with no
+        // visible key yet (m_used = -inf) give 0
         const float neg_m = m_used != -INFINITY ? -m_used : -INFINITY;
         const float2 cc = make_float2(P.scale_log2, P.scale_log2), nm = make_float2(neg_m, neg_m);
         float2 sum2 = make_float2(0.f, 0.f);
-        // exponentials on MUFU, one pair in kPolyEvery as a polynomial on the FMA pipe
-        // one pair of scores -> probabilities: MUFU, or (one pair in kPolyEvery) the FMA-pipe polynomial
-        auto exp_pair = [&](uint32_t a0, uint32_t a1, int i) -> float2 {
-#if SB_ATTN_PACKED
-          const float2 e = tc::fma2(make_float2(__uint_as_float(a0), __uint_as_float(a1)), cc, nm);
-#else
-          const float2 e = make_float2(fmaf(__uint_as_float(a0), cc.x, nm.x), fmaf(__uint_as_float(a1), cc.y, nm.y));
-#endif
-          if (kPolyEvery > 0 && i % (kPolyEvery > 0 ? kPolyEvery : 1) == kPolyEvery - 1) return tc::exp2_poly2(e);
-          return make_float2(tc::ex2_approx(e.x), tc::ex2_approx(e.y));
-        };
-        auto accumulate = [&](float2 pp) {
-#if SB_ATTN_PACKED
-          sum2 = tc::add2(sum2, pp);
-#else
-          sum2.x += pp.x;
-          sum2.y += pp.y;
-#endif
-        };
-        if (!any_diag) {
-#pragma unroll 1
-          for (int c = 0; c < kBN; c += kPChunk) {
-            uint32_t x[kPChunk / 32][32];
 #pragma unroll
-            for (int hh = 0; hh < kPChunk / 32; ++hh) tc::tmem_ld32(s_addr + c + hh * 32, x[hh]);
-            tc::tmem_ld_wait();
+        for (int c = 0; c < kBN; c += 32) {
+          uint32_t r[16];
 #pragma unroll
-            for (int hh = 0; hh < kPChunk / 32; ++hh) {
-              uint32_t r[16];
-#pragma unroll
-              for (int i = 0; i < 16; ++i) {
-                const float2 pp = exp_pair(x[hh][2 * i], x[hh][2 * i + 1], i);
-                accumulate(pp);
-                r[i] = Pack2<T>::pack(pp.x, pp.y);
-              }
-              tc::tmem_st16(s_addr + (c + hh * 32) / 2, r);
-            }
+          for (int i = 0; i < 16; ++i) {
+            const float2 e = tc::fma2(make_float2(__uint_as_float(sr[c + 2 * i]), __uint_as_float(sr[c + 2 * i + 1])),
+                                      cc, nm);
+            const float2 pp = (kPolyEvery > 0 && i % (kPolyEvery > 0 ? kPolyEvery : 1) == kPolyEvery - 1)
+                                  ? tc::exp2_poly2(e)
+                                  : make_float2(tc::ex2_approx(e.x), tc::ex2_approx(e.y));
+            sum2 = tc::add2(sum2, pp);
+            r[i] = Pack2<T>::pack(pp.x, pp.y);
           }
-        } else {
-#pragma unroll 1
-          for (int c = 0; c < kBN; c += 32) {
-            uint32_t x[32];
-            tc::tmem_ld32(s_addr + c, x);
-            tc::tmem_ld_wait();
-            uint32_t r[16];
-#pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              float2 pp = exp_pair(x[2 * i], x[2 * i + 1], i);
-              const int k0 = key0 + c + 2 * i;
-              if (k0 > pos) pp.x = 0.f;
-              if (k0 + 1 > pos) pp.y = 0.f;
-              accumulate(pp);
-              r[i] = Pack2<T>::pack(pp.x, pp.y);
+          tc::tmem_st16(s_addr + c / 2, r);
+          if (c % 64 == 32) {  // a half of P (64 keys) is in TMEM: let its P.V start
+            tc::tmem_st_wait();
+            tc::fence_before_sync();
+            __syncwarp();
+            if (c == kBN - 32) {
+              if (quarter == 2 && lane == 0) SB_TRACE(6 + t, sc);
+              if (lane == 0) SB_TRACE(8 + 4 * t + quarter, sc);
             }
-            tc::tmem_st16(s_addr + c / 2, r);
+            if (lane == 0) tc::mbar_arrive(&p_full[2 * t + c / 64]);
           }
         }
-        const float sum0 = sum2.x, sum1 = sum2.y;
-        tc::tmem_st_wait();
-        l += sum0 + sum1;
-        tc::fence_before_sync();
-        __syncwarp();
-        if (quarter == 2 && lane == 0) SB_TRACE(6 + t, sc);
-        if (lane == 0) SB_TRACE(8 + 4 * t + quarter, sc);
-        if (lane == 0) tc::mbar_arrive(&p_full[t]);
+        l += sum2.x + sum2.y;
       }
       if (!ok) break;
       if (nb == 0) continue;
@@ -543,7 +512,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc::fence_before_sync();
   __syncthreads();
   tc::fence_after_sync();
-  if (warp == 1) tc::tmem_dealloc(tmem, 512);
+  if (warp == 9) tc::tmem_dealloc(tmem, 512);
 }
 
 // ---------------------------------------------------------------------------
@@ -691,7 +660,7 @@ bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 
 
 #if SB_ATTN_TRACE
 extern "C" SB_API int sb_attn_trace_read(long long *dst) {
-  return cudaMemcpyFromSymbol(dst, sb::g_trace, sizeof(long long) * 16 * 512) == cudaSuccess ? 0 : -3;
+  return cudaMemcpyFromSymbol(dst, sb::g_trace, sizeof(long long) * 24 * 512) == cudaSuccess ? 0 : -3;
 }
 #endif
 
