@@ -719,6 +719,242 @@ def run_attention(args, local: int) -> dict:
 
 
 # ---------------------------------------------------------------------------
+# Component: end-to-end reuse step on the Llama-3-70B geometry (configs[4], c5)
+# ---------------------------------------------------------------------------
+C5_L, C5_HQ, C5_HKV, C5_D, C5_THETA = 80, 64, 8, 128, 5e5
+C5_REQ, C5_POOL, C5_SEARCH_ROWS, C5_TP = 64, 64, 262144, 8
+
+
+def c5_lengths(rng: np.random.Generator, n: int) -> np.ndarray:
+    """Lognormal context lengths, median 8K, clipped to [4K, 32K], whole 256-token chunks."""
+    x = np.exp(rng.normal(np.log(8192.0), 0.5, n))
+    return (np.clip(x, 4096, 32768) // CHUNK * CHUNK).astype(np.int64)
+
+
+def c5_plan(rng: np.random.Generator, req_len: np.ndarray, donor_len: np.ndarray):
+    """Per request: 2-4 donors from the pool, each 256-token chunk either
+    recomputed (10-20 % of the request, always its last chunk) or copied from a
+    random chunk of one of its donors.  Returns per-request lists of
+    (donor index, donor positions, target positions) and the recompute masks."""
+    reqs, masks = [], []
+    for L in req_len:
+        n_chunks = L // CHUNK
+        donors = rng.choice(len(donor_len), int(rng.integers(2, 5)), replace=False)
+        frac = rng.uniform(0.10, 0.20)
+        n_re = max(1, int(round(frac * n_chunks)))
+        recompute = set(rng.choice(n_chunks - 1, n_re - 1, replace=False).tolist()) | {n_chunks - 1}
+        per_donor = {int(d): ([], []) for d in donors}
+        mask = np.zeros(L, bool)
+        for c in range(n_chunks):
+            t = np.arange(c * CHUNK, (c + 1) * CHUNK)
+            if c in recompute:
+                mask[t] = True
+                continue
+            d = int(rng.choice(donors))
+            dc = int(rng.integers(0, donor_len[d] // CHUNK))
+            per_donor[d][0].append(np.arange(dc * CHUNK, (dc + 1) * CHUNK))
+            per_donor[d][1].append(t)
+        entries = [(d, np.concatenate(dp).astype(np.int32), np.concatenate(tp).astype(np.int32))
+                   for d, (dp, tp) in per_donor.items() if dp]
+        reqs.append(entries)
+        masks.append(mask)
+    return reqs, masks
+
+
+def run_c5(args, world: int, rank: int, local: int) -> dict | None:
+    """One TP-8 rank's slice of the c5 step (1 KV head, 8 query heads): the
+    donor search (64 queries over 262,144 x 384), the fused inject of all 80
+    layers and every request's donors (one launch), and partial-prefill
+    attention for each of the 80 layers (one launch each).  Ranks beyond the
+    first take the next KV heads (weak scaling up to 8)."""
+    from semblend_b200 import _lib
+    from semblend_b200 import rope_correction as rc
+    from semblend_b200 import triton_kernels as tk
+    from semblend_b200.search import DeviceDonorMatrix, cosine_topk_async
+
+    dev = torch.device("cuda", local)
+    rng = np.random.default_rng(SEED + 7)  # the same workload on every rank
+    req_len, donor_len = c5_lengths(rng, C5_REQ), c5_lengths(rng, C5_POOL)
+    plan, masks_l = c5_plan(rng, req_len, donor_len)
+    s_max = int(req_len.max())
+    hq, hkv = C5_HQ // C5_TP, C5_HKV // C5_TP
+    gen = torch.Generator(device=dev).manual_seed(SEED + 7 + rank)
+
+    # paged target cache [L, blocks, 2, hkv, 16, D] and the donor pool [L, 2, hkv, len, D]
+    nblk = (req_len // BLOCK).astype(np.int64)
+    pool_blocks = int(nblk.sum() * 1.1)
+    perm = rng.permutation(pool_blocks)
+    offs = np.concatenate([[0], np.cumsum(nblk)])
+    tables = [perm[offs[r] : offs[r + 1]].astype(np.int32) for r in range(C5_REQ)]
+    cache = torch.empty(C5_L, pool_blocks, 2, hkv, BLOCK, C5_D, dtype=torch.bfloat16, device=dev)
+    cache.normal_(generator=gen)
+    pool = []
+    for Ld in donor_len:
+        t = torch.empty(C5_L, 2, hkv, int(Ld), C5_D, dtype=torch.bfloat16, device=dev)
+        t.normal_(generator=gen)
+        pool.append(t)
+    host_bt = [torch.from_numpy(b).pin_memory() for b in tables]
+    dev_bt = [h.to(dev) for h in host_bt]
+    host_pos, dev_pos, inj = [], [], []
+    n_pairs = 0
+    for r, entries in enumerate(plan):
+        for d, dp, tp in entries:
+            h = torch.from_numpy(np.stack([dp, tp])).pin_memory()
+            dpos = h.to(dev)
+            host_pos.append(h)
+            dev_pos.append(dpos)
+            inj.append(rc.DonorInjection(pool[d], dev_bt[r], dpos[0], dpos[1]))
+            n_pairs += dp.shape[0]
+
+    # donor search: 262,144 x 384 clustered rows, one query per request
+    emb, _ = make_search_inputs(dev, SEED + 8, n_rows=C5_SEARCH_ROWS, n_q=16)
+    m = DeviceDonorMatrix(C5_SEARCH_ROWS, S_DIM, dev)
+    m.write_range(0, emb)
+    del emb
+    qg = torch.Generator(device=dev).manual_seed(SEED + 9)
+    queries = m.emb[torch.randint(0, C5_SEARCH_ROWS, (C5_REQ,), generator=qg, device=dev)] + \
+        0.05 * torch.randn(C5_REQ, S_DIM, generator=qg, device=dev)
+    s_out = (torch.empty(C5_REQ, S_K, dtype=torch.int64, device=dev),
+             torch.empty(C5_REQ, S_K, dtype=torch.float32, device=dev))
+    s_status = torch.zeros(1, dtype=torch.int32, device=dev)
+
+    # attention operands of one layer (the 80 layers reuse them: same shapes, same cost)
+    scale = 1.0 / np.sqrt(C5_D)
+    q = (torch.randn(C5_REQ, hq, s_max, C5_D, generator=gen, device=dev) * scale).to(torch.bfloat16)
+    k = (torch.randn(C5_REQ, hkv, s_max, C5_D, generator=gen, device=dev) * scale).to(torch.bfloat16)
+    v = (torch.randn(C5_REQ, hkv, s_max, C5_D, generator=gen, device=dev) * scale).to(torch.bfloat16)
+    masks = np.zeros((C5_REQ, s_max), bool)
+    for r, mk in enumerate(masks_l):
+        masks[r, : mk.shape[0]] = mk
+    mask_d = torch.from_numpy(masks).to(dev)
+    rows, counts = tk.mask_to_rows(mask_d)
+    out = torch.zeros_like(q)
+    a_status = torch.zeros(1, dtype=torch.int32, device=dev)
+    err = _lib.err_counter(dev)
+    stream = torch.cuda.current_stream(dev)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+
+    def step(record: bool):
+        if record:
+            ev[0].record(stream)
+        cosine_topk_async(m.emb, m.emb16, m.valid, m.stats, queries, S_K, S_THR, status=s_status,
+                          workspace_owner=m, out=s_out)
+        if record:
+            ev[1].record(stream)
+        rc.inject_donors(cache, inj, rope_base=C5_THETA, rotary_style="neox")
+        if record:
+            ev[2].record(stream)
+        for _ in range(C5_L):
+            tk.gqa_partial_attention(q, k, v, rows, counts, out, max_rows=s_max, status=a_status)
+        if record:
+            ev[3].record(stream)
+
+    for _ in range(2):
+        step(False)
+    torch.cuda.synchronize(dev)
+    steps = max(3, min(args.steps // 50, 6))
+    parts = np.zeros(3)
+    clocks = ClockSampler(local) if rank == 0 else None
+    if clocks:
+        clocks.start()
+    barrier(world)
+    torch.cuda.synchronize(dev)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for _ in range(steps):
+        step(True)
+        torch.cuda.synchronize(dev)
+        parts += [ev[0].elapsed_time(ev[1]), ev[1].elapsed_time(ev[2]), ev[2].elapsed_time(ev[3])]
+    t1.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    clk = clocks.stop() if clocks else None
+    step_ms = max_over_ranks(t0.elapsed_time(t1) / steps, world)
+    parts = [max_over_ranks(x / steps, world) for x in parts]
+    st_s, st_a, skipped = int(s_status.item()), int(a_status.item()), _lib.skipped_pairs(dev, reset=True)
+
+    # end to end: this step's pair lists, block tables, queries and masks from pinned host
+    # memory; search ids and the skipped-pair count back to the host
+    hq_host = queries.cpu().pin_memory()
+    hmask = torch.from_numpy(masks).pin_memory()
+    hres = torch.empty(C5_REQ, S_K, dtype=torch.int64).pin_memory()
+    hskip = torch.empty(1, dtype=torch.int64).pin_memory()
+    h2d = (sum(h.numel() * h.element_size() for h in host_pos) + sum(h.numel() * 4 for h in host_bt)
+           + hq_host.numel() * 4 + hmask.numel())
+
+    def e2e_step():
+        queries.copy_(hq_host, non_blocking=True)
+        for h, d_ in zip(host_pos, dev_pos):
+            d_.copy_(h, non_blocking=True)
+        for h, d_ in zip(host_bt, dev_bt):
+            d_.copy_(h, non_blocking=True)
+        mask_d.copy_(hmask, non_blocking=True)
+        r_, c_ = tk.mask_to_rows(mask_d)
+        cosine_topk_async(m.emb, m.emb16, m.valid, m.stats, queries, S_K, S_THR, status=s_status,
+                          workspace_owner=m, out=s_out)
+        rc.inject_donors(cache, inj, rope_base=C5_THETA, rotary_style="neox")
+        for _ in range(C5_L):
+            tk.gqa_partial_attention(q, k, v, r_, c_, out, max_rows=s_max, status=a_status)
+        hres.copy_(s_out[0], non_blocking=True)
+        hskip.copy_(err, non_blocking=True)
+
+    e2e_step()
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / steps, world)
+
+    inj_bytes = algorithmic_bytes(n_pairs, C5_L, hkv, C5_D, 2, int(nblk.sum()))
+    attn_flops = C5_L * attention_flops(masks, hq, C5_D)
+    search_flops = 2.0 * C5_SEARCH_ROWS * C5_REQ * S_DIM
+    del cache, pool, q, k, v, out
+    torch.cuda.empty_cache()
+    if rank != 0:
+        return None
+    pk = peaks()
+    tokens = int(req_len.sum())
+    return {
+        "metric": "c5 reuse step ms (search + inject + 80-layer partial attention), one TP-8 rank",
+        "value": round(step_ms, 3),
+        "unit": "ms",
+        "higher_is_better": False,
+        "n_gpus": world,
+        "scaling": "weak",
+        "steps": steps,
+        "config": {"workload": f"c5: Llama-3-70B geometry (80 L, 64 q / 8 KV heads, D 128, theta 5e5, bf16), "
+                               f"TP 8 -> {hq} q heads / {hkv} KV head per rank; {C5_REQ} requests, lognormal "
+                               f"lengths (median 8K, 4K-32K; {tokens:,} tokens), 2-4 donors each from a pool of "
+                               f"{C5_POOL} at 256-token chunks, 10-20% recompute (last chunk always); search "
+                               f"{C5_SEARCH_ROWS:,} x 384, 64 queries, top-8",
+                   "pairs": n_pairs, "descriptors": len(inj), "compute_rows": int(masks.sum()),
+                   "attention_operands": "one layer's dense Q/K/V reused by the 80 layer launches",
+                   "status": {"search": st_s, "attention": st_a, "skipped_pairs": skipped}},
+        "components_ms": {"search": round(parts[0], 4), "inject": round(parts[1], 4),
+                          "attention_80_layers": round(parts[2], 3)},
+        "roofline": {
+            "search": {"bound": "tensor", "achieved": round(search_flops / (parts[0] * 1e-3) / 1e12, 1),
+                       "unit": "TFLOP/s", "frac": round(search_flops / (parts[0] * 1e-3) / 1e12 / pk["bf16_tflops"], 4)},
+            "inject": {"bound": "hbm", "achieved": round(inj_bytes / (parts[1] * 1e-3) / 1e9, 1), "unit": "GB/s",
+                       "frac": round(inj_bytes / (parts[1] * 1e-3) / 1e9 / pk["hbm_gbs"], 4),
+                       "algorithmic_bytes": inj_bytes},
+            "attention": {"bound": "tensor", "achieved": round(attn_flops / (parts[2] * 1e-3) / 1e12, 1),
+                          "unit": "TFLOP/s",
+                          "frac": round(attn_flops / (parts[2] * 1e-3) / 1e12 / pk["bf16_tflops"], 4),
+                          "flops": attn_flops},
+            "peak_source": pk["source"]},
+        "e2e": {"value": round(e2e_ms, 3), "unit": "ms", "h2d_bytes_per_step": int(h2d),
+                "d2h_bytes_per_step": C5_REQ * S_K * 8 + 8},
+        "gpu_launches": steps * (3 + 1 + C5_L),
+        "clocks": clk,
+    }
+
+
+# ---------------------------------------------------------------------------
 # CPU baseline (oracle port of the reference's inject) — bounded sample
 # ---------------------------------------------------------------------------
 def inject_config(n_req: int, n_layers: int, world: int, n_pairs: int | None) -> dict:
@@ -808,7 +1044,7 @@ def main() -> int:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-components", action="store_true", help="skip the search / attention components")
-    ap.add_argument("--only", choices=["all", "search", "attention"], default="all",
+    ap.add_argument("--only", choices=["all", "search", "attention", "c5"], default="all",
                     help="print only that component's line")
     ap.add_argument("--attn-batch", type=int, default=A_B, help="attention batch (c4: 4)")
     ap.add_argument("--attn-seq", type=int, default=A_S, help="attention context (c4: 32768)")
@@ -825,9 +1061,11 @@ def main() -> int:
             print(json.dumps(line), flush=True)
         return 0
     world, rank, local = dist_setup(args.gpus)
-    if args.only in ("search", "attention"):
+    if args.only in ("search", "attention", "c5"):
         if args.only == "search" and world > 1:
             res = run_search_sharded(args, world, rank, local)
+        elif args.only == "c5":
+            res = run_c5(args, world, rank, local)
         elif rank == 0:
             res = run_search(args, local) if args.only == "search" else run_attention(args, local)
         else:
@@ -846,10 +1084,14 @@ def main() -> int:
             line["cpu_baseline"] = cpu_baseline()
         if world == 1 and not args.no_components:
             line["components"] = {"search": run_search(args, local), "attention": run_attention(args, local)}
+    if not args.no_components:
+        c5 = run_c5(args, world, rank, local)
+        if line is not None:
+            line.setdefault("components", {})["c5_step"] = c5
     if world > 1 and not args.no_components:
         comp = run_search_sharded(args, world, rank, local)
         if line is not None:
-            line["components"] = {"search": comp}
+            line.setdefault("components", {})["search"] = comp
     if line is not None:
         print(json.dumps(line), flush=True)
     if world > 1:
