@@ -23,6 +23,8 @@
 // CUDA-core path: any head_dim <= 256 and fp32 (the reference's own dtype in
 // its tests), one CTA per (row, head), fp32 online softmax with expf.
 #include <algorithm>
+#include <atomic>
+#include <mutex>
 #include <cmath>
 
 #include "common.cuh"
@@ -85,7 +87,16 @@ struct AttnParams {
   int64_t n_units;
   float scale_log2;
   int *status;
+  unsigned *sched;  // [next unit, CTAs finished] of this launch's scheduler slot
 };
+
+// Work units are handed out dynamically (longest first): each CTA's producer
+// thread takes the next unit index with an atomic add on a per-launch counter
+// pair in device memory.  A launch takes one of kSchedSlots slots (round robin
+// on the host); the last CTA to finish resets its slot, so up to kSchedSlots
+// launches may be in flight on a device at once.
+constexpr int kSchedSlots = 64;
+__device__ unsigned g_attn_sched[kSchedSlots * 2];
 
 // A work unit is two consecutive row tiles of one (batch element, KV group).
 struct Unit {
@@ -152,6 +163,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t *final_bar = bars + 21;
   uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 22);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(bars + 23);
+  uint64_t *unit_full = bars + 24;             // [2] unit ring: producer -> MMA + softmax warps
+  uint64_t *unit_empty = bars + 26;            // [2]
+  volatile int *unit_ring = reinterpret_cast<volatile int *>(bars + 28);  // [2]
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   if (threadIdx.x == 0) {
@@ -172,6 +186,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     tc::mbar_init(q_empty, 1);
     tc::mbar_init(final_bar, 1);
+    for (int i = 0; i < 2; ++i) {
+      tc::mbar_init(&unit_full[i], 1);
+      tc::mbar_init(&unit_empty[i], 1 + 8);  // the MMA thread and the 8 softmax warps
+    }
     *abort_flag = 0;
     tc::fence_mbar_init();
   }
@@ -186,6 +204,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   const tc::Abort ab{abort_flag, P.status};
   volatile int never = 0;
   const tc::Abort drain{&never, nullptr};
+  // n-th unit of this CTA (-1: no more work).  A whole warp (softmax) reads
+  // the slot before lane 0 releases it; the single MMA thread releases it itself.
+  auto pop_unit = [&](uint32_t n, bool whole_warp) -> int {
+    if (!tc::mbar_wait(&unit_full[n & 1], (n >> 1) & 1, ab, 5, kWaitCycles)) return -1;
+    const int u = unit_ring[n & 1];
+    if (whole_warp) __syncwarp();
+    if (!whole_warp || (threadIdx.x & 31) == 0) tc::mbar_arrive(&unit_empty[n & 1]);
+    return u;
+  };
 
   if (warp >= 8) {
    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kControlRegs));
@@ -194,11 +221,25 @@ __global__ void __launch_bounds__(kThreads, 1)
       // ------------------------------ TMA producer ------------------------------
       tc::tma_prefetch_desc(&tmK);
       tc::tma_prefetch_desc(&tmV);
-      uint32_t gl = 0;
+      uint32_t gl = 0, pushed = 0;
       bool ok = true, vfail = false;
-      for (int64_t u = blockIdx.x; u < P.n_units && ok; u += gridDim.x) {
+      auto push_unit = [&](int u) -> bool {
+        const uint32_t slot = pushed & 1, use = pushed >> 1;
+        if (use > 0 && !tc::mbar_wait(&unit_empty[slot], (use - 1) & 1, ab, 2, kWaitCycles)) return false;
+        unit_ring[slot] = u;
+        tc::mbar_arrive(&unit_full[slot]);
+        ++pushed;
+        return true;
+      };
+      while (ok) {
+        const int64_t u = atomicAdd(P.sched, 1u);
+        if (u >= P.n_units) break;
         Unit w;
         if (!decode_unit(P, u, w)) continue;
+        if (!push_unit((int)u)) {
+          ok = false;
+          break;
+        }
         const int nb = max(w.nblk[0], w.nblk[1]);
         for (int j = 0; j < nb; ++j) {
           const uint32_t ks = gl % kKStages, kph = (gl / kKStages) & 1;
@@ -223,6 +264,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc::tma_load_4d(v_dst + kHalfTile, &tmV, &v_full[vs], 64, j * kBN, w.g, w.b);
         }
       }
+      if (ok) push_unit(-1);
       // every load this thread issued lands before the CTA can exit (the V load
       // of the last counted block is missing when its slot wait gave up)
       const uint32_t nk = gl < (uint32_t)kKStages ? gl : (uint32_t)kKStages;
@@ -258,9 +300,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                             (kb | kk) != 0);
         tc::mma_commit(&s_full[t]);
       };
-      for (int64_t u = blockIdx.x; u < P.n_units && ok; u += gridDim.x) {
+      for (uint32_t n = 0; ok; ++n) {
+        const int u = pop_unit(n, false);
+        if (u < 0) break;
         Unit w;
-        if (!decode_unit(P, u, w)) continue;
+        decode_unit(P, u, w);
         const int nb = max(w.nblk[0], w.nblk[1]);
         if (!tc::mbar_wait(&q_full[0], qi & 1, ab, 3, kWaitCycles) ||
             !tc::mbar_wait(&q_full[1], qi & 1, ab, 3, kWaitCycles))
@@ -350,14 +394,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t sc = 0, oc = 0, qi = 0;  // S blocks seen, O finals seen, units seen
     bool ok = true;
     const bool neg_scale = P.scale_log2 < 0.f;
-    for (int64_t u = blockIdx.x; u < P.n_units && ok; u += gridDim.x) {
+    for (uint32_t n = 0; ok; ++n) {
+      const int u = pop_unit(n, true);
+      if (u < 0) break;
       Unit w;
-      if (!decode_unit(P, u, w)) continue;
+      decode_unit(P, u, w);
       const int hh = m / P.Pt, pi = m - hh * P.Pt;
       const bool valid = hh < P.G && pi < w.n_rows[t];
       const int pos = valid ? P.rows[(int64_t)w.b * P.rows_sb + w.r0 + t * P.Pt + pi] : -1;
       const int head = w.g * P.G + hh;
       // gather this row of Q into the 128-byte-swizzled K-major tile (zeros for unused rows)
+      if (t == 0 && quarter == 2 && lane == 0) SB_TRACE(22, qi);
       if (qi > 0 && !tc::mbar_wait(q_empty, (qi - 1) & 1, ab, 4, kWaitCycles)) break;
       {
         uint8_t *q_tile = sQ + t * kTileBytes;
@@ -505,6 +552,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int i = 0; i < 4; ++i) dst[c / 8 + i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
         }
       }
+      if (t == 0 && quarter == 2 && lane == 0) SB_TRACE(23, qi - 1);
       tc::fence_before_sync();
     }
   }
@@ -513,6 +561,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc::fence_after_sync();
   if (warp == 9) tc::tmem_dealloc(tmem, 512);
+  if (threadIdx.x == 0) {
+    // every producer of this launch has stopped taking units once all CTAs got here
+    __threadfence();
+    if (atomicAdd(P.sched + 1, 1u) == gridDim.x - 1) {
+      P.sched[0] = 0;
+      P.sched[1] = 0;
+      __threadfence();
+    }
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -618,6 +675,33 @@ int sm_count() {
   return n > 0 ? n : 148;
 }
 
+// This launch's scheduler counter pair on the current device (the symbol's
+// address is looked up once per device, with that device current).
+unsigned *sched_slot() {
+  static std::mutex mu;
+  static unsigned *base[64] = {};
+  static std::atomic<unsigned> next{0};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess || dev < 0 || dev >= 64) {
+    set_last_cuda_error(e);
+    return nullptr;
+  }
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (base[dev] == nullptr) {
+      void *p = nullptr;
+      e = cudaGetSymbolAddress(&p, g_attn_sched);
+      if (e != cudaSuccess) {
+        set_last_cuda_error(e);
+        return nullptr;
+      }
+      base[dev] = static_cast<unsigned *>(p);
+    }
+  }
+  return base[dev] + 2 * (next.fetch_add(1) % kSchedSlots);
+}
+
 template <typename T>
 int launch_tc(const sb_attn_tensor &k, const sb_attn_tensor &v, const AttnParams &P, CUtensorMapDataType dt,
               cudaStream_t st) {
@@ -633,9 +717,12 @@ int launch_tc(const sb_attn_tensor &k, const sb_attn_tensor &v, const AttnParams
     set_last_cuda_error(e);
     return SB_ERR_CUDA;
   }
+  AttnParams Pl = P;
+  Pl.sched = sched_slot();
+  if (Pl.sched == nullptr) return SB_ERR_CUDA;
   const int grid = (int)std::min<int64_t>(sm_count(), P.n_units);
   const int slot = prof_before(st);
-  attn_tc_kernel<T><<<grid, kThreads, kSmemBytes, st>>>(tk, tv, P);
+  attn_tc_kernel<T><<<grid, kThreads, kSmemBytes, st>>>(tk, tv, Pl);
   prof_after(slot, st);
   return launch_status();
 }
