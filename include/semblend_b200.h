@@ -279,7 +279,11 @@ SB_API int sb_mask_to_rows(const uint8_t *mask, int64_t mask_stride, int32_t bat
  * head_dim 128 run on the tensor cores (fp32 accumulation and softmax);
  * other head dims (<= 256) and fp32 run on CUDA cores.  *status (device
  * int32, zeroed by the caller) receives a value >= 2 if a kernel wait timed
- * out.
+ * out.  The tensor-core kernel hands out its work units from a counter pair
+ * inside the library (one of 64 per device, taken round robin per call and
+ * reset by the call's last CTA): at most 64 calls may be in flight on one
+ * device at a time, and the first call on a device looks the counters up
+ * (make it before any stream capture).
  *
  * Replaces partial_prefill_attention (semblend_core/triton_kernels.py:655-734;
  * kernel :532-652), which has the same math for n_q_heads == n_kv_heads and
