@@ -105,10 +105,22 @@ struct Unit {
   int nblk[2];
 };
 
+// Unit order: windows of kUnitWindow consecutive row-tile pairs, last window
+// first (longest units first); inside a window every (batch, KV group) takes
+// its kUnitWindow pairs in a row, so CTAs running at the same time share a few
+// K/V streams in L2 instead of one per CTA.
+#ifndef SB_ATTN_UNIT_WINDOW
+#define SB_ATTN_UNIT_WINDOW 4
+#endif
+constexpr int kUnitWindow = SB_ATTN_UNIT_WINDOW;
+
 __device__ __forceinline__ bool decode_unit(const AttnParams &P, int64_t u, Unit &w) {
   const int64_t bg_all = (int64_t)P.B * P.Hkv;
-  const int tp = P.T_max - 1 - (int)(u / bg_all);  // longest units first
-  const int bg = (int)(u % bg_all);
+  const int64_t per_window = bg_all * kUnitWindow;
+  const int64_t win = u / per_window, rem = u % per_window;
+  const int bg = (int)(rem / kUnitWindow);
+  const int tp = P.T_max - 1 - (int)(win * kUnitWindow + rem % kUnitWindow);
+  if (tp < 0) return false;
   w.b = bg / P.Hkv;
   w.g = bg % P.Hkv;
   w.r0 = tp * 2 * P.Pt;
@@ -799,7 +811,7 @@ extern "C" SB_API int sb_partial_attention(sb_attn_tensor q, sb_attn_tensor k, s
   if (tc_ok) {
     P.Pt = kBM / P.G;
     P.T_max = (max_rows + 2 * P.Pt - 1) / (2 * P.Pt);
-    P.n_units = (int64_t)P.T_max * batch * n_kv_heads;
+    P.n_units = (int64_t)((P.T_max + kUnitWindow - 1) / kUnitWindow) * kUnitWindow * batch * n_kv_heads;
     P.scale_log2 = scale * 1.4426950408889634f;
     if (dtype == SB_DTYPE_BF16) return launch_tc<__nv_bfloat16>(k, v, P, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, st);
     return launch_tc<__half>(k, v, P, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, st);

@@ -418,11 +418,96 @@ def inject_donors(
     del keep
 
 
+def inject_plan(
+    kv_cache: torch.Tensor | Sequence[torch.Tensor],
+    donor_kv,
+    block_table: torch.Tensor,
+    plan,
+    rope_base: float = 10000.0,
+    *,
+    mode: str = "delta",
+    rotary_style: str = "interleaved",
+    layout: str = "canonical",
+) -> int:
+    """Inject one request's donor rows for every partial layer of a
+    :class:`~semblend_b200.partial_attention.PartialAttentionPlan` in one launch.
+
+    The reference's hook converts the plan's per-layer position lists into
+    tensors and calls the inject once per layer (model_runner_hook.py:499-555);
+    here the plan is flattened once (:func:`~semblend_b200.partial_attention.plan_arrays`),
+    layers the plan recomputes in full are left untouched, and the remaining
+    layers are addressed through per-layer pointer tables, so no donor data is
+    copied.  ``kv_cache`` is ``[L, *per_layer]`` or a list of ``L`` per-layer
+    caches; ``donor_kv`` is ``[L, 2, H, S_donor, D]``, or for a multi-donor
+    plan a mapping ``donor_id -> [L, 2, H, S_donor, D]``.  Returns the number
+    of layers injected.
+    """
+    import numpy as np
+
+    from .partial_attention import plan_arrays
+
+    if mode not in _MODES:
+        raise ValueError(f"mode must be one of {tuple(_MODES)}, got {mode!r}")
+    arr = plan_arrays(plan)
+    layers = np.nonzero(~arr.recompute_layers)[0].tolist()
+    if not layers or arr.donor_positions.shape[0] == 0:
+        return 0
+    caches = list(kv_cache) if isinstance(kv_cache, (list, tuple)) else [kv_cache[i] for i in layers]
+    if isinstance(kv_cache, (list, tuple)):
+        caches = [caches[i] for i in layers]
+    first = caches[0]
+    _lib.require_cuda(first, "kv_cache")
+    dev = first.device
+    layout = _rows.resolve_layout(first, layout)
+    bt = _rows.device_index_tensor(block_table, dev, "block_table")
+    dst, g, keep = _rows.paged_rows(caches, bt, layout, has_layer_dim=False)
+    keep.append(bt)
+    _, _, nh, _, hd = g
+    # group the reuse pairs by donor (one descriptor each)
+    if isinstance(donor_kv, torch.Tensor):
+        groups = {None: (donor_kv, np.arange(arr.donor_positions.shape[0]))}
+    else:
+        owner = dict(plan.donor_map)
+        ids = np.array([owner.get(int(t)) for t in arr.target_positions], dtype=object)
+        groups = {d: (donor_kv[d], np.nonzero(ids == d)[0]) for d in dict.fromkeys(ids.tolist())}
+    descs = []
+    for _, (dk, idx) in groups.items():
+        if idx.shape[0] == 0:
+            continue
+        if dk.ndim != 5 or dk.shape[1:3] != (2, nh) or dk.shape[-1] != hd or dk.shape[0] <= max(layers):
+            raise ValueError(f"donor_kv shape {tuple(dk.shape)} does not match the cache ({nh} heads, D={hd}) "
+                             f"and layers up to {max(layers)}")
+        if dk.dtype != first.dtype:
+            raise TypeError(f"donor_kv dtype {dk.dtype} differs from kv_cache dtype {first.dtype}")
+        _lib.require_cuda(dk, "donor_kv")
+        per_layer = [dk[i] for i in layers]
+        src = _donor_rows(per_layer[0], False)
+        table = _rows._layer_ptr_table(per_layer, dev)
+        src.layer_ptrs = table.data_ptr()
+        keep += per_layer + [table]
+        pair_idx = torch.from_numpy(idx)
+        sp = torch.from_numpy(arr.donor_positions)[pair_idx].to(dev)
+        tp = torch.from_numpy(arr.target_positions)[pair_idx].to(dev)
+        keep += [sp, tp]
+        descs.append(_pair_desc(src, dst, sp, tp, _lib.SB_ROW_AT_SRC_POS, _lib.SB_ROW_AT_DST_POS))
+    if not descs:
+        return 0
+    p = _rows.params(
+        n_layers=len(layers), n_heads=nh, head_dim=hd, dtype=first.dtype, rotary_style=rotary_style,
+        k_angle=_MODES[mode], kv_select=_lib.SB_KV_BOTH,
+        inv_freq=_lib.inv_freq(rope_base, hd, dev) if mode != "copy" else None,
+    )
+    _launch(descs, p, dev, "inject_plan")
+    del keep
+    return len(layers)
+
+
 __all__ = [
     "HAS_TRITON",
     "DonorInjection",
     "apply_rope_delta_inplace",
     "inject_donors",
+    "inject_plan",
     "nope_permute_paged_kv",
     "permute_paged_kv_with_rope",
     "rope_correct_k",

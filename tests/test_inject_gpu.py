@@ -340,3 +340,63 @@ def test_inject_donors_matches_per_layer_oracle(as_list, mode):
             torch.testing.assert_close(got[layer].float(), want[layer].float(), atol=2e-2, rtol=2e-2)
         else:
             _split_check(got[layer], want[layer], style="neox")
+
+
+def _plan_case(seed, multi):
+    """A plan over 6 layers (layers 1 and 4 recomputed in full) with reused and
+    recomputed target positions, one donor or three."""
+    from semblend_b200 import partial_attention as pa
+
+    rng = np.random.default_rng(seed)
+    L, target_len = 6, 300
+    hints = [{"recomputeAll": layer in (1, 4)} for layer in range(L)]
+    donors = {"a": 180, "b": 260, "c": 120} if multi else {"a": 280}
+    actions, reuse = [], []
+    for t in rng.permutation(target_len)[:250].tolist():
+        if rng.random() < 0.8:
+            did = str(rng.choice(list(donors)))
+            dpos = int(rng.integers(0, donors[did]))
+            act = {"action": "copy_from_donor", "targetPos": t, "donorPos": dpos}
+            if multi:
+                act["donorId"] = did
+            actions.append(act)
+            reuse.append((did, dpos, t))
+        else:
+            actions.append({"action": "recompute" if multi else "placeholder", "targetPos": t})
+    if multi:
+        plan = pa.build_multi_donor_attention_plan(target_len, actions, hints, L)
+    else:
+        copy = [t for _, _, t in reuse]
+        plan = pa.build_attention_plan("a", target_len, donors["a"], copy, [], actions, hints, L)
+    return plan, donors, reuse, L
+
+
+@pytest.mark.parametrize("multi", [False, True])
+@pytest.mark.parametrize("as_list", [False, True])
+def test_inject_plan_one_launch_matches_per_layer_oracle(multi, as_list):
+    plan, donor_lens, reuse, L = _plan_case(21 + multi, multi)
+    g = torch.Generator().manual_seed(22)
+    H, D, bs, nb = 2, 128, 16, 40
+    cache = torch.randn(L, nb, 2, H, bs, D, generator=g).to(torch.bfloat16)
+    bt = torch.randperm(nb, generator=g)[: (300 + bs - 1) // bs].to(torch.int32)
+    donors = {k: torch.randn(L, 2, H, n, D, generator=g).to(torch.bfloat16) for k, n in donor_lens.items()}
+    want = cache.clone()
+    for did in donors:
+        d = torch.tensor([dp for x, dp, _ in reuse if x == did], dtype=torch.int32)
+        t = torch.tensor([tp for x, _, tp in reuse if x == did], dtype=torch.int32)
+        for layer in range(L):
+            if layer in (1, 4):
+                continue
+            want[layer] = orope.rope_correct_scatter_paged(want[layer], donors[did][layer], bt, d, t, 5e5, "neox")
+    c = cache.to(DEV)
+    kv = [c[layer] for layer in range(L)] if as_list else c
+    dk = {k: v.to(DEV) for k, v in donors.items()} if multi else donors["a"].to(DEV)
+    n = rc.inject_plan(kv, dk, bt.to(DEV), plan, rope_base=5e5, rotary_style="neox")
+    assert n == L - 2
+    got = c.cpu()
+    for layer in range(L):
+        if layer in (1, 4):
+            assert torch.equal(got[layer], cache[layer])  # recomputed in full: untouched
+        else:
+            assert torch.equal(got[layer][:, 1], want[layer][:, 1])
+            assert_rope_close(got[layer][:, 0].contiguous(), want[layer][:, 0].contiguous(), "neox")
