@@ -113,6 +113,100 @@ class ShardedDonorMatrix:
         ids, scores = self._merge(all_ids, all_sc)
         return ids, scores, status
 
+    def search_batches(self, batches, k: int, min_similarity: float, capacity: int = DEFAULT_CAPACITY,
+                       on_result=None) -> list[tuple[torch.Tensor, torch.Tensor, torch.Tensor]]:
+        """Search a sequence of query batches with two in flight, without a
+        host synchronisation: batch i's all-gather and merge run on a second
+        stream while batch i+1 is searched on the current one (the exchange
+        needs few SMs and hides behind the screening kernel).  Returns
+        ``(ids, scores, status [W])`` per batch, ready on the current stream.
+        ``on_result(i, ids, scores)``, if given, is called on the exchange
+        stream right after batch i is merged (e.g. to queue its copy to the
+        host).  Batches in pinned host memory are copied to the device on a
+        third stream, each copy overlapping the previous batch's search.
+        """
+        batches = list(batches)
+        if self.world == 1 or self._local_search is not None:
+            out = []
+            for i, q in enumerate(batches):
+                r = self.search_async(q, k, min_similarity, capacity=capacity)
+                if on_result is not None:
+                    on_result(i, r[0], r[1])
+                out.append(r)
+            return out
+        m = self.local
+        dev = m.device
+        cur = torch.cuda.current_stream(dev)
+        if getattr(self, "_xstream", None) is None:
+            self._xstream = torch.cuda.Stream(dev)
+        xs = self._xstream
+        kk = int(k)
+        results = []
+        sends, recvs, ready, done = [], [], [], []
+        # host batches: copied on a copy stream into two device buffers, each copy
+        # overlapping the previous batch's search
+        host = batches and batches[0].device.type == "cpu"
+        if host:
+            if getattr(self, "_cstream", None) is None:
+                self._cstream = torch.cuda.Stream(dev)
+            cs = self._cstream
+            qbufs = [torch.empty(batches[0].shape, dtype=torch.float32, device=dev) for _ in range(2)]
+            copied = [torch.cuda.Event() for _ in range(2)]
+            consumed = [torch.cuda.Event() for _ in range(2)]
+
+            def stage(j):
+                with torch.cuda.stream(cs):
+                    if j >= 2:
+                        cs.wait_event(consumed[j % 2])
+                    qbufs[j % 2].copy_(batches[j], non_blocking=True)
+                    copied[j % 2].record(cs)
+
+            stage(0)
+        for i, q in enumerate(batches):
+            if host:
+                if i + 1 < len(batches):
+                    stage(i + 1)
+                cur.wait_event(copied[i % 2])
+                q = qbufs[i % 2]
+            nq = q.shape[0]
+            qk, rec = nq * kk, self._record_bytes(nq, kk)
+            slot = i % 2
+            if len(sends) <= slot:
+                sends.append(torch.empty(rec, dtype=torch.uint8, device=dev))
+                recvs.append(torch.empty(self.world * rec, dtype=torch.uint8, device=dev))
+                ready.append(torch.cuda.Event())
+                done.append(torch.cuda.Event())
+            send, recv = sends[slot], recvs[slot]
+            if send.numel() < rec:
+                raise ValueError("search_batches needs batches of one shape")
+            if i >= 2:
+                cur.wait_event(done[slot])  # the exchange of batch i - 2 has read this slot
+            ids_v = send[: 8 * qk].view(torch.int64).view(nq, kk)
+            sc_v = send[8 * qk : 12 * qk].view(torch.float32).view(nq, kk)
+            st_v = send[12 * qk : 12 * qk + 4].view(torch.int32)
+            qd = q.to(device=dev, dtype=torch.float32).contiguous()
+            cosine_topk_async(m.emb, m.emb16, m.valid, m.stats, qd, kk, min_similarity, n_rows=self.n_local,
+                              id_offset=self.row_begin, capacity=capacity, status=st_v, workspace_owner=m,
+                              out=(ids_v, sc_v))
+            if host:
+                consumed[i % 2].record(cur)
+            ready[slot].record(cur)
+            with torch.cuda.stream(xs):
+                xs.wait_event(ready[slot])
+                dist.all_gather_into_tensor(recv[: self.world * rec], send[:rec], group=self.group)
+                table = recv[: self.world * rec].view(self.world, rec)
+                ids, scores = self._merge(table[:, : 8 * qk].view(torch.int64).view(self.world, nq, kk),
+                                          table[:, 8 * qk : 12 * qk].view(torch.float32).view(self.world, nq, kk))
+                status = table[:, 12 * qk : 12 * qk + 4].view(torch.int32).reshape(self.world).clone()
+                if on_result is not None:
+                    on_result(i, ids, scores)
+                done[slot].record(xs)
+            for t in (ids, scores, status):
+                t.record_stream(cur)
+            results.append((ids, scores, status))
+        cur.wait_stream(xs)
+        return results
+
     def search(self, queries: torch.Tensor, k: int, min_similarity: float,
                capacity: int = DEFAULT_CAPACITY) -> tuple[torch.Tensor, torch.Tensor]:
         """Global top-``k`` (ids, similarities) ``[Q, k]``, identical on every rank.

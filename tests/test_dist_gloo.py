@@ -70,6 +70,9 @@ def _worker(rank, world, port, mode, result_path):
         if mode == "die" and rank == 1:
             os._exit(3)  # leaves without joining the collective
         ids, sc = m.search(torch.from_numpy(Q), 5, 0.5)
+        batched = m.search_batches([torch.from_numpy(Q)] * 2, 5, 0.5)
+        for bi, bs, bst in batched:
+            assert torch.equal(bi, ids) and torch.equal(bs, sc) and int(bst.abs().sum()) == 0
         if rank == 0:
             torch.save({"ids": ids, "scores": sc}, result_path)
         dist.destroy_process_group()
