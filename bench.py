@@ -368,8 +368,7 @@ def run_search(args, local: int) -> dict:
     assert int(status.item()) == 0, f"search status {int(status.item())}"
     steps = max(5, args.steps // 10)
     stream = torch.cuda.current_stream(dev)
-    clocks = ClockSampler(local)
-    clocks.start()
+    # eager launches: the screening kernel's own time (library-recorded events)
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with _lib.KernelTimer(steps) as kt:
         t0.record(stream)
@@ -377,6 +376,21 @@ def run_search(args, local: int) -> dict:
             step(queries)
         t1.record(stream)
         torch.cuda.synchronize(dev)
+    eager_ms = t0.elapsed_time(t1) / steps
+    # the step as one CUDA graph (query preparation, screening, rescoring), as a serving loop runs it
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step(queries)
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize(dev)
+    clocks = ClockSampler(local)
+    clocks.start()
+    t0.record(stream)
+    for _ in range(steps):
+        graph.replay()
+    t1.record(stream)
+    torch.cuda.synchronize(dev)
     clk = clocks.stop()
     st = int(status.item())
     ms = t0.elapsed_time(t1) / steps
@@ -386,10 +400,14 @@ def run_search(args, local: int) -> dict:
     dq = torch.empty_like(queries)
     hi = torch.empty(S_QUERIES, S_K, dtype=torch.int64).pin_memory()
     hs = torch.empty(S_QUERIES, S_K, dtype=torch.float32).pin_memory()
+    graph_e2e = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph_e2e):
+        step(dq)
 
     def e2e_step():
         dq.copy_(hq, non_blocking=True)
-        i, s, _ = step(dq)
+        graph_e2e.replay()
+        i, s = out
         hi.copy_(i, non_blocking=True)
         hs.copy_(s, non_blocking=True)
 
@@ -438,7 +456,8 @@ def run_search(args, local: int) -> dict:
         "config": {"workload": f"c3{'' if n_rows == S_ROWS else ' (reduced)'}: {n_rows:,} x 384 fp32 donors "
                                "(256 clusters, sigma 0.3, L2-normalised), 4096 queries (70% clustered, 30% "
                                "uniform), top-8, threshold 0.60",
-                   "fill": round(hits, 4), "status": st,
+                   "fill": round(hits, 4), "status": st, "eager_launch_ms": round(eager_ms, 4),
+                   "step": "one CUDA graph per step (query preparation, screening, rescoring)",
                    "candidates_per_query": {"mean": round(float(cand.mean()), 1), "max": int(cand.max())}},
         "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
                      "frac": round(achieved / pk["bf16_tflops"], 4), "peak_source": pk["source"],

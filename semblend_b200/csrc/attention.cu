@@ -216,6 +216,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const tc::Abort ab{abort_flag, P.status};
   volatile int never = 0;
   const tc::Abort drain{&never, nullptr};
+  pdl_wait();  // everything the previous kernel on this stream writes is visible from here on
   // n-th unit of this CTA (-1: no more work).  A whole warp (softmax) reads
   // the slot before lane 0 releases it; the single MMA thread releases it itself.
   auto pop_unit = [&](uint32_t n, bool whole_warp) -> int {
@@ -569,6 +570,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
 
+  pdl_launch_dependents();
   tc::fence_before_sync();
   __syncthreads();
   tc::fence_after_sync();
@@ -724,18 +726,18 @@ int launch_tc(const sb_attn_tensor &k, const sb_attn_tensor &v, const AttnParams
       !make_tmap_4d(&tv, dt, v.data, kD, P.S, P.Hkv, P.B, v.stride_seq * es, v.stride_head * es,
                     v.stride_batch * es, 64, kBN))
     return SB_ERR_CUDA;
-  cudaError_t e = cudaFuncSetAttribute(attn_tc_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-  if (e != cudaSuccess) {
-    set_last_cuda_error(e);
-    return SB_ERR_CUDA;
-  }
+  if (ensure_dynamic_smem(reinterpret_cast<const void *>(attn_tc_kernel<T>), kSmemBytes) != SB_OK) return SB_ERR_CUDA;
   AttnParams Pl = P;
   Pl.sched = sched_slot();
   if (Pl.sched == nullptr) return SB_ERR_CUDA;
   const int grid = (int)std::min<int64_t>(sm_count(), P.n_units);
   const int slot = prof_before(st);
-  attn_tc_kernel<T><<<grid, kThreads, kSmemBytes, st>>>(tk, tv, Pl);
+  const cudaError_t e = launch_pdl(attn_tc_kernel<T>, dim3(grid), dim3(kThreads), kSmemBytes, st, tk, tv, Pl);
   prof_after(slot, st);
+  if (e != cudaSuccess) {
+    set_last_cuda_error(e);
+    return SB_ERR_CUDA;
+  }
   return launch_status();
 }
 

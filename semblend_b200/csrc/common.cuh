@@ -22,6 +22,41 @@ inline int launch_status() {
   return SB_OK;
 }
 
+// Programmatic dependent launch (off by default: measured neutral on one GPU
+// and slower when an NCCL exchange of a pipelined search runs next to the
+// search kernels, whose early-launched CTAs then hold SMs while they wait).
+#ifndef SB_PDL
+#define SB_PDL 0
+#endif
+
+// Programmatic dependent launch: a kernel launched with launch_pdl may start
+// (prologue, TMEM allocation, barrier set-up) while the previous kernel on its
+// stream finishes; it must call pdl_wait() before touching anything that
+// kernel writes or reads.  pdl_launch_dependents() lets the next such kernel
+// be scheduled early.  Without a programmatic predecessor both are no-ops.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                              Args &&...args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = SB_PDL ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
+// cudaFuncSetAttribute(MaxDynamicSharedMemorySize) once per (kernel, device):
+// returns SB_OK or SB_ERR_CUDA.  Setting it on every call costs launch latency.
+int ensure_dynamic_smem(const void *func, int bytes);
+
 inline int elem_bytes(int dtype) {
   switch (dtype) {
     case SB_DTYPE_F32: return 4;

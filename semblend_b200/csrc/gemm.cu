@@ -278,11 +278,7 @@ int launch_tc(const T *x, int64_t ldx, const T *w, int64_t ldw, const T *bias, c
   P.rows = rows, P.bias = bias, P.out = out, P.ldo = ldo;
   P.idesc = tc::idesc_f16(kBM, kBN, fmt, 0);
   P.status = status;
-  cudaError_t e = cudaFuncSetAttribute(gemm_rows_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
-  if (e != cudaSuccess) {
-    set_last_cuda_error(e);
-    return SB_ERR_CUDA;
-  }
+  if (ensure_dynamic_smem(reinterpret_cast<const void *>(gemm_rows_kernel<T>), kSmem) != SB_OK) return SB_ERR_CUDA;
   const int grid = (int)std::min<int64_t>(sm_count(), (int64_t)P.m_tiles * P.n_tiles);
   const int slot = prof_before(st);
   gemm_rows_kernel<T><<<grid, kThreads, kSmem, st>>>(ta, tb, P);

@@ -1,4 +1,5 @@
 // Status strings, version, error bookkeeping and kernel timing of the C ABI.
+#include <map>
 #include <mutex>
 #include <vector>
 
@@ -124,3 +125,26 @@ extern "C" SB_API int sb_profile_stop(float *total_ms, int32_t *n_launches) {
   sb::g_prof_used = 0;
   return SB_OK;
 }
+
+namespace sb {
+int ensure_dynamic_smem(const void *func, int bytes) {
+  static std::mutex mu;
+  static std::map<std::pair<const void *, int>, int> done;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) {
+    set_last_cuda_error(e);
+    return SB_ERR_CUDA;
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = done.find({func, dev});
+  if (it != done.end() && it->second >= bytes) return SB_OK;
+  e = cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e != cudaSuccess) {
+    set_last_cuda_error(e);
+    return SB_ERR_CUDA;
+  }
+  done[{func, dev}] = bytes;
+  return SB_OK;
+}
+}  // namespace sb

@@ -113,6 +113,8 @@ __global__ void query_prep_kernel(const float *__restrict__ q, int64_t ld_q, int
                                   float *__restrict__ delta, int *__restrict__ count, int *__restrict__ lower,
                                   int q_blocks, const uint8_t *__restrict__ valid, int64_t n_rows,
                                   uint32_t *__restrict__ bits, int64_t n_words) {
+  pdl_wait();  // the previous search on this stream still reads this workspace
+  pdl_launch_dependents();
   if ((int)blockIdx.x >= q_blocks) {  // trailing blocks: the row-validity bitmask
     const int64_t w = (int64_t)(blockIdx.x - q_blocks) * blockDim.x + threadIdx.x;
     if (w < n_words) valid_bits_word(valid, n_rows, bits, w);
@@ -212,6 +214,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc::fence_after_sync();
   const uint32_t tmem = *tmem_holder;
   const tc::Abort ab{abort_flag, P.status};
+  pdl_wait();  // query preparation (the previous kernel) has finished and is visible
 
   if (warp == 0) {
     if (lane == 0) {
@@ -413,6 +416,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
 
+  pdl_launch_dependents();
   tc::fence_before_sync();
   __syncthreads();
   tc::fence_after_sync();
@@ -451,6 +455,8 @@ __global__ void __launch_bounds__(kRescoreWarps * 32, 4)
                    float *__restrict__ out_scores, int *status) {
   __shared__ __align__(16) float sq_all[kRescoreWarps][kMaxDim];
   __shared__ int queue_all[kRescoreWarps][kQueue];
+  pdl_wait();  // the screening kernel's candidates are complete and visible
+  pdl_launch_dependents();
   const int lane = threadIdx.x % 32, wib = threadIdx.x / 32;
   const int q = blockIdx.x * kRescoreWarps + wib;
   if (q >= nq) return;
@@ -705,16 +711,16 @@ void launch_rescore_kt(int t, unsigned grid, cudaStream_t st, const float *emb, 
                        int k, int nq, int64_t id_offset, int64_t *out_ids, float *out_scores, int *status) {
   const dim3 block(kRescoreWarps * 32);
   if (t == 1)
-    rescore_kernel<KT, 1><<<grid, block, 0, st>>>(emb, ld_emb, dim, qn, delta, count, cand, cap, thr, k, nq,
+    launch_pdl(rescore_kernel<KT, 1>, grid, block, 0, st, emb, ld_emb, dim, qn, delta, count, cand, cap, thr, k, nq,
                                                   id_offset, out_ids, out_scores, status);
   else if (t == 2)
-    rescore_kernel<KT, 2><<<grid, block, 0, st>>>(emb, ld_emb, dim, qn, delta, count, cand, cap, thr, k, nq,
+    launch_pdl(rescore_kernel<KT, 2>, grid, block, 0, st, emb, ld_emb, dim, qn, delta, count, cand, cap, thr, k, nq,
                                                   id_offset, out_ids, out_scores, status);
   else if (t == 3)
-    rescore_kernel<KT, 3><<<grid, block, 0, st>>>(emb, ld_emb, dim, qn, delta, count, cand, cap, thr, k, nq,
+    launch_pdl(rescore_kernel<KT, 3>, grid, block, 0, st, emb, ld_emb, dim, qn, delta, count, cand, cap, thr, k, nq,
                                                   id_offset, out_ids, out_scores, status);
   else
-    rescore_kernel<KT, 4><<<grid, block, 0, st>>>(emb, ld_emb, dim, qn, delta, count, cand, cap, thr, k, nq,
+    launch_pdl(rescore_kernel<KT, 4>, grid, block, 0, st, emb, ld_emb, dim, qn, delta, count, cand, cap, thr, k, nq,
                                                   id_offset, out_ids, out_scores, status);
 }
 
@@ -774,14 +780,14 @@ int sm_count() {
 template <int KT>
 int launch_screen(const CUtensorMap &tq, const CUtensorMap &te, const ScreenParams &P, int grid, int smem,
                   cudaStream_t st) {
-  cudaError_t e = cudaFuncSetAttribute(screen_kernel<KT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (ensure_dynamic_smem(reinterpret_cast<const void *>(screen_kernel<KT>), smem) != SB_OK) return SB_ERR_CUDA;
+  const int slot = prof_before(st);
+  const cudaError_t e = launch_pdl(screen_kernel<KT>, dim3(grid), dim3(kThreads), smem, st, tq, te, P);
+  prof_after(slot, st);
   if (e != cudaSuccess) {
     set_last_cuda_error(e);
     return SB_ERR_CUDA;
   }
-  const int slot = prof_before(st);
-  screen_kernel<KT><<<grid, kThreads, smem, st>>>(tq, te, P);
-  prof_after(slot, st);
   return launch_status();
 }
 
