@@ -318,6 +318,32 @@ SB_API int sb_masked_linear(const void *x, int64_t ldx, const void *w, int64_t l
                             void *workspace, int64_t workspace_bytes, int32_t *status, void *stream);
 
 /* ------------------------------------------------------------------------ */
+/* Chunk-hash alignment                                                     */
+/* ------------------------------------------------------------------------ */
+/* SHA-256 of every full chunk of `chunk` token ids (device int32 / int64,
+ * SB_INDEX_*), each id packed as a little-endian uint32; the first 128 bits of
+ * each digest as four big-endian words: digests[n_tokens / chunk][4].  A
+ * trailing partial chunk is not hashed.  Replaces _chunk_hash
+ * (semblend_core/alignment.py:120-130) over the chunks of
+ * compute_chunk_alignment (:170-180) and estimate_reuse_ratio (:752-774). */
+SB_API int sb_chunk_digests(const void *tokens, int32_t token_dtype, int64_t n_tokens, int32_t chunk,
+                            uint32_t *digests, void *stream);
+
+/* Exact chunk matching of compute_chunk_alignment (alignment.py:181-252):
+ * full target chunk t (in order) takes the first donor chunk with its digest
+ * that no earlier target chunk took; with context_gate != 0 a match survives
+ * only if target chunk t - 1 or t + 1 also matched.  Writes match[t] (device
+ * int32, donor chunk or -1) for the n_target_chunks full target chunks and
+ * the position pairs of the matched chunks in target order,
+ * donor_positions[i] / target_positions[i] (device int32, room for
+ * n_target_chunks * chunk entries), with their count in *n_pairs (device
+ * int64) — the inputs of sb_inject, built without the host. */
+SB_API int sb_chunk_align(const uint32_t *donor_digests, int32_t n_donor_chunks,
+                          const uint32_t *target_digests, int32_t n_target_chunks, int32_t chunk,
+                          int32_t context_gate, int32_t *match, int32_t *donor_positions,
+                          int32_t *target_positions, int64_t *n_pairs, void *stream);
+
+/* ------------------------------------------------------------------------ */
 /* Miscellaneous                                                            */
 /* ------------------------------------------------------------------------ */
 SB_API const char *sb_status_string(int status);

@@ -1,0 +1,163 @@
+"""Chunk-hash alignment of a target token sequence to a donor on the GPU.
+
+The reference aligns on the host (semblend_core/alignment.py, SemBlend 0.3.2):
+SHA-256 of every full chunk of token ids (:120-130), greedy exact matching of
+target chunks to donor chunks with an optional context gate (:133-268), and
+an expansion into one ``SlotAction`` object per position.  Here the hashes,
+the matching and the expansion into position pairs run on the device
+(``sb_chunk_digests``, ``sb_chunk_align``), so the pairs feed the inject kernel
+without visiting the host.  :func:`compute_chunk_alignment` keeps the
+reference's signature and result type for callers that want it (the
+``SlotAction`` list is built on the host from the device result).
+"""
+
+from __future__ import annotations
+
+import os
+from dataclasses import dataclass
+
+import torch
+
+from . import _lib
+
+DEFAULT_CHUNK_SIZE = 256
+# the reference's default (alignment.py:43): the context gate is on unless SEMBLEND_CONTEXT_GATE=0
+_CONTEXT_GATE_ENABLED = os.environ.get("SEMBLEND_CONTEXT_GATE", "1") != "0"
+
+
+def _tokens(t, device) -> torch.Tensor:
+    x = torch.as_tensor(t)
+    if x.dtype not in (torch.int32, torch.int64):
+        x = x.to(torch.int64)
+    if device is not None:
+        x = x.to(device, non_blocking=True)
+    return x.contiguous()
+
+
+def chunk_digests(tokens: torch.Tensor, chunk_size: int = DEFAULT_CHUNK_SIZE) -> torch.Tensor:
+    """First 128 bits of SHA-256 of every full chunk (token ids as little-endian
+    uint32), ``[n_full_chunks, 4]`` int32 holding the big-endian words."""
+    _lib.require_cuda(tokens, "tokens")
+    t = _tokens(tokens, None)
+    n = t.shape[0] // chunk_size
+    out = torch.empty(n, 4, dtype=torch.int32, device=t.device)
+    if n:
+        lib = _lib.load()
+        _lib.check(lib.sb_chunk_digests(t.data_ptr(), _lib.index_code(t.dtype), t.shape[0], chunk_size,
+                                        out.data_ptr(), _lib.stream_ptr(t.device)), "sb_chunk_digests")
+    return out
+
+
+@dataclass
+class DeviceAlignment:
+    """Device result of :func:`chunk_alignment`.
+
+    ``match [n_target_chunks]`` int32: donor chunk per target chunk (-1:
+    recompute; a trailing partial chunk is always -1).  ``donor_positions`` /
+    ``target_positions`` int32 hold the pairs of the matched chunks in target
+    order; the first ``n_pairs`` (a device int64 scalar) entries are valid.
+    """
+
+    match: torch.Tensor
+    donor_positions: torch.Tensor
+    target_positions: torch.Tensor
+    n_pairs: torch.Tensor
+    donor_len: int
+    target_len: int
+    chunk_size: int
+
+    def pairs(self) -> tuple[torch.Tensor, torch.Tensor]:
+        """The valid pairs (reads ``n_pairs``: one host synchronisation)."""
+        n = int(self.n_pairs.item())
+        return self.donor_positions[:n], self.target_positions[:n]
+
+
+def chunk_alignment(donor_tokens, target_tokens, chunk_size: int = DEFAULT_CHUNK_SIZE,
+                    context_gate: bool | None = None, device=None) -> DeviceAlignment:
+    """Exact chunk alignment on the device (compute_chunk_alignment's
+    matching, alignment.py:181-252), without a host synchronisation."""
+    gate = _CONTEXT_GATE_ENABLED if context_gate is None else bool(context_gate)
+    if device is None:
+        device = target_tokens.device if isinstance(target_tokens, torch.Tensor) and target_tokens.is_cuda else \
+            torch.device("cuda", torch.cuda.current_device())
+    d = _tokens(donor_tokens, device)
+    t = _tokens(target_tokens, device)
+    dd, td = chunk_digests(d, chunk_size), chunk_digests(t, chunk_size)
+    n_full = td.shape[0]
+    n_chunks = (t.shape[0] + chunk_size - 1) // chunk_size
+    match = torch.full((n_chunks,), -1, dtype=torch.int32, device=device)
+    dpos = torch.empty(max(n_full * chunk_size, 1), dtype=torch.int32, device=device)
+    tpos = torch.empty_like(dpos)
+    n_pairs = torch.zeros(1, dtype=torch.int64, device=device)
+    lib = _lib.load()
+    _lib.check(lib.sb_chunk_align(dd.data_ptr() if dd.shape[0] else None, dd.shape[0], td.data_ptr(), n_full,
+                                  chunk_size, int(gate), match.data_ptr(), dpos.data_ptr(), tpos.data_ptr(),
+                                  n_pairs.data_ptr(), _lib.stream_ptr(device)), "sb_chunk_align")
+    return DeviceAlignment(match, dpos, tpos, n_pairs, int(d.shape[0]), int(t.shape[0]), chunk_size)
+
+
+def estimate_chunk_reuse(donor_tokens, target_tokens, chunk_size: int = DEFAULT_CHUNK_SIZE, device=None) -> float:
+    """Chunk stage of estimate_reuse_ratio (alignment.py:752-774): matched
+    tokens / target length with greedy, ungated chunk matching.  (The
+    reference falls back to a token-multiset overlap when no chunk matches;
+    that fallback stays with the caller.)"""
+    a = chunk_alignment(donor_tokens, target_tokens, chunk_size, context_gate=False, device=device)
+    return float(a.n_pairs.item()) / max(a.target_len, 1)
+
+
+@dataclass(frozen=True)
+class SlotAction:
+    """The reference's SlotAction (alignment.py:100-104): ``action`` is
+    ``"copy_from_donor"`` or ``"recompute"``."""
+
+    action: str
+    target_pos: int
+    donor_pos: int | None = None
+
+
+@dataclass(frozen=True)
+class AlignmentResult:
+    """The fields of the reference's AlignmentResult (alignment.py:107-118) that
+    exact chunk alignment sets."""
+
+    reuse_ratio: float
+    slot_actions: list[SlotAction]
+    edit_distance: int
+    donor_len: int
+    target_len: int
+    fuzzy_chunks: int = 0
+    exact_chunks: int = 0
+
+
+def compute_chunk_alignment(donor_tokens, target_tokens, chunk_size: int = DEFAULT_CHUNK_SIZE,
+                            context_gate: bool | None = None) -> AlignmentResult:
+    """compute_chunk_alignment (alignment.py:133-268) with the hashing and
+    matching on the device; the per-position ``slot_actions`` are built on the
+    host from the chunk matches, as the reference returns them."""
+    a = chunk_alignment(donor_tokens, target_tokens, chunk_size, context_gate)
+    match = a.match.cpu().tolist()
+    actions: list[SlotAction] = []
+    n_reused = 0
+    for ti, di in enumerate(match):
+        t0 = ti * chunk_size
+        n = min(chunk_size, a.target_len - t0)
+        if di >= 0:
+            actions.extend(SlotAction("copy_from_donor", t0 + i, di * chunk_size + i) for i in range(n))
+            n_reused += n
+        else:
+            actions.extend(SlotAction("recompute", t0 + i) for i in range(n))
+    return AlignmentResult(reuse_ratio=n_reused / max(a.target_len, 1), slot_actions=actions,
+                           edit_distance=a.target_len - n_reused, donor_len=a.donor_len, target_len=a.target_len,
+                           exact_chunks=sum(1 for m in match if m >= 0))
+
+
+__all__ = [
+    "AlignmentResult",
+    "DEFAULT_CHUNK_SIZE",
+    "DeviceAlignment",
+    "SlotAction",
+    "chunk_alignment",
+    "chunk_digests",
+    "compute_chunk_alignment",
+    "estimate_chunk_reuse",
+]

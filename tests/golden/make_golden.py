@@ -238,6 +238,41 @@ def main() -> int:
         "pairs": [pa.compute_donor_kv_indices(plan, l) for l in range(3)],
     })
     (HERE / "plans.json").write_text(json.dumps(plans, indent=0))
+
+    # --- chunk-hash alignment (alignment.py:120-268, :741-787) ---
+    import semblend_core.alignment as al
+
+    def align_case(name, seed, chunk, n_donor_chunks, gate):
+        rng = np.random.default_rng(seed)
+        donor = rng.integers(0, 152064, n_donor_chunks * chunk + chunk // 3).astype(np.int64)
+        dch = [donor[i * chunk : (i + 1) * chunk] for i in range(n_donor_chunks)]
+        pieces = []
+        for i in range(n_donor_chunks + 6):
+            r = rng.random()
+            if r < 0.55:  # a donor chunk, anywhere
+                pieces.append(dch[int(rng.integers(0, n_donor_chunks))])
+            elif r < 0.65 and pieces:  # a repeat of an earlier target chunk
+                pieces.append(pieces[int(rng.integers(0, len(pieces)))])
+            else:  # new content
+                pieces.append(rng.integers(0, 152064, chunk))
+        target = np.concatenate(pieces + [rng.integers(0, 152064, chunk // 2)])
+        dl, tl = donor.tolist(), target.tolist()
+        res = al.compute_chunk_alignment(dl, tl, chunk_size=chunk, context_gate=gate)
+        n_t = (len(tl) + chunk - 1) // chunk
+        match = np.full(n_t, -1, np.int64)
+        for a in res.slot_actions:
+            if a.action == al.SlotActionType.COPY_FROM_DONOR and a.target_pos % chunk == 0:
+                match[a.target_pos // chunk] = a.donor_pos // chunk
+        digests = lambda toks: np.array([[int(al._chunk_hash(toks[i * chunk : (i + 1) * chunk])[8 * w : 8 * w + 8], 16)
+                                          for w in range(4)] for i in range(len(toks) // chunk)], np.uint32)
+        save(name, donor=donor, target=target, chunk=chunk, gate=int(gate), match=match,
+             reuse_ratio=res.reuse_ratio, exact_chunks=res.exact_chunks,
+             estimate=al.estimate_reuse_ratio(dl, tl, chunk_size=chunk),
+             donor_digests=digests(dl), target_digests=digests(tl))
+
+    align_case("align_gate", 31, 256, 24, True)
+    align_case("align_nogate", 32, 256, 24, False)
+    align_case("align_small", 33, 16, 60, True)
     print("wrote", sorted(p.name for p in HERE.glob("*.npz")), "plans.json")
     return 0
 

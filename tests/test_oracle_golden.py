@@ -118,3 +118,21 @@ def test_store_rows_and_cosine_stage_match_reference():
         got = [idx_to_id[int(i)] for i in c[: len(want)]]
         assert got == want
         np.testing.assert_array_equal(s[: len(want)], g["result_sims"][qi].numpy()[: len(want)].astype(np.float32))
+
+
+@pytest.mark.parametrize("name", ["align_gate", "align_nogate", "align_small"])
+def test_alignment_oracle_matches_reference(name):
+    from oracle import alignment as oal
+
+    g = load_golden(name)
+    donor, target = g["donor"].tolist(), g["target"].tolist()
+    chunk, gate = int(g["chunk"]), bool(g["gate"])
+    assert np.array_equal(oal.digests(donor, chunk), g["donor_digests"].numpy())
+    assert np.array_equal(oal.digests(target, chunk), g["target_digests"].numpy())
+    match = oal.chunk_matches(donor, target, chunk, gate)
+    assert np.array_equal(match, g["match"].numpy())
+    n_match = int((match >= 0).sum())
+    assert n_match == int(g["exact_chunks"])
+    assert n_match * chunk / len(target) == pytest.approx(float(g["reuse_ratio"]), abs=0)
+    est = oal.estimate_chunk_reuse(donor, target, chunk)
+    assert est == pytest.approx(float(g["estimate"]), abs=0)
