@@ -55,7 +55,9 @@ class DeviceAlignment:
     ``match [n_target_chunks]`` int32: donor chunk per target chunk (-1:
     recompute; a trailing partial chunk is always -1).  ``donor_positions`` /
     ``target_positions`` int32 hold the pairs of the matched chunks in target
-    order; the first ``n_pairs`` (a device int64 scalar) entries are valid.
+    order; the first ``n_pairs`` (a device int64 scalar) entries are valid and
+    the rest are -1, so the whole arrays can go to an inject without a host
+    synchronisation (the -1 pairs are skipped, and counted as skipped).
     """
 
     match: torch.Tensor
@@ -86,8 +88,9 @@ def chunk_alignment(donor_tokens, target_tokens, chunk_size: int = DEFAULT_CHUNK
     n_full = td.shape[0]
     n_chunks = (t.shape[0] + chunk_size - 1) // chunk_size
     match = torch.full((n_chunks,), -1, dtype=torch.int32, device=device)
-    dpos = torch.empty(max(n_full * chunk_size, 1), dtype=torch.int32, device=device)
-    tpos = torch.empty_like(dpos)
+    # entries past n_pairs stay -1: an inject handed the whole arrays skips them (counted as skipped pairs)
+    dpos = torch.full((max(n_full * chunk_size, 1),), -1, dtype=torch.int32, device=device)
+    tpos = torch.full_like(dpos, -1)
     n_pairs = torch.zeros(1, dtype=torch.int64, device=device)
     lib = _lib.load()
     _lib.check(lib.sb_chunk_align(dd.data_ptr() if dd.shape[0] else None, dd.shape[0], td.data_ptr(), n_full,
