@@ -117,3 +117,38 @@ class StoreRows:
             self.embeddings[idx] = 0.0
         self.valid[idx] = True
         self.entries[request_id] = idx
+
+
+class RadixStore:
+    """The SGLang integration's donor store (semblend/integration/sglang/
+    radix_backend.py:144-211): LRU OrderedDict keyed by the first 256 token
+    ids, a Python loop for the best cosine strictly above the threshold."""
+
+    def __init__(self, max_entries: int, min_similarity: float):
+        from collections import OrderedDict
+
+        self.entries = OrderedDict()
+        self.max_entries = max_entries
+        self.min_similarity = min_similarity
+
+    def add_donor(self, token_ids, embedding):
+        key = token_ids[:256]
+        if key in self.entries:
+            self.entries.move_to_end(key)
+            return
+        self.entries[key] = (token_ids, embedding / (np.linalg.norm(embedding) + 1e-10))
+        while len(self.entries) > self.max_entries:
+            self.entries.popitem(last=False)
+
+    def find_donor(self, query, exclude_tokens=None):
+        if not self.entries:
+            return None, None
+        qn = query / (np.linalg.norm(query) + 1e-10)
+        best, best_sim = None, self.min_similarity
+        for toks, emb in self.entries.values():
+            if exclude_tokens and toks[:256] == exclude_tokens[:256]:
+                continue
+            sim = float(np.dot(emb, qn))
+            if sim > best_sim:
+                best, best_sim = toks, sim
+        return best, (best_sim if best is not None else None)

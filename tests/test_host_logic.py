@@ -92,8 +92,12 @@ def test_compat_install_aliases_reference_names():
         assert rope_correct_scatter_paged.__module__ == "semblend_b200.rope_correction"
         assert DonorStore.__module__ == "semblend_b200.donor_store"
         assert done["semblend_core.triton_kernels"] == "semblend_b200.triton_kernels"
+        from synapse_kv_connector.cagra_donor_store import CAGRADonorStore, make_donor_store
+
+        assert issubclass(CAGRADonorStore, DonorStore) and make_donor_store.__module__ == "semblend_b200.cagra_donor_store"
         compat.uninstall()
         assert "semblend_core.rope_correction" not in sys.modules
+        assert "synapse_kv_connector.cagra_donor_store" not in sys.modules
     finally:
         for k in [k for k in sys.modules if k.split(".")[0] in compat.PARENTS]:
             del sys.modules[k]

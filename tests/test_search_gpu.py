@@ -246,3 +246,71 @@ def test_merge_strided_lists_with_ties_and_empties(n_lists, k):
     got_i, got_s = merge_topk(di[:, : Q * k].view(n_lists, Q, k), ds_[:, : Q * k].view(n_lists, Q, k))
     assert torch.equal(got_i.cpu(), want_i)
     assert torch.equal(got_s.cpu(), want_s)
+
+
+def test_radix_store_matches_reference_loop():
+    """SGLang store: LRU keys, eviction, exclusion, strict threshold, ties by
+    insertion order — against the reference's loop (restated in the oracle)."""
+    from semblend_b200.radix_store import RadixDonorStore
+
+    rng = np.random.default_rng(17)
+    dim = 384
+    centers = rng.standard_normal((6, dim)).astype(np.float32)
+    ref = osearch.RadixStore(max_entries=40, min_similarity=0.6)
+    ours = RadixDonorStore(max_entries=40, min_similarity=0.6, embedding_dim=dim, device=DEV)
+    keys = []
+    for step in range(140):
+        if keys and rng.random() < 0.15:  # re-add an existing key (moves to the end)
+            toks = keys[int(rng.integers(0, len(keys)))]
+            emb = rng.standard_normal(dim).astype(np.float32)
+        else:
+            toks = tuple(int(x) for x in rng.integers(0, 50000, int(rng.integers(200, 400))))
+            c = centers[int(rng.integers(0, 6))]
+            emb = (c + 0.3 * rng.standard_normal(dim)).astype(np.float32)
+            if rng.random() < 0.1 and keys:  # an exact duplicate embedding: a tie
+                emb = ref.entries[keys[-1][:256]][1].copy() if keys[-1][:256] in ref.entries else emb
+            keys.append(toks)
+        ref.add_donor(toks, emb)
+        ours.add_donor(toks, emb)
+        assert ours.size == len(ref.entries)
+        if step % 7 == 0:
+            q = (centers[int(rng.integers(0, 6))] + 0.3 * rng.standard_normal(dim)).astype(np.float32)
+            excl = keys[int(rng.integers(0, len(keys)))] if rng.random() < 0.5 else None
+            want, want_sim = ref.find_donor(q, excl)
+            got = ours.find_donor(q, excl)
+            if want is None:
+                assert got is None or float(np.dot(got.embedding, q / (np.linalg.norm(q) + 1e-10))) <= 0.6 + 1e-6
+            else:
+                assert got is not None
+                got_sim = float(np.dot(got.embedding, q / (np.linalg.norm(q) + 1e-10)))
+                assert got.token_ids == want or abs(got_sim - want_sim) <= 1e-6
+
+
+def test_cagra_factory_is_the_exact_store():
+    """make_donor_store(use_cagra=True) answers like DonorStore (the exact search
+    replaces cuVS CAGRA); no index rebuild between adds and finds."""
+    from semblend_b200.cagra_donor_store import CAGRADonorStore, make_donor_store
+
+    rng = np.random.default_rng(5)
+
+    class _A:
+        reuse_ratio = 1.0
+
+    align = (lambda *a, **k: 1.0, lambda *a, **k: _A())
+    a = make_donor_store(max_entries=200, embedding_dim=384, min_similarity=0.5, use_cagra=True, device=DEV,
+                         alignment=align)
+    b = ds.DonorStore(max_entries=200, embedding_dim=384, min_similarity=0.5, device=DEV, alignment=align)
+    assert isinstance(a, CAGRADonorStore)
+    base = rng.standard_normal(384).astype(np.float32)
+    for i in range(150):
+        emb = base + 0.3 * rng.standard_normal(384).astype(np.float32)
+        node = ds.DonorNode(request_id=f"r{i}", token_ids=[1, 2, 3, 1000 + i], embedding=emb / np.linalg.norm(emb),
+                            timestamp=float(i))
+        a.add_donor(node)
+        b.add_donor(node)
+        if i % 25 == 24:
+            q = base + 0.3 * rng.standard_normal(384).astype(np.float32)
+            ra = a.find_donors(q, [1, 2, 3], top_k=3)
+            rb = b.find_donors(q, [1, 2, 3], top_k=3)
+            assert ra
+            assert [m.donor.request_id for m in ra] == [m.donor.request_id for m in rb]
