@@ -980,6 +980,129 @@ def run_c5(args, world: int, rank: int, local: int) -> dict | None:
 
 
 # ---------------------------------------------------------------------------
+# Chunk-hash alignment (the step before the inject: which donor chunk feeds which target chunk)
+# ---------------------------------------------------------------------------
+AL_VOCAB = 128256  # Llama-3 vocabulary: token ids are int64 in [0, AL_VOCAB)
+
+
+def alignment_inputs(rng: np.random.Generator):
+    """c2 geometry: 8 requests, a 16384-token donor and a 16384-token target
+    each; 85 % of the target's 256-token chunks are donor chunks in shuffled
+    order, the rest fresh tokens (recompute)."""
+    n_chunks = SEQ // CHUNK
+    donors, targets = [], []
+    for _ in range(N_REQ):
+        d = rng.integers(0, AL_VOCAB, SEQ)
+        src = rng.permutation(n_chunks)
+        fresh = rng.random(n_chunks) < RECOMPUTE_FRAC
+        t = np.concatenate([rng.integers(0, AL_VOCAB, CHUNK) if fresh[i] else d[src[i] * CHUNK : (src[i] + 1) * CHUNK]
+                            for i in range(n_chunks)])
+        donors.append(d)
+        targets.append(t)
+    return np.stack(donors), np.stack(targets)
+
+
+def run_alignment(args, local: int) -> dict:
+    """Chunk-hash alignment of the c2 requests on the device (SHA-256 of every
+    256-token chunk, greedy matching with the context gate, position pairs for
+    the inject), against the reference's CPU algorithm (the oracle port)."""
+    from oracle import alignment as oal
+    from semblend_b200 import _lib
+    from semblend_b200.alignment import chunk_alignment, chunk_alignment_batch
+
+    dev = torch.device("cuda", local)
+    rng = np.random.default_rng(SEED + 11)
+    donors, targets = alignment_inputs(rng)
+    hd = torch.from_numpy(donors).pin_memory()
+    ht = torch.from_numpy(targets).pin_memory()
+    dd, dt = hd.to(dev), ht.to(dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step(d, t):  # every request of the step in one batch: 1 hashing + 2 matching launches
+        return chunk_alignment_batch(list(d), list(t), CHUNK, context_gate=True, device=dev)
+
+    def step_each(d, t):  # one chunk_alignment call per request
+        return [chunk_alignment(d[r], t[r], CHUNK, context_gate=True, device=dev) for r in range(N_REQ)]
+
+    for _ in range(max(args.warmup, 3)):
+        res = step(dd, dt)
+        res_each = step_each(dd, dt)
+    torch.cuda.synchronize(dev)
+    got = [int(a.n_pairs.item()) for a in res]
+    same = got == [int(a.n_pairs.item()) for a in res_each] and all(
+        torch.equal(a.match, b.match) for a, b in zip(res, res_each))
+    steps = max(10, min(args.steps, 200))
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with _lib.KernelTimer(steps) as kt:
+        e0.record(stream)
+        for _ in range(steps):
+            step(dd, dt)
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1) / steps
+    e0.record(stream)
+    for _ in range(steps):
+        step_each(dd, dt)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    each_ms = e0.elapsed_time(e1) / steps
+
+    # end to end: token ids from pinned host memory, the pair counts back (the pairs stay on the device)
+    hn = torch.empty(N_REQ, dtype=torch.int64).pin_memory()
+    bd, bt = torch.empty_like(dd), torch.empty_like(dt)
+    torch.cuda.synchronize(dev)
+    c0 = time.perf_counter()
+    e0.record(stream)
+    for _ in range(steps):
+        bd.copy_(hd, non_blocking=True)
+        bt.copy_(ht, non_blocking=True)
+        r = step(bd, bt)
+        hn.copy_(torch.cat([a.n_pairs for a in r]), non_blocking=True)
+        torch.cuda.synchronize(dev)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    e2e_ms = (time.perf_counter() - c0) * 1e3 / steps
+
+    # the reference's CPU algorithm (oracle port: hashlib SHA-256 + greedy matching), bounded sample
+    want = [int((oal.chunk_matches(donors[r].tolist(), targets[r].tolist(), CHUNK, True) >= 0).sum()) * CHUNK
+            for r in range(2)]
+    ok = got[:2] == want and hn.tolist() == got and same
+    cpu_s, n_cpu = 0.0, 0
+    while cpu_s < 3.0:
+        r = n_cpu % N_REQ
+        c0 = time.perf_counter()
+        oal.chunk_matches(donors[r].tolist(), targets[r].tolist(), CHUNK, True)
+        cpu_s += time.perf_counter() - c0
+        n_cpu += 1
+    tok = N_REQ * SEQ
+    pk = peaks()
+    sha_bytes = N_REQ * 2 * (SEQ * 8 + (SEQ // CHUNK) * 16)  # donors + targets: int64 ids read, digests written
+    sha_ms = kt.mean_ms
+    ach = sha_bytes / (sha_ms * 1e-3) / 1e9
+    return {
+        "metric": "chunk alignment tokens/s", "value": round(tok / (ms * 1e-3), 1), "unit": "tokens/s",
+        "higher_is_better": True, "ms_per_step": round(ms, 4), "steps": steps, "dtype": "int64",
+        "config": {"workload": f"c2 alignment: {N_REQ} targets x {SEQ} tokens against one {SEQ}-token donor each, "
+                               f"256-token chunks, {int(round((1 - RECOMPUTE_FRAC) * 100))}% donor chunks shuffled, "
+                               "context gate on; the step's requests in one chunk_alignment_batch call (digests "
+                               "of donors and targets, matching, pair arrays on the device)",
+                   "pairs_per_step": int(sum(got)), "matches_oracle": ok, "seed": SEED + 11,
+                   "one_call_per_request_ms": round(each_ms, 4)},
+        "roofline": {"bound": "hbm", "kernel": "chunk_sha256_kernel<int64_t>", "achieved": round(ach, 2),
+                     "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": round(ach / pk["hbm_gbs"], 6),
+                     "kernel_ms": round(sha_ms, 5), "traffic": None, "peak_source": pk["source"],
+                     "note": "latency-bound: one thread per 256-token chunk (1,024 per launch), 17 dependent "
+                             "SHA-256 compressions each"},
+        "cpu_baseline": {"value": round(n_cpu * SEQ / cpu_s, 1), "unit": "tokens/s", "cores": 1, "kind": "port",
+                         "sample": f"{n_cpu} requests through oracle.alignment.chunk_matches (hashlib SHA-256 + "
+                                   f"greedy matching + gate), {cpu_s:.1f} s of CPU work"},
+        "e2e": {"value": round(tok / (e2e_ms * 1e-3), 1), "unit": "tokens/s",
+                "h2d_bytes_per_step": int(hd.numel() * 8 + ht.numel() * 8), "d2h_bytes_per_step": N_REQ * 8},
+        "gpu_launches": steps * 3,
+    }
+
+
+# ---------------------------------------------------------------------------
 # CPU baseline (oracle port of the reference's inject) — bounded sample
 # ---------------------------------------------------------------------------
 def inject_config(n_req: int, n_layers: int, world: int, n_pairs: int | None) -> dict:
@@ -1069,7 +1192,7 @@ def main() -> int:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-components", action="store_true", help="skip the search / attention components")
-    ap.add_argument("--only", choices=["all", "search", "attention", "c5"], default="all",
+    ap.add_argument("--only", choices=["all", "search", "attention", "c5", "alignment"], default="all",
                     help="print only that component's line")
     ap.add_argument("--attn-batch", type=int, default=A_B, help="attention batch (c4: 4)")
     ap.add_argument("--attn-seq", type=int, default=A_S, help="attention context (c4: 32768)")
@@ -1086,11 +1209,13 @@ def main() -> int:
             print(json.dumps(line), flush=True)
         return 0
     world, rank, local = dist_setup(args.gpus)
-    if args.only in ("search", "attention", "c5"):
+    if args.only in ("search", "attention", "c5", "alignment"):
         if args.only == "search" and world > 1:
             res = run_search_sharded(args, world, rank, local)
         elif args.only == "c5":
             res = run_c5(args, world, rank, local)
+        elif args.only == "alignment":
+            res = run_alignment(args, local) if rank == 0 else None
         elif rank == 0:
             res = run_search(args, local) if args.only == "search" else run_attention(args, local)
         else:
@@ -1108,7 +1233,8 @@ def main() -> int:
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline()
         if world == 1 and not args.no_components:
-            line["components"] = {"search": run_search(args, local), "attention": run_attention(args, local)}
+            line["components"] = {"search": run_search(args, local), "attention": run_attention(args, local),
+                                  "alignment": run_alignment(args, local)}
     if not args.no_components:
         c5 = run_c5(args, world, rank, local)
         if line is not None:

@@ -335,13 +335,33 @@ SB_API int sb_chunk_digests(const void *tokens, int32_t token_dtype, int64_t n_t
  * only if target chunk t - 1 or t + 1 also matched.  Writes match[t] (device
  * int32, donor chunk or -1) for the n_target_chunks full target chunks and
  * the position pairs of the matched chunks in target order,
- * donor_positions[i] / target_positions[i] (device int32, room for
- * n_target_chunks * chunk entries), with their count in *n_pairs (device
- * int64) — the inputs of sb_inject, built without the host. */
+ * donor_positions[i] / target_positions[i] (device int32, all
+ * n_target_chunks * chunk entries written: -1 after the *n_pairs valid
+ * ones), with their count in *n_pairs (device int64) — the inputs of
+ * sb_inject, built without the host (the -1 entries are skipped there).
+ * n_target_chunks <= 65536. */
 SB_API int sb_chunk_align(const uint32_t *donor_digests, int32_t n_donor_chunks,
                           const uint32_t *target_digests, int32_t n_target_chunks, int32_t chunk,
                           int32_t context_gate, int32_t *match, int32_t *donor_positions,
                           int32_t *target_positions, int64_t *n_pairs, void *stream);
+
+/* sb_chunk_align for n_requests (donor, target) pairs in two launches.
+ * offsets (device int32 [3][n_requests + 1], prefix sums) give request r its
+ * donor digests [offsets[r], offsets[r + 1]) of donor_digests, its full
+ * target chunks [t0, t1) = [offsets[s + r], offsets[s + r + 1]) of
+ * target_digests (s = n_requests + 1) with pair slots [t0 * chunk, t1 * chunk)
+ * of donor_positions / target_positions, and its match entries
+ * [offsets[2s + r], offsets[2s + r + 1]) of match: its full target chunks,
+ * then -1 for a trailing partial chunk.  n_pairs[r] gets request r's pair
+ * count (-1 if its offsets are inconsistent or it has more than
+ * max_target_chunks full target chunks; nothing else is written for it).
+ * max_target_chunks (<= 65536) is the largest t1 - t0.  Positions are
+ * relative to each request's own sequences. */
+SB_API int sb_chunk_align_batch(const uint32_t *donor_digests, const uint32_t *target_digests,
+                                const int32_t *offsets, int32_t n_requests, int32_t max_target_chunks,
+                                int32_t chunk, int32_t context_gate, int32_t *match,
+                                int32_t *donor_positions, int32_t *target_positions, int64_t *n_pairs,
+                                void *stream);
 
 /* ------------------------------------------------------------------------ */
 /* Miscellaneous                                                            */

@@ -16,6 +16,7 @@ from __future__ import annotations
 import os
 from dataclasses import dataclass
 
+import numpy as np
 import torch
 
 from . import _lib
@@ -84,19 +85,87 @@ def chunk_alignment(donor_tokens, target_tokens, chunk_size: int = DEFAULT_CHUNK
             torch.device("cuda", torch.cuda.current_device())
     d = _tokens(donor_tokens, device)
     t = _tokens(target_tokens, device)
-    dd, td = chunk_digests(d, chunk_size), chunk_digests(t, chunk_size)
+    nd_full = d.shape[0] // chunk_size
+    if d.dtype == t.dtype:
+        # one hashing launch for both sequences (the donor's partial chunk is never hashed)
+        both = chunk_digests(torch.cat([d[: nd_full * chunk_size], t]), chunk_size)
+        dd, td = both[:nd_full], both[nd_full:]
+    else:
+        dd, td = chunk_digests(d, chunk_size), chunk_digests(t, chunk_size)
     n_full = td.shape[0]
     n_chunks = (t.shape[0] + chunk_size - 1) // chunk_size
     match = torch.full((n_chunks,), -1, dtype=torch.int32, device=device)
-    # entries past n_pairs stay -1: an inject handed the whole arrays skips them (counted as skipped pairs)
-    dpos = torch.full((max(n_full * chunk_size, 1),), -1, dtype=torch.int32, device=device)
-    tpos = torch.full_like(dpos, -1)
-    n_pairs = torch.zeros(1, dtype=torch.int64, device=device)
+    # the kernel writes -1 past n_pairs: an inject handed the whole arrays skips them (counted as skipped pairs)
+    n_pos = n_full * chunk_size
+    dpos = torch.empty(max(n_pos, 1), dtype=torch.int32, device=device)
+    tpos = torch.empty_like(dpos)
+    if n_pos == 0:
+        dpos.fill_(-1)
+        tpos.fill_(-1)
+    n_pairs = torch.empty(1, dtype=torch.int64, device=device)
     lib = _lib.load()
     _lib.check(lib.sb_chunk_align(dd.data_ptr() if dd.shape[0] else None, dd.shape[0], td.data_ptr(), n_full,
                                   chunk_size, int(gate), match.data_ptr(), dpos.data_ptr(), tpos.data_ptr(),
                                   n_pairs.data_ptr(), _lib.stream_ptr(device)), "sb_chunk_align")
     return DeviceAlignment(match, dpos, tpos, n_pairs, int(d.shape[0]), int(t.shape[0]), chunk_size)
+
+
+def chunk_alignment_batch(donors, targets, chunk_size: int = DEFAULT_CHUNK_SIZE, context_gate: bool | None = None,
+                          device=None) -> list[DeviceAlignment]:
+    """:func:`chunk_alignment` for several (donor, target) pairs at once — a
+    request against each of its donor candidates, or many requests — in one
+    hashing launch and two matching launches (``sb_chunk_align_batch``), with
+    no host synchronisation.  Returns one :class:`DeviceAlignment` per pair,
+    views into shared result buffers."""
+    donors, targets = list(donors), list(targets)
+    if len(donors) != len(targets):
+        raise ValueError(f"{len(donors)} donors for {len(targets)} targets")
+    n = len(targets)
+    if n == 0:
+        return []
+    if n > 65535:
+        raise ValueError("at most 65535 pairs per batch")
+    gate = _CONTEXT_GATE_ENABLED if context_gate is None else bool(context_gate)
+    c = int(chunk_size)
+    if c <= 0:
+        raise ValueError(f"chunk_size must be positive, got {chunk_size}")
+    if device is None:
+        first = next((x for x in targets + donors if isinstance(x, torch.Tensor) and x.is_cuda), None)
+        device = first.device if first is not None else torch.device("cuda", torch.cuda.current_device())
+    ds = [_tokens(x, device) for x in donors]
+    ts = [_tokens(x, device) for x in targets]
+    dtype = ds[0].dtype if all(x.dtype == ds[0].dtype for x in ds + ts) else torch.int64
+    nd = [x.shape[0] // c for x in ds]
+    nt = [x.shape[0] // c for x in ts]
+    nm = [(x.shape[0] + c - 1) // c for x in ts]
+    if max(nt) > 65536:
+        raise ValueError("a target has more than 65536 chunks")
+    # every sequence's full chunks, donors first: chunk boundaries stay at multiples of chunk_size
+    parts = [x[: k * c].to(dtype) for x, k in zip(ds, nd)] + [x[: k * c].to(dtype) for x, k in zip(ts, nt)]
+    dig = chunk_digests(torch.cat(parts), c)
+    n_d = sum(nd)
+    dd, td = dig[:n_d], dig[n_d:]
+    offs = np.zeros((3, n + 1), np.int64)
+    offs[0, 1:], offs[1, 1:], offs[2, 1:] = np.cumsum(nd), np.cumsum(nt), np.cumsum(nm)
+    if offs[1, -1] * c > 0x7FFFFFFF or offs[2, -1] > 0x7FFFFFFF:
+        raise ValueError("batch too large for int32 offsets")
+    offs_d = torch.from_numpy(offs.astype(np.int32)).to(device)
+    match = torch.empty(max(int(offs[2, -1]), 1), dtype=torch.int32, device=device)
+    n_pos = int(offs[1, -1]) * c
+    dpos = torch.empty(max(n_pos, 1), dtype=torch.int32, device=device)
+    tpos = torch.empty_like(dpos)
+    n_pairs = torch.empty(n, dtype=torch.int64, device=device)
+    lib = _lib.load()
+    _lib.check(lib.sb_chunk_align_batch(dd.data_ptr() if n_d else None, td.data_ptr() if td.shape[0] else None,
+                                        offs_d.data_ptr(), n, max(nt), c, int(gate), match.data_ptr(),
+                                        dpos.data_ptr(), tpos.data_ptr(), n_pairs.data_ptr(),
+                                        _lib.stream_ptr(device)), "sb_chunk_align_batch")
+    out = []
+    for r in range(n):
+        t0, t1 = int(offs[1, r]) * c, int(offs[1, r + 1]) * c
+        out.append(DeviceAlignment(match[offs[2, r] : offs[2, r + 1]], dpos[t0:t1], tpos[t0:t1], n_pairs[r : r + 1],
+                                   int(ds[r].shape[0]), int(ts[r].shape[0]), c))
+    return out
 
 
 def estimate_chunk_reuse(donor_tokens, target_tokens, chunk_size: int = DEFAULT_CHUNK_SIZE, device=None) -> float:
@@ -160,6 +229,7 @@ __all__ = [
     "DeviceAlignment",
     "SlotAction",
     "chunk_alignment",
+    "chunk_alignment_batch",
     "chunk_digests",
     "compute_chunk_alignment",
     "estimate_chunk_reuse",

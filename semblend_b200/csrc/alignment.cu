@@ -8,31 +8,37 @@
 // matched neighbour; the result is expanded into per-position pairs.  Here:
 //   1. chunk_sha256_kernel   one thread per full chunk: SHA-256 (FIPS 180-4)
 //                            of the chunk's 4 * chunk bytes;
-//   2. chunk_match_kernel    one thread per target chunk: its rank among the
-//                            earlier target chunks with the same digest picks
-//                            the donor chunk of the same rank among donor
-//                            chunks with that digest (= the greedy first-unused
-//                            rule of the reference, computed in parallel), then
-//                            the context gate on its neighbours' matches;
-//   3. chunk_pairs_kernel    one CTA: a block-wide scan over the matched chunks
-//                            and the (donor, target) position pairs written
-//                            straight into the inject kernel's input arrays,
-//                            with their count.
+//   2. chunk_match_kernel    one CTA per request, one thread per target chunk:
+//                            its rank among the earlier target chunks with the
+//                            same digest picks the donor chunk of the same
+//                            rank among donor chunks with that digest (= the
+//                            greedy first-unused rule of the reference,
+//                            computed in parallel), then the context gate on
+//                            its neighbours' matches;
+//   3. chunk_pairs_kernel    a few target chunks per CTA: the matched chunks'
+//                            (donor, target) position pairs written straight
+//                            into the inject kernel's input arrays (-1 after
+//                            the last), with their count.
 // The SHA-256 round constants and initial hash are computed on the host from
 // their definition (fractional parts of the cube / square roots of the first
 // 64 / 8 primes) and copied to constant memory once per device.
+#include <algorithm>
 #include <cmath>
 #include <mutex>
 
 #include "common.cuh"
+#include "prof.cuh"
 
 namespace sb {
 namespace {
 
+// chunks are few (one per 256 tokens): small CTAs spread them over the SMs
+constexpr int kShaThreads = 32;
+
 __constant__ uint32_t c_sha_k[64];
 __constant__ uint32_t c_sha_h0[8];
 
-__device__ __forceinline__ uint32_t rotr(uint32_t x, int n) { return (x >> n) | (x << (32 - n)); }
+__device__ __forceinline__ uint32_t rotr(uint32_t x, int n) { return __funnelshift_r(x, x, n); }
 __device__ __forceinline__ uint32_t bswap(uint32_t x) { return __byte_perm(x, 0, 0x0123); }
 
 __device__ __forceinline__ void sha256_block(uint32_t (&h)[8], const uint32_t (&m)[16]) {
@@ -60,121 +66,200 @@ __device__ __forceinline__ void sha256_block(uint32_t (&h)[8], const uint32_t (&
 }
 
 // Digest (first 128 bits, as four big-endian words) of every full chunk.
+// One loop over the message blocks (data, then the 0x80 byte and the bit
+// length as FIPS 180-4 pads them), so the compression is inlined once; the
+// ids of the next block are loaded while the current one is compressed.
 template <typename I>
-__global__ void chunk_sha256_kernel(const I *__restrict__ tokens, int chunk, int64_t n_chunks,
-                                    uint32_t *__restrict__ digests) {
+__global__ void __launch_bounds__(kShaThreads) chunk_sha256_kernel(const I *__restrict__ tokens, int chunk,
+                                                                   int64_t n_chunks, uint32_t *__restrict__ digests) {
   const int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (c >= n_chunks) return;
   const I *t = tokens + c * chunk;
   uint32_t h[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) h[i] = c_sha_h0[i];
-  uint32_t m[16];
-  // message: 4 bytes per token (little-endian uint32), SHA-256 reads big-endian words
-  for (int base = 0; base < chunk; base += 16) {
+  // message: 4 bytes per token (little-endian uint32) then the padding; SHA-256 reads big-endian words
+  const int n_blocks = (chunk + 2) / 16 + 1;  // 4 * chunk + 9 bytes, rounded up to 64-byte blocks
+  const uint64_t bits = (uint64_t)chunk * 32;
+  uint32_t m[16], nxt[16];
 #pragma unroll
-    for (int i = 0; i < 16; ++i) m[i] = base + i < chunk ? bswap((uint32_t)t[base + i]) : 0u;
-    const int n = chunk - base;
-    if (n >= 16) {
-      sha256_block(h, m);
-    } else {  // tail block (chunk not a multiple of 16 tokens): padding follows the data
-      m[n] = 0x80000000u;
-      if (n <= 13) {
-        m[14] = (uint32_t)(((uint64_t)chunk * 32) >> 32);
-        m[15] = (uint32_t)((uint64_t)chunk * 32);
-        sha256_block(h, m);
-      } else {
-        sha256_block(h, m);
+  for (int i = 0; i < 16; ++i) nxt[i] = i < chunk ? (uint32_t)t[i] : 0u;
+  for (int blk = 0; blk < n_blocks; ++blk) {
+    const int base = blk * 16;
 #pragma unroll
-        for (int i = 0; i < 16; ++i) m[i] = 0;
-        m[14] = (uint32_t)(((uint64_t)chunk * 32) >> 32);
-        m[15] = (uint32_t)((uint64_t)chunk * 32);
-        sha256_block(h, m);
-      }
-      break;
+    for (int i = 0; i < 16; ++i) {
+      const int g = base + i;
+      m[i] = g < chunk ? bswap(nxt[i]) : (g == chunk ? 0x80000000u : 0u);
     }
-  }
-  if (chunk % 16 == 0) {  // data filled whole blocks: one padding block
+    if (blk == n_blocks - 1) {
+      m[14] = (uint32_t)(bits >> 32);
+      m[15] = (uint32_t)bits;
+    }
+    if (base + 16 < chunk) {
 #pragma unroll
-    for (int i = 0; i < 16; ++i) m[i] = 0;
-    m[0] = 0x80000000u;
-    m[14] = (uint32_t)(((uint64_t)chunk * 32) >> 32);
-    m[15] = (uint32_t)((uint64_t)chunk * 32);
+      for (int i = 0; i < 16; ++i) nxt[i] = base + 16 + i < chunk ? (uint32_t)t[base + 16 + i] : 0u;
+    }
     sha256_block(h, m);
   }
 #pragma unroll
   for (int i = 0; i < 4; ++i) digests[c * 4 + i] = h[i];
 }
 
-__device__ __forceinline__ bool same(const uint32_t *a, const uint32_t *b) {
-  return a[0] == b[0] && a[1] == b[1] && a[2] == b[2] && a[3] == b[3];
-}
+// The requests of one launch.  Request r owns donor digests [d0, d0 + nd),
+// full target chunks [t0, t0 + nt) (digests, and pair slots [t0 * chunk,
+// (t0 + nt) * chunk)) and match entries [m0, m0 + nm) (its full target
+// chunks, then -1 for a trailing partial chunk).  offs holds the three prefix
+// arrays [3][n + 1]; NULL means one request with the counts nd1 / nt1 / nm1.
+struct AlignBatch {
+  const uint32_t *dd, *td;
+  const int32_t *offs;
+  int n, nd1, nt1, nm1, max_nt;
+  int chunk, gate;
+  int32_t *match, *dpos, *tpos;
+  int64_t *n_pairs;
+};
 
-// Phase 1 (no gate): target chunk t takes the donor chunk whose rank among
-// donor chunks with t's digest equals t's rank among target chunks with it.
-__device__ int phase1_match(const uint32_t *__restrict__ dd, int nd, const uint32_t *__restrict__ td, int t) {
-  const uint32_t *me = td + 4 * t;
-  int rank = 0;
-  for (int u = 0; u < t; ++u) rank += same(td + 4 * u, me);
-  for (int d = 0; d < nd; ++d) {
-    if (same(dd + 4 * d, me)) {
-      if (rank == 0) return d;
-      --rank;
-    }
+struct ReqRange {
+  int d0, nd, t0, nt, m0, nm;
+};
+
+__device__ __forceinline__ bool req_range(const AlignBatch &B, int r, ReqRange &q) {
+  if (B.offs == nullptr) {
+    q = ReqRange{0, B.nd1, 0, B.nt1, 0, B.nm1};
+  } else {
+    const int s = B.n + 1;
+    q.d0 = B.offs[r], q.nd = B.offs[r + 1] - q.d0;
+    q.t0 = B.offs[s + r], q.nt = B.offs[s + r + 1] - q.t0;
+    q.m0 = B.offs[2 * s + r], q.nm = B.offs[2 * s + r + 1] - q.m0;
   }
-  return -1;
+  // offsets that do not describe a request this launch was sized for: skip it
+  return q.nd >= 0 && q.nt >= 0 && q.nt <= B.max_nt && q.nm >= q.nt && q.d0 >= 0 && q.t0 >= 0 && q.m0 >= 0;
 }
 
-// Final match of target chunk t; with the context gate a match survives only
-// if a neighbouring target chunk matched in phase 1 (each thread recomputes
-// its neighbours' phase-1 result, so no pass over the whole array is needed).
-__global__ void chunk_match_kernel(const uint32_t *__restrict__ dd, int nd, const uint32_t *__restrict__ td, int nt,
-                                   int gate, int32_t *__restrict__ match) {
-  const int t = blockIdx.x * blockDim.x + threadIdx.x;
-  if (t >= nt) return;
-  int m = phase1_match(dd, nd, td, t);
-  if (gate && m >= 0) {
-    const bool left = t > 0 && phase1_match(dd, nd, td, t - 1) >= 0;
-    const bool right = t + 1 < nt && phase1_match(dd, nd, td, t + 1) >= 0;
-    if (!left && !right) m = -1;
+__device__ __forceinline__ bool same(const uint32_t *a, const uint4 b) {
+  return a[0] == b.x && a[1] == b.y && a[2] == b.z && a[3] == b.w;
+}
+
+constexpr int kMatchThreads = 512;
+constexpr int kMatchSmemWords = 8192;  // first digest words of a request staged in shared memory (32 KB)
+constexpr int kMaxTargetChunks = 65536;  // per request: the matched-chunk flags live in shared memory (8 KB)
+
+// One CTA per request.  Phase 1 (no gate): target chunk t takes the donor
+// chunk whose rank among the donor chunks with t's digest equals t's rank
+// among the earlier target chunks with it (= the greedy first-unused rule).
+// The scans compare the digests' first words (staged in shared memory and
+// read by a warp in step, so each read is a broadcast) and the full digests
+// only on a first-word hit.  Then the context gate: a match survives only if
+// target chunk t - 1 or t + 1 also matched in phase 1.
+__global__ void __launch_bounds__(kMatchThreads) chunk_match_kernel(const AlignBatch B) {
+  __shared__ uint32_t w0[kMatchSmemWords];
+  __shared__ uint32_t hit[kMaxTargetChunks / 32];
+  ReqRange q;
+  if (!req_range(B, blockIdx.x, q)) return;
+  const uint32_t *dd = B.dd + 4LL * q.d0, *td = B.td + 4LL * q.t0;
+  int32_t *match = B.match + q.m0;
+  const bool staged = q.nd + q.nt <= kMatchSmemWords;
+  if (staged) {
+    for (int i = threadIdx.x; i < q.nd; i += kMatchThreads) w0[i] = dd[4 * i];
+    for (int i = threadIdx.x; i < q.nt; i += kMatchThreads) w0[q.nd + i] = td[4 * i];
   }
-  match[t] = m;
-}
-
-// The pair arrays: matched chunk i (in target order) owns pairs
-// [i * chunk, (i + 1) * chunk).  One CTA, a block-wide scan per 1024 chunks.
-__global__ void chunk_pairs_kernel(const int32_t *__restrict__ match, int nt, int chunk,
-                                   int32_t *__restrict__ donor_pos, int32_t *__restrict__ target_pos,
-                                   int64_t *__restrict__ n_pairs) {
-  __shared__ int warp_sum[32];
-  __shared__ int carry;
-  if (threadIdx.x == 0) carry = 0;
+  for (int i = threadIdx.x; i < (q.nt + 31) / 32; i += kMatchThreads) hit[i] = 0;
   __syncthreads();
-  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
-  for (int base = 0; base < nt; base += blockDim.x) {
-    const int t = base + threadIdx.x;
-    const int m = t < nt ? match[t] : -1;
-    const int f = m >= 0;
-    const unsigned bal = __ballot_sync(0xffffffffu, f);
-    if (lane == 0) warp_sum[wid] = __popc(bal);
-    __syncthreads();
-    int off = carry, tot = 0;
-    for (int i = 0; i < nw; ++i) {
-      if (i < wid) off += warp_sum[i];
-      tot += warp_sum[i];
+  for (int t = threadIdx.x; t < q.nt; t += kMatchThreads) {
+    const uint4 me = make_uint4(td[4 * t], td[4 * t + 1], td[4 * t + 2], td[4 * t + 3]);
+    int rank = 0;
+    for (int u = 0; u < t; ++u) {
+      const uint32_t w = staged ? w0[q.nd + u] : td[4 * u];
+      rank += w == me.x && same(td + 4 * u, me);
     }
-    off += __popc(bal & ((1u << lane) - 1));
-    if (f) {
-      for (int i = 0; i < chunk; ++i) {
-        donor_pos[(int64_t)off * chunk + i] = m * chunk + i;
-        target_pos[(int64_t)off * chunk + i] = t * chunk + i;
+    int m = -1;
+    for (int d = 0; d < q.nd; ++d) {
+      const uint32_t w = staged ? w0[d] : dd[4 * d];
+      if (w == me.x && same(dd + 4 * d, me)) {
+        if (rank == 0) {
+          m = d;
+          break;
+        }
+        --rank;
       }
     }
-    __syncthreads();
-    if (threadIdx.x == 0) carry += tot;
-    __syncthreads();
+    match[t] = m;
+    if (m >= 0) atomicOr(&hit[t >> 5], 1u << (t & 31));
   }
-  if (threadIdx.x == 0) *n_pairs = (int64_t)carry * chunk;
+  __syncthreads();
+  auto flag = [&](int t) { return (hit[t >> 5] >> (t & 31)) & 1u; };
+  for (int t = threadIdx.x; t < q.nm; t += kMatchThreads) {
+    if (t >= q.nt) {
+      match[t] = -1;
+    } else if (B.gate && flag(t) && !(t > 0 && flag(t - 1)) && !(t + 1 < q.nt && flag(t + 1))) {
+      match[t] = -1;
+    }
+  }
+}
+
+// The pair arrays: matched chunk i of a request (in target order) owns pairs
+// [i * chunk, (i + 1) * chunk) of the request's slots; the slots after its
+// last matched chunk are filled with -1, unmatched chunk c taking slot
+// (matched total + unmatched chunks before c).  CTA (x, r) handles
+// kPairChunks consecutive target chunks of request r: it counts the matched
+// chunks before its range and in total (one entry per chunk: small), then
+// writes its chunks' pairs with the whole block, so the stores are coalesced.
+constexpr int kPairChunks = 4;
+constexpr int kPairThreads = 256;
+
+__global__ void __launch_bounds__(kPairThreads) chunk_pairs_kernel(const AlignBatch B) {
+  __shared__ int red[2][kPairThreads / 32];
+  ReqRange q;
+  const bool ok = req_range(B, blockIdx.y, q);
+  if (!ok) {
+    if (blockIdx.x == 0 && threadIdx.x == 0) B.n_pairs[blockIdx.y] = -1;
+    return;
+  }
+  const int c0 = blockIdx.x * kPairChunks;
+  if (blockIdx.x > 0 && c0 >= q.nt) return;
+  const int32_t *match = B.match + q.m0;
+  const int c1 = min(q.nt, c0 + kPairChunks);
+  int before = 0, total = 0;
+  for (int i = threadIdx.x; i < q.nt; i += kPairThreads) {
+    const int f = match[i] >= 0;
+    total += f;
+    before += f & (i < c0);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    before += __shfl_xor_sync(0xffffffffu, before, o);
+    total += __shfl_xor_sync(0xffffffffu, total, o);
+  }
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  if (lane == 0) red[0][wid] = before, red[1][wid] = total;
+  __syncthreads();
+  before = 0, total = 0;
+#pragma unroll
+  for (int i = 0; i < kPairThreads / 32; ++i) before += red[0][i], total += red[1][i];
+  const int chunk = B.chunk;
+  if (blockIdx.x == 0 && threadIdx.x == 0) B.n_pairs[blockIdx.y] = (int64_t)total * chunk;
+  int32_t *dpos = B.dpos + (int64_t)q.t0 * chunk, *tpos = B.tpos + (int64_t)q.t0 * chunk;
+  int matched = before;
+  for (int c = c0; c < c1; ++c) {
+    const int m = match[c];
+    const bool got = m >= 0;
+    const int64_t slot = got ? matched : (int64_t)total + (c - matched);
+    int32_t *dp = dpos + slot * chunk, *tp = tpos + slot * chunk;
+    for (int i = threadIdx.x; i < chunk; i += kPairThreads) {
+      dp[i] = got ? m * chunk + i : -1;
+      tp[i] = got ? c * chunk + i : -1;
+    }
+    matched += got;
+  }
+}
+
+int launch_align(const AlignBatch &B, cudaStream_t st) {
+  chunk_match_kernel<<<(unsigned)B.n, kMatchThreads, 0, st>>>(B);
+  int s = launch_status();
+  if (s != SB_OK) return s;
+  const unsigned gx = (unsigned)std::max(1, (B.max_nt + kPairChunks - 1) / kPairChunks);
+  chunk_pairs_kernel<<<dim3(gx, (unsigned)B.n), kPairThreads, 0, st>>>(B);
+  return launch_status();
 }
 
 // SHA-256 constants from their definition, on the host with 64-bit-mantissa
@@ -225,13 +310,15 @@ extern "C" SB_API int sb_chunk_digests(const void *tokens, int32_t token_dtype, 
   const int s = upload_constants();
   if (s != SB_OK) return s;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  const unsigned grid = (unsigned)((n_chunks + 127) / 128);
+  const unsigned grid = (unsigned)((n_chunks + kShaThreads - 1) / kShaThreads);
+  const int slot = prof_before(st);
   if (token_dtype == SB_INDEX_I32)
-    chunk_sha256_kernel<int32_t><<<grid, 128, 0, st>>>(static_cast<const int32_t *>(tokens), chunk, n_chunks,
-                                                       digests);
+    chunk_sha256_kernel<int32_t><<<grid, kShaThreads, 0, st>>>(static_cast<const int32_t *>(tokens), chunk,
+                                                               n_chunks, digests);
   else
-    chunk_sha256_kernel<int64_t><<<grid, 128, 0, st>>>(static_cast<const int64_t *>(tokens), chunk, n_chunks,
-                                                       digests);
+    chunk_sha256_kernel<int64_t><<<grid, kShaThreads, 0, st>>>(static_cast<const int64_t *>(tokens), chunk,
+                                                               n_chunks, digests);
+  prof_after(slot, st);
   return launch_status();
 }
 
@@ -241,7 +328,8 @@ extern "C" SB_API int sb_chunk_align(const uint32_t *donor_digests, int32_t n_do
                                      int32_t *target_positions, int64_t *n_pairs, void *stream) {
   using namespace sb;
   if (n_donor_chunks < 0 || n_target_chunks < 0 || chunk <= 0) return SB_ERR_INVALID_ARGUMENT;
-  if ((int64_t)n_target_chunks * chunk > 0x7fffffffLL || (int64_t)n_donor_chunks * chunk > 0x7fffffffLL)
+  if ((int64_t)n_target_chunks * chunk > 0x7fffffffLL || (int64_t)n_donor_chunks * chunk > 0x7fffffffLL ||
+      n_target_chunks > kMaxTargetChunks)
     return SB_ERR_TOO_LARGE;
   if (!n_pairs || (n_target_chunks > 0 && (!target_digests || !match || !donor_positions || !target_positions)))
     return SB_ERR_INVALID_ARGUMENT;
@@ -255,11 +343,32 @@ extern "C" SB_API int sb_chunk_align(const uint32_t *donor_digests, int32_t n_do
     }
     return SB_OK;
   }
-  chunk_match_kernel<<<(unsigned)((n_target_chunks + 127) / 128), 128, 0, st>>>(
-      donor_digests, n_donor_chunks, target_digests, n_target_chunks, context_gate ? 1 : 0, match);
-  int s = launch_status();
-  if (s != SB_OK) return s;
-  chunk_pairs_kernel<<<1, 1024, 0, st>>>(match, n_target_chunks, chunk, donor_positions, target_positions,
-                                         n_pairs);
-  return launch_status();
+  AlignBatch B{};
+  B.dd = donor_digests, B.td = target_digests, B.offs = nullptr;
+  B.n = 1, B.nd1 = n_donor_chunks, B.nt1 = n_target_chunks, B.nm1 = n_target_chunks, B.max_nt = n_target_chunks;
+  B.chunk = chunk, B.gate = context_gate ? 1 : 0;
+  B.match = match, B.dpos = donor_positions, B.tpos = target_positions, B.n_pairs = n_pairs;
+  return launch_align(B, st);
+}
+
+extern "C" SB_API int sb_chunk_align_batch(const uint32_t *donor_digests, const uint32_t *target_digests,
+                                           const int32_t *offsets, int32_t n_requests, int32_t max_target_chunks,
+                                           int32_t chunk, int32_t context_gate, int32_t *match,
+                                           int32_t *donor_positions, int32_t *target_positions, int64_t *n_pairs,
+                                           void *stream) {
+  using namespace sb;
+  if (n_requests < 0 || max_target_chunks < 0 || chunk <= 0) return SB_ERR_INVALID_ARGUMENT;
+  if (n_requests > 65535 || max_target_chunks > kMaxTargetChunks ||
+      (int64_t)max_target_chunks * chunk > 0x7fffffffLL)
+    return SB_ERR_TOO_LARGE;
+  if (n_requests == 0) return SB_OK;
+  if (!offsets || !match || !n_pairs || (max_target_chunks > 0 && (!target_digests || !donor_positions ||
+                                                                   !target_positions)))
+    return SB_ERR_INVALID_ARGUMENT;
+  AlignBatch B{};
+  B.dd = donor_digests, B.td = target_digests, B.offs = offsets;
+  B.n = n_requests, B.max_nt = max_target_chunks;
+  B.chunk = chunk, B.gate = context_gate ? 1 : 0;
+  B.match = match, B.dpos = donor_positions, B.tpos = target_positions, B.n_pairs = n_pairs;
+  return launch_align(B, reinterpret_cast<cudaStream_t>(stream));
 }

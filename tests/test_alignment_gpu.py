@@ -73,6 +73,67 @@ def test_alignment_vs_oracle_with_repeats(gate, chunk):
     dp, tp = a.pairs()
     wd, wt = _expected_pairs(want, chunk)
     assert np.array_equal(dp.cpu().numpy(), wd) and np.array_equal(tp.cpu().numpy(), wt)
+    n = int(a.n_pairs.item())
+    assert (a.donor_positions[n:] == -1).all() and (a.target_positions[n:] == -1).all()
+
+
+def test_alignment_many_chunks():
+    """Thousands of chunks: matched chunks out of order, repeats and unmatched
+    chunks spread over every pair-writing CTA."""
+    rng = np.random.default_rng(11)
+    chunk, nd = 16, 3000
+    donor = rng.integers(0, 1 << 30, chunk * nd)
+    donor[chunk * 100 : chunk * 110] = np.tile(donor[: chunk], 10)  # ten copies of chunk 0
+    picks = np.concatenate([rng.permutation(nd)[:2500], np.zeros(12, np.int64)])
+    rng.shuffle(picks)
+    parts = [donor[i * chunk : (i + 1) * chunk] for i in picks]
+    for j in rng.choice(len(parts), 400, replace=False):  # unmatched chunks
+        parts[j] = rng.integers(0, 1 << 30, chunk)
+    target = np.concatenate(parts + [rng.integers(0, 1 << 30, 7)])
+    for gate in (False, True):
+        a = al.chunk_alignment(torch.from_numpy(donor).to(DEV), torch.from_numpy(target).to(DEV), chunk, gate)
+        want = oal.chunk_matches(donor.tolist(), target.tolist(), chunk, gate)
+        assert np.array_equal(a.match.cpu().numpy(), want.astype(np.int32))
+        wd, wt = _expected_pairs(want, chunk)
+        n = int(a.n_pairs.item())
+        assert n == wd.shape[0]
+        assert np.array_equal(a.donor_positions[:n].cpu().numpy(), wd)
+        assert np.array_equal(a.target_positions[:n].cpu().numpy(), wt)
+        assert (a.donor_positions[n:] == -1).all() and (a.target_positions[n:] == -1).all()
+
+
+@pytest.mark.parametrize("gate", [False, True])
+def test_alignment_batch_vs_oracle(gate):
+    """Pairs of mixed sizes in one batch: each result equals the oracle's and
+    the single-pair call's (empty donor, target shorter than a chunk, partial
+    chunks, repeats, int32 beside int64 ids)."""
+    rng = np.random.default_rng(21 + gate)
+    chunk = 32
+    base = [rng.integers(0, 5000, chunk) for _ in range(10)]
+
+    def seq(n_chunks, tail):
+        s = [base[i] for i in rng.integers(0, 12, n_chunks) if i < 10]
+        s.append(rng.integers(0, 5000, tail))
+        return np.concatenate(s)
+
+    donors = [seq(40, 5), np.zeros(0, np.int64), seq(3, 0), seq(70, 31), seq(1, 0), seq(25, 3)]
+    targets = [seq(50, 7), seq(6, 0), rng.integers(0, 5000, 20), seq(90, 0), seq(2, 1), seq(30, 16)]
+    dt = [torch.from_numpy(d).to(DEV) for d in donors]
+    tt = [torch.from_numpy(t).to(DEV) for t in targets]
+    tt[5] = tt[5].to(torch.int32)
+    res = al.chunk_alignment_batch(dt, tt, chunk, gate)
+    assert len(res) == len(targets)
+    for r, a in enumerate(res):
+        want = oal.chunk_matches(donors[r].tolist(), targets[r].tolist(), chunk, gate)
+        assert np.array_equal(a.match.cpu().numpy(), want.astype(np.int32)), r
+        wd, wt = _expected_pairs(want, chunk)
+        dp, tp = a.pairs()
+        assert np.array_equal(dp.cpu().numpy(), wd) and np.array_equal(tp.cpu().numpy(), wt), r
+        n = int(a.n_pairs.item())
+        assert (a.donor_positions[n:] == -1).all() and (a.target_positions[n:] == -1).all()
+        one = al.chunk_alignment(dt[r], tt[r], chunk, gate)
+        assert torch.equal(one.match, a.match) and int(one.n_pairs.item()) == n
+    assert al.chunk_alignment_batch([], [], chunk) == []
 
 
 def test_alignment_edge_cases():
