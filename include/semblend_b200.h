@@ -363,6 +363,20 @@ SB_API int sb_chunk_align_batch(const uint32_t *donor_digests, const uint32_t *t
                                 int32_t *donor_positions, int32_t *target_positions, int64_t *n_pairs,
                                 void *stream);
 
+/* Workspace bytes of sb_token_overlap (8-byte aligned). */
+SB_API int64_t sb_token_overlap_workspace_bytes(int64_t n_donor_tokens, int64_t n_target_tokens);
+
+/* Multiset overlap of two token sequences (device int32 / int64 ids,
+ * SB_INDEX_*): *overlap (device int64) = sum over ids of min(occurrences in
+ * donor, occurrences in target) — the token-count fallback of
+ * estimate_reuse_ratio (semblend_core/alignment.py:776-785), where each target
+ * token consumes one unused occurrence in the donor.  Ids compare as 64-bit
+ * integers (an int32 id equals the int64 id of the same value).
+ * n_donor_tokens + n_target_tokens < 2^31. */
+SB_API int sb_token_overlap(const void *donor_tokens, int32_t donor_dtype, int64_t n_donor_tokens,
+                            const void *target_tokens, int32_t target_dtype, int64_t n_target_tokens,
+                            void *workspace, int64_t workspace_bytes, int64_t *overlap, void *stream);
+
 /* ------------------------------------------------------------------------ */
 /* Miscellaneous                                                            */
 /* ------------------------------------------------------------------------ */

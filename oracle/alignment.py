@@ -5,8 +5,8 @@ SHA-256 of the chunk's token ids packed as little-endian uint32, first 128
 bits), the exact chunk matching of `compute_chunk_alignment` (:133-268: each
 target chunk, in order, takes the first unused donor chunk with the same hash;
 the optional context gate then drops matches with no matched neighbour) and
-the chunk stage of `estimate_reuse_ratio` (:741-787).  Python's hashlib is the
-checker's SHA-256.
+`estimate_reuse_ratio` (:741-787: the chunk stage, else the token-multiset
+overlap).  Python's hashlib is the checker's SHA-256.
 """
 
 from __future__ import annotations
@@ -59,3 +59,28 @@ def estimate_chunk_reuse(donor_tokens, target_tokens, chunk: int) -> float:
     """Chunk stage of estimate_reuse_ratio (:752-774): matched tokens / target length."""
     m = chunk_matches(donor_tokens, target_tokens, chunk, False)
     return float((m >= 0).sum() * chunk) / max(len(target_tokens), 1)
+
+
+def token_overlap(donor_tokens, target_tokens) -> int:
+    """Multiset overlap: each target token consumes one unused donor occurrence
+    of the same id (alignment.py:776-785)."""
+    counts: dict[int, int] = {}
+    for tok in donor_tokens:
+        counts[int(tok)] = counts.get(int(tok), 0) + 1
+    n = 0
+    for tok in target_tokens:
+        c = counts.get(int(tok), 0)
+        if c > 0:
+            counts[int(tok)] = c - 1
+            n += 1
+    return n
+
+
+def estimate_reuse_ratio(donor_tokens, target_tokens, chunk: int) -> float:
+    """estimate_reuse_ratio (alignment.py:741-787): the chunk stage, else the
+    token-overlap fallback, over the target length."""
+    m = chunk_matches(donor_tokens, target_tokens, chunk, False)
+    matched = int((m >= 0).sum()) * chunk
+    if matched == 0:
+        matched = token_overlap(donor_tokens, target_tokens)
+    return matched / max(len(target_tokens), 1)

@@ -170,11 +170,42 @@ def chunk_alignment_batch(donors, targets, chunk_size: int = DEFAULT_CHUNK_SIZE,
 
 def estimate_chunk_reuse(donor_tokens, target_tokens, chunk_size: int = DEFAULT_CHUNK_SIZE, device=None) -> float:
     """Chunk stage of estimate_reuse_ratio (alignment.py:752-774): matched
-    tokens / target length with greedy, ungated chunk matching.  (The
-    reference falls back to a token-multiset overlap when no chunk matches;
-    that fallback stays with the caller.)"""
+    tokens / target length with greedy, ungated chunk matching (no fallback)."""
     a = chunk_alignment(donor_tokens, target_tokens, chunk_size, context_gate=False, device=device)
     return float(a.n_pairs.item()) / max(a.target_len, 1)
+
+
+def token_overlap(donor_tokens, target_tokens, device=None) -> torch.Tensor:
+    """Multiset overlap (sum over ids of min(donor count, target count)) as a
+    device int64 scalar ``[1]`` (``sb_token_overlap``; no host synchronisation)."""
+    if device is None:
+        first = next((x for x in (target_tokens, donor_tokens) if isinstance(x, torch.Tensor) and x.is_cuda), None)
+        device = first.device if first is not None else torch.device("cuda", torch.cuda.current_device())
+    d, t = _tokens(donor_tokens, device), _tokens(target_tokens, device)
+    lib = _lib.load()
+    nbytes = lib.sb_token_overlap_workspace_bytes(d.shape[0], t.shape[0])
+    if nbytes < 0:
+        _lib.check(int(nbytes), "sb_token_overlap_workspace_bytes")
+    ws = torch.empty((nbytes + 7) // 8, dtype=torch.int64, device=device)
+    out = torch.empty(1, dtype=torch.int64, device=device)
+    _lib.check(lib.sb_token_overlap(d.data_ptr() if d.numel() else None, _lib.index_code(d.dtype), d.shape[0],
+                                    t.data_ptr() if t.numel() else None, _lib.index_code(t.dtype), t.shape[0],
+                                    ws.data_ptr(), ws.numel() * 8, out.data_ptr(), _lib.stream_ptr(device)),
+               "sb_token_overlap")
+    return out
+
+
+def estimate_reuse_ratio(donor_tokens, target_tokens, chunk_size: int = DEFAULT_CHUNK_SIZE, device=None) -> float:
+    """estimate_reuse_ratio (alignment.py:741-787) on the device: tokens of the
+    target chunks that find an unused donor chunk with the same digest, or —
+    when no chunk matches — the multiset token overlap, over the target
+    length.  Both stages run on the device; reading the ratio is the one host
+    synchronisation."""
+    a = chunk_alignment(donor_tokens, target_tokens, chunk_size, context_gate=False, device=device)
+    dev = a.match.device
+    ov = token_overlap(donor_tokens, target_tokens, device=dev)
+    matched = torch.where(a.n_pairs > 0, a.n_pairs, ov)
+    return float(matched.item()) / max(a.target_len, 1)
 
 
 @dataclass(frozen=True)
@@ -233,4 +264,6 @@ __all__ = [
     "chunk_digests",
     "compute_chunk_alignment",
     "estimate_chunk_reuse",
+    "estimate_reuse_ratio",
+    "token_overlap",
 ]

@@ -253,6 +253,77 @@ __global__ void __launch_bounds__(kPairThreads) chunk_pairs_kernel(const AlignBa
   }
 }
 
+// Multiset overlap of two token sequences, sum over ids of min(count in
+// donor, count in target): an open-addressing table (linear probing, at most
+// half full) of 64-bit ids with a donor and a target count per slot.  The
+// all-ones id (-1), which marks empty slots, is counted in a slot of its own.
+constexpr uint64_t kEmptyKey = ~0ull;
+
+struct OverlapTable {
+  unsigned long long *keys;  // [cap]
+  unsigned *cnt;             // [cap + 1][2]: donor, target (slot cap: id -1)
+  uint64_t mask;             // cap - 1 (cap a power of two)
+};
+
+__device__ __forceinline__ uint64_t mix64(uint64_t x) {  // splitmix64 finaliser
+  x ^= x >> 30;
+  x *= 0xbf58476d1ce4e5b9ull;
+  x ^= x >> 27;
+  x *= 0x94d049bb133111ebull;
+  return x ^ (x >> 31);
+}
+
+template <typename ID, typename IT>
+__global__ void overlap_count_kernel(const ID *__restrict__ donor, int64_t n_d, const IT *__restrict__ target,
+                                     int64_t n_t, OverlapTable T) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n_d + n_t) return;
+  const bool is_t = i >= n_d;
+  const uint64_t key = is_t ? (uint64_t)(int64_t)target[i - n_d] : (uint64_t)(int64_t)donor[i];
+  uint64_t slot;
+  if (key == kEmptyKey) {
+    slot = T.mask + 1;
+  } else {
+    slot = mix64(key) & T.mask;
+    // at most half full: the probe ends at the key or at an empty slot
+    for (uint64_t n = 0; n <= T.mask; ++n) {
+      const unsigned long long prev = atomicCAS(&T.keys[slot], kEmptyKey, (unsigned long long)key);
+      if (prev == kEmptyKey || prev == key) break;
+      slot = (slot + 1) & T.mask;
+    }
+  }
+  atomicAdd(&T.cnt[2 * slot + (is_t ? 1 : 0)], 1u);
+}
+
+__global__ void overlap_sum_kernel(OverlapTable T, unsigned long long *__restrict__ out) {
+  unsigned long long acc = 0;
+  for (uint64_t s = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; s <= T.mask + 1;
+       s += (uint64_t)gridDim.x * blockDim.x)
+    acc += min(T.cnt[2 * s], T.cnt[2 * s + 1]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  if ((threadIdx.x & 31) == 0 && acc) atomicAdd(out, acc);
+}
+
+uint64_t overlap_capacity(int64_t n_d, int64_t n_t) {
+  uint64_t cap = 1024;
+  while (cap < 2 * (uint64_t)(n_d + n_t)) cap <<= 1;
+  return cap;
+}
+
+int64_t overlap_workspace_bytes(int64_t n_d, int64_t n_t) {
+  const uint64_t cap = overlap_capacity(n_d, n_t);
+  return (int64_t)(cap * 8 + (cap + 1) * 8);
+}
+
+template <typename ID, typename IT>
+void launch_overlap_count(const void *d, int64_t n_d, const void *t, int64_t n_t, const OverlapTable &T,
+                          cudaStream_t st) {
+  const unsigned grid = (unsigned)((n_d + n_t + 255) / 256);
+  overlap_count_kernel<ID, IT><<<grid, 256, 0, st>>>(static_cast<const ID *>(d), n_d, static_cast<const IT *>(t),
+                                                      n_t, T);
+}
+
 int launch_align(const AlignBatch &B, cudaStream_t st) {
   chunk_match_kernel<<<(unsigned)B.n, kMatchThreads, 0, st>>>(B);
   int s = launch_status();
@@ -371,4 +442,53 @@ extern "C" SB_API int sb_chunk_align_batch(const uint32_t *donor_digests, const 
   B.chunk = chunk, B.gate = context_gate ? 1 : 0;
   B.match = match, B.dpos = donor_positions, B.tpos = target_positions, B.n_pairs = n_pairs;
   return launch_align(B, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" SB_API int64_t sb_token_overlap_workspace_bytes(int64_t n_donor_tokens, int64_t n_target_tokens) {
+  if (n_donor_tokens < 0 || n_target_tokens < 0) return SB_ERR_INVALID_ARGUMENT;
+  return sb::overlap_workspace_bytes(n_donor_tokens, n_target_tokens);
+}
+
+extern "C" SB_API int sb_token_overlap(const void *donor_tokens, int32_t donor_dtype, int64_t n_donor_tokens,
+                                       const void *target_tokens, int32_t target_dtype, int64_t n_target_tokens,
+                                       void *workspace, int64_t workspace_bytes, int64_t *overlap, void *stream) {
+  using namespace sb;
+  if (n_donor_tokens < 0 || n_target_tokens < 0 || !overlap) return SB_ERR_INVALID_ARGUMENT;
+  if ((donor_dtype != SB_INDEX_I32 && donor_dtype != SB_INDEX_I64) ||
+      (target_dtype != SB_INDEX_I32 && target_dtype != SB_INDEX_I64))
+    return SB_ERR_UNSUPPORTED;
+  if (n_donor_tokens + n_target_tokens > 0x7fffffffLL) return SB_ERR_TOO_LARGE;  // 32-bit counts per id
+  if ((n_donor_tokens > 0 && !donor_tokens) || (n_target_tokens > 0 && !target_tokens))
+    return SB_ERR_INVALID_ARGUMENT;
+  const int64_t need = overlap_workspace_bytes(n_donor_tokens, n_target_tokens);
+  if (!workspace || workspace_bytes < need) return SB_ERR_WORKSPACE_TOO_SMALL;
+  if (reinterpret_cast<uintptr_t>(workspace) % 8) return SB_ERR_INVALID_ARGUMENT;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const uint64_t cap = overlap_capacity(n_donor_tokens, n_target_tokens);
+  OverlapTable T;
+  T.keys = static_cast<unsigned long long *>(workspace);
+  T.cnt = reinterpret_cast<unsigned *>(T.keys + cap);
+  T.mask = cap - 1;
+  cudaError_t e = cudaMemsetAsync(T.keys, 0xff, cap * 8, st);
+  if (e == cudaSuccess) e = cudaMemsetAsync(T.cnt, 0, (cap + 1) * 8, st);
+  if (e == cudaSuccess) e = cudaMemsetAsync(overlap, 0, sizeof(int64_t), st);
+  if (e != cudaSuccess) {
+    set_last_cuda_error(e);
+    return SB_ERR_CUDA;
+  }
+  if (n_donor_tokens == 0 || n_target_tokens == 0) return SB_OK;
+  const bool d64 = donor_dtype == SB_INDEX_I64, t64 = target_dtype == SB_INDEX_I64;
+  if (d64 && t64)
+    launch_overlap_count<int64_t, int64_t>(donor_tokens, n_donor_tokens, target_tokens, n_target_tokens, T, st);
+  else if (d64)
+    launch_overlap_count<int64_t, int32_t>(donor_tokens, n_donor_tokens, target_tokens, n_target_tokens, T, st);
+  else if (t64)
+    launch_overlap_count<int32_t, int64_t>(donor_tokens, n_donor_tokens, target_tokens, n_target_tokens, T, st);
+  else
+    launch_overlap_count<int32_t, int32_t>(donor_tokens, n_donor_tokens, target_tokens, n_target_tokens, T, st);
+  int s = launch_status();
+  if (s != SB_OK) return s;
+  const unsigned grid = (unsigned)std::min<uint64_t>((cap + 1 + 255) / 256, 1184);
+  overlap_sum_kernel<<<grid, 256, 0, st>>>(T, reinterpret_cast<unsigned long long *>(overlap));
+  return launch_status();
 }

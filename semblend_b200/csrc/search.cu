@@ -357,7 +357,28 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc::tmem_ld32(base + c + 32, r1);
           tc::tmem_ld_wait();
           if (!active) continue;
-          // compact hot path: one compare per column into a hit mask
+          // hot path: the 64 columns' maximum (NaN-propagating 3-input max, ~0.5
+          // instruction per column) against the cut; almost every group ends here
+          {
+            float a[22];
+#pragma unroll
+            for (int i = 0; i < 10; ++i)
+              a[i] = tc::max3_nan(__uint_as_float(r0[3 * i]), __uint_as_float(r0[3 * i + 1]),
+                                  __uint_as_float(r0[3 * i + 2]));
+            a[10] = tc::max3_nan(__uint_as_float(r0[30]), __uint_as_float(r0[31]), __uint_as_float(r1[0]));
+#pragma unroll
+            for (int i = 0; i < 10; ++i)
+              a[11 + i] = tc::max3_nan(__uint_as_float(r1[3 * i + 1]), __uint_as_float(r1[3 * i + 2]),
+                                       __uint_as_float(r1[3 * i + 3]));
+            a[21] = __uint_as_float(r1[31]);
+#pragma unroll
+            for (int i = 0; i < 7; ++i) a[i] = tc::max3_nan(a[3 * i], a[3 * i + 1], a[3 * i + 2]);
+            a[7] = a[21];  // a[0..7]: 8 partial maxima
+            const float mx = tc::max3_nan(tc::max3_nan(a[0], a[1], a[2]), tc::max3_nan(a[3], a[4], a[5]),
+                                          tc::max3_nan(a[6], a[7], a[7]));
+            if (mx < cut) continue;  // false for NaN: such groups take the exact path below
+          }
+          // one compare per column into a hit mask
           // (!(x < cut) also keeps NaN scores, and everything once cut is -inf)
           uint32_t h0 = 0, h1 = 0;
 #pragma unroll

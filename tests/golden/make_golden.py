@@ -273,6 +273,19 @@ def main() -> int:
     align_case("align_gate", 31, 256, 24, True)
     align_case("align_nogate", 32, 256, 24, False)
     align_case("align_small", 33, 16, 60, True)
+
+    # estimate_reuse_ratio's token-multiset fallback (:776-785): no full chunk in common
+    def reuse_case(name, seed, chunk, n_donor, n_shared, n_new):
+        rng = np.random.default_rng(seed)
+        donor = rng.integers(0, 300, n_donor).astype(np.int64)  # small vocabulary: repeated ids
+        shared = rng.permutation(donor)[:n_shared]
+        target = np.concatenate([shared, rng.integers(200, 600, n_new)]).astype(np.int64)
+        dl, tl = donor.tolist(), target.tolist()
+        save(name, donor=donor, target=target, chunk=chunk,
+             estimate=al.estimate_reuse_ratio(dl, tl, chunk_size=chunk))
+
+    reuse_case("reuse_fallback", 41, 64, 5 * 64 + 7, 3 * 64, 2 * 64 + 5)
+    reuse_case("reuse_short", 42, 256, 900, 100, 50)
     print("wrote", sorted(p.name for p in HERE.glob("*.npz")), "plans.json")
     return 0
 

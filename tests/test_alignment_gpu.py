@@ -136,6 +136,30 @@ def test_alignment_batch_vs_oracle(gate):
     assert al.chunk_alignment_batch([], [], chunk) == []
 
 
+@pytest.mark.parametrize("name", ["align_gate", "align_nogate", "align_small", "reuse_fallback", "reuse_short"])
+def test_estimate_reuse_ratio_matches_reference_golden(name):
+    g = load_golden(name)
+    chunk = int(g["chunk"])
+    got = al.estimate_reuse_ratio(g["donor"].to(DEV), g["target"].to(DEV), chunk)
+    assert got == float(g["estimate"])
+
+
+def test_token_overlap_vs_oracle():
+    """Repeated ids, int32 beside int64, the id -1 (the table's empty marker),
+    large ids and empty sides."""
+    rng = np.random.default_rng(5)
+    for n_d, n_t, vocab in ((5000, 3000, 50), (20000, 20000, 1 << 40), (1, 1000, 3), (0, 10, 5), (10, 0, 5)):
+        d = rng.integers(-1, vocab, n_d)
+        t = rng.integers(-1, vocab, n_t)
+        want = oal.token_overlap(d.tolist(), t.tolist())
+        got = int(al.token_overlap(torch.from_numpy(d).to(DEV), torch.from_numpy(t).to(DEV)).item())
+        assert got == want, (n_d, n_t, vocab)
+    d = rng.integers(-1, 40, 3000)
+    t = rng.integers(-1, 40, 2000)
+    got = int(al.token_overlap(torch.from_numpy(d).to(DEV, torch.int32), torch.from_numpy(t).to(DEV)).item())
+    assert got == oal.token_overlap(d.tolist(), t.tolist())
+
+
 def test_alignment_edge_cases():
     t = torch.arange(300, dtype=torch.int64, device=DEV)
     a = al.chunk_alignment(torch.empty(0, dtype=torch.int64, device=DEV), t, 256, True)  # empty donor

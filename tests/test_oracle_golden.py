@@ -136,3 +136,15 @@ def test_alignment_oracle_matches_reference(name):
     assert n_match * chunk / len(target) == pytest.approx(float(g["reuse_ratio"]), abs=0)
     est = oal.estimate_chunk_reuse(donor, target, chunk)
     assert est == pytest.approx(float(g["estimate"]), abs=0)
+
+
+@pytest.mark.parametrize("name", ["align_gate", "align_nogate", "align_small", "reuse_fallback", "reuse_short"])
+def test_reuse_ratio_oracle_matches_reference(name):
+    """estimate_reuse_ratio: chunk stage, else the token-multiset fallback."""
+    from oracle import alignment as oal
+
+    g = load_golden(name)
+    donor, target, chunk = g["donor"].tolist(), g["target"].tolist(), int(g["chunk"])
+    assert oal.estimate_reuse_ratio(donor, target, chunk) == pytest.approx(float(g["estimate"]), abs=0)
+    if name.startswith("reuse"):  # these goldens exercise the fallback: no full chunk in common
+        assert not (oal.chunk_matches(donor, target, chunk, False) >= 0).any()
