@@ -150,6 +150,20 @@ SB_API int sb_inject(const sb_inject_desc *descs, int32_t n_desc,
                      const sb_inject_params *params, uint64_t *err_counter,
                      void *stream);
 
+/* Device bytes of the descriptor table sb_inject_many needs for n_desc
+ * descriptors. */
+SB_API int64_t sb_inject_table_bytes(int32_t n_desc);
+
+/* sb_inject for any number of descriptors (every request of a step) in one
+ * launch: the descriptors and each one's first pair tile are copied on the
+ * stream into `table` (device memory, 16-byte aligned, table_bytes >=
+ * sb_inject_table_bytes(n_desc)), which the kernel reads; the table must not
+ * be written again until this launch has run (stream order).  Same
+ * arguments, semantics and replaced reference functions as sb_inject. */
+SB_API int sb_inject_many(const sb_inject_desc *descs, int32_t n_desc,
+                          const sb_inject_params *params, void *table, int64_t table_bytes,
+                          uint64_t *err_counter, void *stream);
+
 /* Bytes of workspace sb_permute_paged needs for n_pairs pairs. */
 SB_API int64_t sb_permute_workspace_bytes(int64_t n_pairs, int32_t n_layers,
                                           int32_t n_heads, int32_t head_dim,

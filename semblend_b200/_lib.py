@@ -101,6 +101,12 @@ class SbAttnTensor(ctypes.Structure):
 _P = ctypes.POINTER
 _SIGNATURES: dict[str, tuple] = {
     "sb_inject": (ctypes.c_int, [_P(SbInjectDesc), ctypes.c_int32, _P(SbInjectParams), ctypes.c_void_p, ctypes.c_void_p]),
+    "sb_inject_table_bytes": (ctypes.c_int64, [ctypes.c_int32]),
+    "sb_inject_many": (
+        ctypes.c_int,
+        [_P(SbInjectDesc), ctypes.c_int32, _P(SbInjectParams), ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p,
+         ctypes.c_void_p],
+    ),
     "sb_permute_workspace_bytes": (ctypes.c_int64, [ctypes.c_int64, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32]),
     "sb_permute_paged": (
         ctypes.c_int,

@@ -19,7 +19,9 @@
 // (rope_correction.py:117-129, triton_kernels.py:106-108, :246-260) and are
 // counted in a device error counter.
 #include <algorithm>
+#include <cstring>
 #include <mutex>
+#include <vector>
 
 #include "common.cuh"
 #include "prof.cuh"
@@ -36,7 +38,7 @@ namespace {
 constexpr int kThreads = 256;
 constexpr int kUnroll = SB_INJECT_UNROLL;
 
-template <int MAXD> struct InjectLaunch {
+struct InjectCommon {
   sb_inject_params p;
   unsigned long long *err;
   int32_t n_desc;
@@ -46,9 +48,44 @@ template <int MAXD> struct InjectLaunch {
   int32_t kv_first;
   int32_t units_per_chunk;
   int64_t n_units;
+};
+
+// Descriptors in the kernel parameters (up to MAXD of them)...
+template <int MAXD> struct InjectLaunch {
+  InjectCommon c;
   int64_t tile_start[MAXD + 1];
   sb_inject_desc desc[MAXD];
 };
+
+// ... or in a device table (any number): tile_start[n_desc + 1] after desc[n_desc].
+struct InjectLaunchTable {
+  InjectCommon c;
+  const sb_inject_desc *desc;
+  const int64_t *tile_start;
+};
+
+// The descriptor owning pair tile `tile` and that descriptor's first tile.
+template <int MAXD>
+__device__ __forceinline__ const sb_inject_desc &find_desc(const InjectLaunch<MAXD> &L, int64_t tile,
+                                                           int64_t &first) {
+  int di = 0;
+#pragma unroll 1
+  while (di + 1 < L.c.n_desc && tile >= L.tile_start[di + 1]) ++di;
+  first = L.tile_start[di];
+  return L.desc[di];
+}
+
+__device__ __forceinline__ const sb_inject_desc &find_desc(const InjectLaunchTable &L, int64_t tile,
+                                                           int64_t &first) {
+  // the last descriptor whose first tile is <= tile (descriptors without pairs own no tile)
+  int lo = 0, hi = L.c.n_desc - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (__ldg(L.tile_start + mid) <= tile) lo = mid; else hi = mid - 1;
+  }
+  first = __ldg(L.tile_start + lo);
+  return L.desc[lo];
+}
 
 __device__ __forceinline__ bool resolve_row(const sb_rows &r, int64_t pos, int64_t &off) {
   if (pos < 0) return false;
@@ -132,20 +169,19 @@ __device__ __forceinline__ void rotate_vectors(Vec<T, VEC> &va, Vec<T, VEC> &vb,
   }
 }
 
-template <typename T, int VEC, int MAXD, bool NOPE>
+template <typename T, int VEC, typename LT, bool NOPE>
 __global__ void __launch_bounds__(kThreads, SB_INJECT_MIN_BLOCKS)
-    inject_kernel(const __grid_constant__ InjectLaunch<MAXD> L) {
-  const int tpr = L.tpr;
+    inject_kernel(const __grid_constant__ LT L) {
+  const InjectCommon &C = L.c;
+  const int tpr = C.tpr;
   const int pl = threadIdx.x / tpr;
   const int slice = threadIdx.x - pl * tpr;
-  if (pl >= L.pairs_per_tile) return;
+  if (pl >= C.pairs_per_tile) return;
 
   const int64_t tile = blockIdx.x;
-  int di = 0;
-#pragma unroll 1
-  while (di + 1 < L.n_desc && tile >= L.tile_start[di + 1]) ++di;
-  const sb_inject_desc &d = L.desc[di];
-  const int64_t pair = (tile - L.tile_start[di]) * L.pairs_per_tile + pl;
+  int64_t first;
+  const sb_inject_desc &d = find_desc(L, tile, first);
+  const int64_t pair = (tile - first) * C.pairs_per_tile + pl;
   if (pair >= d.n_pairs) return;
 
   const int64_t sp = load_index(d.src_pos, pair, d.pos_dtype);
@@ -158,11 +194,11 @@ __global__ void __launch_bounds__(kThreads, SB_INJECT_MIN_BLOCKS)
   bool ok = resolve_row(d.src, srow, soff) && resolve_row(d.dst, drow, doff);
   if (ok && (d.flags & SB_DESC_CHECK_SRC_IN_DST)) ok = resolve_row(d.dst, sp, chk);
   if (!ok) {
-    if (blockIdx.y == 0 && slice == 0 && L.err != nullptr) atomicAdd(L.err, 1ull);
+    if (blockIdx.y == 0 && slice == 0 && C.err != nullptr) atomicAdd(C.err, 1ull);
     return;
   }
 
-  const sb_inject_params &P = L.p;
+  const sb_inject_params &P = C.p;
   const int D = P.head_dim;
   const bool neox = P.rotary_style == SB_ROTARY_NEOX;
   int oa, ob;
@@ -204,8 +240,8 @@ __global__ void __launch_bounds__(kThreads, SB_INJECT_MIN_BLOCKS)
   }
 
   const int H = P.n_heads;
-  const int64_t ua = (int64_t)blockIdx.y * L.units_per_chunk;
-  const int64_t ub = min(ua + (int64_t)L.units_per_chunk, L.n_units);
+  const int64_t ua = (int64_t)blockIdx.y * C.units_per_chunk;
+  const int64_t ub = min(ua + (int64_t)C.units_per_chunk, C.n_units);
   const int64_t sdim = d.src.stride_dim, ddim = d.dst.stride_dim;
 
 #pragma unroll 1
@@ -221,8 +257,8 @@ __global__ void __launch_bounds__(kThreads, SB_INJECT_MIN_BLOCKS)
       if (u < ub) {
         const int h = (int)(u % H);
         const int64_t rest = u / H;
-        const int kv = L.kv_first + (int)(rest % L.n_kv_sel);
-        const int l = (int)(rest / L.n_kv_sel);
+        const int kv = C.kv_first + (int)(rest % C.n_kv_sel);
+        const int l = (int)(rest / C.n_kv_sel);
         const T *s = layer_base<T>(d.src, l) + kv * d.src.stride_kv + h * d.src.stride_head + soff;
         T *t = layer_base<T>(d.dst, l) + kv * d.dst.stride_kv + h * d.dst.stride_head + doff;
         if (VEC == 1) {
@@ -289,34 +325,34 @@ int pick_vec(const sb_inject_desc *descs, int n, int D, int es) {
   return 1;
 }
 
-template <typename T, int VEC, int MAXD>
-int launch_typed(const InjectLaunch<MAXD> &L, dim3 grid, cudaStream_t st) {
+template <typename T, int VEC, typename LT>
+int launch_typed(const LT &L, dim3 grid, cudaStream_t st) {
   const int slot = prof_before(st);
-  if (L.p.k_angle == SB_ANGLE_NOPE && (L.p.kv_select & SB_KV_K))
-    inject_kernel<T, VEC, MAXD, true><<<grid, kThreads, 0, st>>>(L);
+  if (L.c.p.k_angle == SB_ANGLE_NOPE && (L.c.p.kv_select & SB_KV_K))
+    inject_kernel<T, VEC, LT, true><<<grid, kThreads, 0, st>>>(L);
   else
-    inject_kernel<T, VEC, MAXD, false><<<grid, kThreads, 0, st>>>(L);
+    inject_kernel<T, VEC, LT, false><<<grid, kThreads, 0, st>>>(L);
   prof_after(slot, st);
   return launch_status();
 }
 
-template <int MAXD>
-int launch(const InjectLaunch<MAXD> &L, int vec, dim3 grid, cudaStream_t st) {
-  switch (L.p.dtype) {
+template <typename LT>
+int launch(const LT &L, int vec, dim3 grid, cudaStream_t st) {
+  switch (L.c.p.dtype) {
     case SB_DTYPE_F32:
-      if (vec == 4) return launch_typed<float, 4, MAXD>(L, grid, st);
-      if (vec == 2) return launch_typed<float, 2, MAXD>(L, grid, st);
-      return launch_typed<float, 1, MAXD>(L, grid, st);
+      if (vec == 4) return launch_typed<float, 4>(L, grid, st);
+      if (vec == 2) return launch_typed<float, 2>(L, grid, st);
+      return launch_typed<float, 1>(L, grid, st);
     case SB_DTYPE_F16:
-      if (vec == 8) return launch_typed<__half, 8, MAXD>(L, grid, st);
-      if (vec == 4) return launch_typed<__half, 4, MAXD>(L, grid, st);
-      if (vec == 2) return launch_typed<__half, 2, MAXD>(L, grid, st);
-      return launch_typed<__half, 1, MAXD>(L, grid, st);
+      if (vec == 8) return launch_typed<__half, 8>(L, grid, st);
+      if (vec == 4) return launch_typed<__half, 4>(L, grid, st);
+      if (vec == 2) return launch_typed<__half, 2>(L, grid, st);
+      return launch_typed<__half, 1>(L, grid, st);
     case SB_DTYPE_BF16:
-      if (vec == 8) return launch_typed<__nv_bfloat16, 8, MAXD>(L, grid, st);
-      if (vec == 4) return launch_typed<__nv_bfloat16, 4, MAXD>(L, grid, st);
-      if (vec == 2) return launch_typed<__nv_bfloat16, 2, MAXD>(L, grid, st);
-      return launch_typed<__nv_bfloat16, 1, MAXD>(L, grid, st);
+      if (vec == 8) return launch_typed<__nv_bfloat16, 8>(L, grid, st);
+      if (vec == 4) return launch_typed<__nv_bfloat16, 4>(L, grid, st);
+      if (vec == 2) return launch_typed<__nv_bfloat16, 2>(L, grid, st);
+      return launch_typed<__nv_bfloat16, 1>(L, grid, st);
   }
   return SB_ERR_UNSUPPORTED;
 }
@@ -335,53 +371,61 @@ int validate_params(const sb_inject_params *p) {
   return SB_OK;
 }
 
-template <int MAXD>
-int inject_impl(const sb_inject_desc *descs, int n_desc, const sb_inject_params *params,
-                uint64_t *err, cudaStream_t st) {
-  InjectLaunch<MAXD> L;
-  memset(&L, 0, sizeof(L));
-  L.p = *params;
-  L.err = reinterpret_cast<unsigned long long *>(err);
-  L.n_desc = n_desc;
+// Launch geometry shared by both descriptor-table forms: the common fields,
+// each descriptor's first pair tile (tile_start[n_desc + 1]) and the grid.
+// Returns SB_OK with grid.x == 0 when there is nothing to do.
+int plan_inject(const sb_inject_desc *descs, int n_desc, const sb_inject_params *params, uint64_t *err,
+                InjectCommon &C, int64_t *tile_start, int &vec, dim3 &grid) {
+  memset(&C, 0, sizeof(C));
+  C.p = *params;
+  C.err = reinterpret_cast<unsigned long long *>(err);
+  C.n_desc = n_desc;
   const int D = params->head_dim;
   const int es = elem_bytes(params->dtype);
-  const int vec = pick_vec(descs, n_desc, D, es);
-  L.tpr = D / (2 * vec);
-  if (L.tpr > kThreads) return SB_ERR_UNSUPPORTED;
-  L.pairs_per_tile = kThreads / L.tpr;
-  L.n_kv_sel = params->kv_select == SB_KV_BOTH ? 2 : 1;
-  L.kv_first = params->kv_select == SB_KV_V ? 1 : 0;
-  L.n_units = (int64_t)params->n_layers * L.n_kv_sel * params->n_heads;
+  vec = pick_vec(descs, n_desc, D, es);
+  C.tpr = D / (2 * vec);
+  if (C.tpr > kThreads) return SB_ERR_UNSUPPORTED;
+  C.pairs_per_tile = kThreads / C.tpr;
+  C.n_kv_sel = params->kv_select == SB_KV_BOTH ? 2 : 1;
+  C.kv_first = params->kv_select == SB_KV_V ? 1 : 0;
+  C.n_units = (int64_t)params->n_layers * C.n_kv_sel * params->n_heads;
   int64_t tiles = 0;
   for (int i = 0; i < n_desc; ++i) {
-    L.desc[i] = descs[i];
-    L.tile_start[i] = tiles;
-    tiles += (descs[i].n_pairs + L.pairs_per_tile - 1) / L.pairs_per_tile;
+    tile_start[i] = tiles;
+    tiles += (descs[i].n_pairs + C.pairs_per_tile - 1) / C.pairs_per_tile;
   }
-  L.tile_start[n_desc] = tiles;
+  tile_start[n_desc] = tiles;
+  grid = dim3(0, 1);
   if (tiles == 0) return SB_OK;
   if (tiles > 0x7fffffffLL) return SB_ERR_TOO_LARGE;
   // Aim for ~16 waves of resident CTAs so the last wave's imbalance is small,
   // while keeping at least 8 rows per thread to amortise the cos/sin set-up.
   const int64_t target = (int64_t)sm_count() * (2048 / kThreads) * 16;
   int64_t chunks = std::max<int64_t>(1, (target + tiles - 1) / tiles);
-  chunks = std::min<int64_t>(chunks, std::max<int64_t>(1, (L.n_units + 7) / 8));
+  chunks = std::min<int64_t>(chunks, std::max<int64_t>(1, (C.n_units + 7) / 8));
   chunks = std::min<int64_t>(chunks, 65535);
-  int64_t upc = (L.n_units + chunks - 1) / chunks;
-  chunks = (L.n_units + upc - 1) / upc;
+  int64_t upc = (C.n_units + chunks - 1) / chunks;
+  chunks = (C.n_units + upc - 1) / upc;
   if (upc > 0x7fffffffLL) return SB_ERR_TOO_LARGE;
-  L.units_per_chunk = (int32_t)upc;
-  dim3 grid((unsigned)tiles, (unsigned)chunks);
-  return launch<MAXD>(L, vec, grid, st);
+  C.units_per_chunk = (int32_t)upc;
+  grid = dim3((unsigned)tiles, (unsigned)chunks);
+  return SB_OK;
 }
 
-}  // namespace
+template <int MAXD>
+int inject_impl(const sb_inject_desc *descs, int n_desc, const sb_inject_params *params,
+                uint64_t *err, cudaStream_t st) {
+  InjectLaunch<MAXD> L;
+  memset(&L, 0, sizeof(L));
+  int vec = 1;
+  dim3 grid;
+  const int s = plan_inject(descs, n_desc, params, err, L.c, L.tile_start, vec, grid);
+  if (s != SB_OK || grid.x == 0) return s;
+  for (int i = 0; i < n_desc; ++i) L.desc[i] = descs[i];
+  return launch(L, vec, grid, st);
+}
 
-int inject_dispatch(const sb_inject_desc *descs, int32_t n_desc, const sb_inject_params *params,
-                    uint64_t *err_counter, cudaStream_t st) {
-  int s = validate_params(params);
-  if (s != SB_OK) return s;
-  if (n_desc < 0 || n_desc > SB_MAX_INJECT_DESC) return SB_ERR_INVALID_ARGUMENT;
+int validate_descs(const sb_inject_desc *descs, int32_t n_desc) {
   if (n_desc == 0) return SB_OK;
   if (descs == nullptr) return SB_ERR_INVALID_ARGUMENT;
   for (int i = 0; i < n_desc; ++i) {
@@ -394,8 +438,64 @@ int inject_dispatch(const sb_inject_desc *descs, int32_t n_desc, const sb_inject
     if (d.dst_row < SB_ROW_AT_SRC_POS || d.dst_row > SB_ROW_AT_PAIR) return SB_ERR_INVALID_ARGUMENT;
     if (!rows_valid(d.src) || !rows_valid(d.dst)) return SB_ERR_INVALID_ARGUMENT;
   }
+  return SB_OK;
+}
+
+}  // namespace
+
+int64_t inject_table_bytes(int32_t n_desc) {
+  if (n_desc < 0) return SB_ERR_INVALID_ARGUMENT;
+  const int64_t d = (int64_t)n_desc * (int64_t)sizeof(sb_inject_desc);
+  return (d + 15) / 16 * 16 + ((int64_t)n_desc + 1) * 8;
+}
+
+int inject_dispatch(const sb_inject_desc *descs, int32_t n_desc, const sb_inject_params *params,
+                    uint64_t *err_counter, cudaStream_t st) {
+  int s = validate_params(params);
+  if (s != SB_OK) return s;
+  if (n_desc < 0 || n_desc > SB_MAX_INJECT_DESC) return SB_ERR_INVALID_ARGUMENT;
+  if (n_desc == 0) return SB_OK;
+  s = validate_descs(descs, n_desc);
+  if (s != SB_OK) return s;
   if (n_desc == 1) return inject_impl<1>(descs, n_desc, params, err_counter, st);
   return inject_impl<SB_MAX_INJECT_DESC>(descs, n_desc, params, err_counter, st);
+}
+
+// Any number of descriptors in one launch: the table (descriptors, then each
+// descriptor's first pair tile) is staged on the host and copied to `table`
+// on the stream ahead of the kernel.
+int inject_table_dispatch(const sb_inject_desc *descs, int32_t n_desc, const sb_inject_params *params,
+                          void *table, int64_t table_bytes, uint64_t *err_counter, cudaStream_t st) {
+  int s = validate_params(params);
+  if (s != SB_OK) return s;
+  if (n_desc < 0 || n_desc > (1 << 24)) return SB_ERR_INVALID_ARGUMENT;
+  if (n_desc == 0) return SB_OK;
+  s = validate_descs(descs, n_desc);
+  if (s != SB_OK) return s;
+  const int64_t need = inject_table_bytes(n_desc);
+  if (table == nullptr || table_bytes < need) return SB_ERR_WORKSPACE_TOO_SMALL;
+  if (reinterpret_cast<uintptr_t>(table) % 16) return SB_ERR_INVALID_ARGUMENT;
+  const int64_t desc_bytes = (int64_t)n_desc * (int64_t)sizeof(sb_inject_desc);
+  const int64_t ts_off = (desc_bytes + 15) / 16 * 16;
+  std::vector<uint8_t> host((size_t)need, 0);
+  memcpy(host.data(), descs, (size_t)desc_bytes);
+  int64_t *tile_start = reinterpret_cast<int64_t *>(host.data() + ts_off);
+  InjectLaunchTable L;
+  memset(&L, 0, sizeof(L));
+  int vec = 1;
+  dim3 grid;
+  s = plan_inject(descs, n_desc, params, err_counter, L.c, tile_start, vec, grid);
+  if (s != SB_OK || grid.x == 0) return s;
+  uint8_t *dev = static_cast<uint8_t *>(table);
+  // pageable source: staged before this call returns, so `host` may go out of scope
+  const cudaError_t e = cudaMemcpyAsync(dev, host.data(), (size_t)need, cudaMemcpyHostToDevice, st);
+  if (e != cudaSuccess) {
+    set_last_cuda_error(e);
+    return SB_ERR_CUDA;
+  }
+  L.desc = reinterpret_cast<const sb_inject_desc *>(dev);
+  L.tile_start = reinterpret_cast<const int64_t *>(dev + ts_off);
+  return launch(L, vec, grid, st);
 }
 
 }  // namespace sb
@@ -405,6 +505,14 @@ extern "C" SB_API int sb_inject(const sb_inject_desc *descs, int32_t n_desc,
                                 void *stream) {
   return sb::inject_dispatch(descs, n_desc, params, err_counter,
                              reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" SB_API int64_t sb_inject_table_bytes(int32_t n_desc) { return sb::inject_table_bytes(n_desc); }
+
+extern "C" SB_API int sb_inject_many(const sb_inject_desc *descs, int32_t n_desc, const sb_inject_params *params,
+                                     void *table, int64_t table_bytes, uint64_t *err_counter, void *stream) {
+  return sb::inject_table_dispatch(descs, n_desc, params, table, table_bytes, err_counter,
+                                   reinterpret_cast<cudaStream_t>(stream));
 }
 
 extern "C" SB_API int64_t sb_permute_workspace_bytes(int64_t n_pairs, int32_t n_layers,

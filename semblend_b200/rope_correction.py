@@ -54,13 +54,22 @@ def _check_head_dim(head_dim, hd: int, fn: str) -> int:
 
 
 def _launch(descs: Sequence[_lib.SbInjectDesc], p: _lib.SbInjectParams, device: torch.device, what: str):
+    """One kernel launch for all descriptors: up to SB_MAX_INJECT_DESC travel in
+    the kernel parameters (sb_inject), more in a device table (sb_inject_many)."""
     lib = _lib.load()
     err = _lib.err_counter(device)
     stream = _lib.stream_ptr(device)
-    for start in range(0, len(descs), _lib.SB_MAX_INJECT_DESC):
-        chunk = descs[start : start + _lib.SB_MAX_INJECT_DESC]
-        arr = (_lib.SbInjectDesc * len(chunk))(*chunk)
-        _lib.check(lib.sb_inject(arr, len(chunk), p, err.data_ptr(), stream), what)
+    arr = (_lib.SbInjectDesc * len(descs))(*descs)
+    if len(descs) <= _lib.SB_MAX_INJECT_DESC:
+        _lib.check(lib.sb_inject(arr, len(descs), p, err.data_ptr(), stream), what)
+        return
+    nbytes = int(lib.sb_inject_table_bytes(len(descs)))
+    if nbytes < 0:
+        _lib.check(nbytes, what)
+    # the table is read by this launch only; the caching allocator keeps it for this stream until then
+    table = torch.empty((nbytes + 15) // 16 * 16, dtype=torch.uint8, device=device)
+    _lib.check(lib.sb_inject_many(arr, len(descs), p, table.data_ptr(), table.numel(), err.data_ptr(), stream),
+               what)
 
 
 def _pair_desc(src: _lib.SbRows, dst: _lib.SbRows, sp: torch.Tensor, tp: torch.Tensor,

@@ -342,6 +342,39 @@ def test_inject_donors_matches_per_layer_oracle(as_list, mode):
             _split_check(got[layer], want[layer], style="neox")
 
 
+def test_inject_donors_many_requests_one_launch():
+    """More descriptors than the kernel parameters hold (device descriptor
+    table): 150 requests, some without pairs, some with out-of-range pairs."""
+    g = torch.Generator().manual_seed(27)
+    L, H, D, bs, nb = 2, 2, 64, 16, 400
+    cache = torch.randn(L, nb, 2, H, bs, D, generator=g).to(torch.bfloat16)
+    perm = torch.randperm(nb, generator=g)
+    reqs, n_bad = [], 0
+    for r in range(150):
+        Sd = 20 + (r % 7) * 5
+        donor = torch.randn(L, 2, H, Sd, D, generator=g).to(torch.bfloat16)
+        bt = perm[(r * 2) % (nb - 2) : (r * 2) % (nb - 2) + 2].to(torch.int32)
+        n = 0 if r % 11 == 0 else int(torch.randint(1, 20, (1,), generator=g))
+        t = torch.randperm(2 * bs, generator=g)[:n].to(torch.int32)
+        d = torch.randint(0, Sd, (n,), generator=g, dtype=torch.int32)
+        if r % 13 == 5 and n:
+            d[0] = Sd + 3  # out of the donor's range: skipped and counted
+            n_bad += 1
+        reqs.append((donor, bt, d, t))
+    want = cache.clone()
+    for donor, bt, d, t in reqs:
+        for layer in range(L):
+            want[layer] = orope.rope_correct_scatter_paged(want[layer], donor[layer], bt, d, t, 1e4, "neox")
+    c = cache.to(DEV)
+    _lib.skipped_pairs(DEV, reset=True)
+    rc.inject_donors(c, [rc.DonorInjection(x.to(DEV), bt.to(DEV), d.to(DEV), t.to(DEV)) for x, bt, d, t in reqs],
+                     rope_base=1e4, mode="delta", rotary_style="neox")
+    got = c.cpu()
+    assert _lib.skipped_pairs(DEV, reset=True) == n_bad
+    for layer in range(L):
+        _split_check(got[layer], want[layer], style="neox")
+
+
 def _plan_case(seed, multi):
     """A plan over 6 layers (layers 1 and 4 recomputed in full) with reused and
     recomputed target positions, one donor or three."""
