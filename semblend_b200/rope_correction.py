@@ -378,8 +378,8 @@ def inject_donors(
 ) -> None:
     """Inject several requests' donor KV into a multi-layer paged cache.
 
-    One launch covers every layer, head, request and pair (up to 64 requests
-    per launch).  ``kv_cache`` is either ``[L, *per_layer]`` with a per-layer
+    One launch covers every layer, head, request and pair (beyond 64
+    requests the descriptors travel in a device table).  ``kv_cache`` is either ``[L, *per_layer]`` with a per-layer
     ``layout`` or a list of ``L`` per-layer tensors (vLLM's ``kv_caches``).
     ``mode`` is ``"delta"`` (``RoPE(target - donor)``, as
     :func:`rope_correct_scatter_paged`), ``"nope"`` (strip, then apply) or
