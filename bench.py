@@ -980,6 +980,105 @@ def run_c5(args, world: int, rank: int, local: int) -> dict | None:
 
 
 # ---------------------------------------------------------------------------
+# Component: masked QKV projection (the projection step of partial prefill, c4 geometry)
+# ---------------------------------------------------------------------------
+P_HIDDEN = A_HQ * A_D  # 3584: Qwen2-7B's hidden size (28 heads x 128)
+
+
+def run_projection(args, local: int) -> dict:
+    """masked_qkv_projection over c4's batch: per sequence hidden [32768, 3584]
+    bf16 times W [3 * 3584, 3584] plus bias at the ~10 % compute rows (the
+    reference's shapes: one weight row per q/k/v feature), reuse rows zero."""
+    from semblend_b200 import _lib
+    from semblend_b200 import triton_kernels as tk
+
+    dev = torch.device("cuda", local)
+    B, S, hid, nout = args.attn_batch, args.attn_seq, P_HIDDEN, 3 * P_HIDDEN
+    rng = np.random.default_rng(SEED + 5)
+    masks = np.stack([make_attention_mask(rng, S) for _ in range(B)])  # the attention component's rows
+    g = torch.Generator(device=dev).manual_seed(SEED + 13)
+    x = [torch.randn(S, hid, generator=g, device=dev).to(torch.bfloat16) for _ in range(B)]
+    w = (torch.randn(nout, hid, generator=g, device=dev) / np.sqrt(hid)).to(torch.bfloat16)
+    bias = (0.1 * torch.randn(nout, generator=g, device=dev)).to(torch.bfloat16)
+    mk = [torch.from_numpy(m).to(dev) for m in masks]
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    rows = masks.sum(axis=1)
+    flops = 2.0 * float(rows.sum()) * hid * nout
+
+    def step(ms_):
+        return [tk.masked_qkv_projection(x[b], w, ms_[b], bias, status=status) for b in range(B)]
+
+    for _ in range(max(args.warmup, 3)):
+        out = step(mk)
+    torch.cuda.synchronize(dev)
+    # parity spot check: 64 compute rows and 64 reuse rows of sequence 0 against fp32
+    r_c = np.nonzero(masks[0])[0][:: max(1, rows[0] // 64)][:64]
+    r_r = np.nonzero(~masks[0])[0][:64]
+    ref = x[0][r_c].float() @ w.float().T + bias.float()
+    err = float((out[0][r_c].float() - ref).abs().max().item())
+    zero_ok = bool((out[0][r_r] == 0).all().item())
+    steps = max(5, min(args.steps // 10, 30))
+    stream = torch.cuda.current_stream(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with _lib.KernelTimer(steps * B) as kt:
+        e0.record(stream)
+        for _ in range(steps):
+            step(mk)
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1) / steps
+    kms = kt.mean_ms * B  # the GEMM launches of one step
+
+    # end to end: each step's compute masks copied from pinned host memory, the status read back
+    hm = [torch.from_numpy(m).pin_memory() for m in masks]
+    hs = torch.zeros(1, dtype=torch.int32).pin_memory()
+    torch.cuda.synchronize(dev)
+    c0 = time.perf_counter()
+    for _ in range(steps):
+        dm = [h.to(dev, non_blocking=True) for h in hm]
+        step(dm)
+        hs.copy_(status, non_blocking=True)
+        torch.cuda.synchronize(dev)
+    e2e_ms = (time.perf_counter() - c0) * 1e3 / steps
+
+    # the reference's CPU algorithm (every row multiplied, reuse rows zeroed afterwards,
+    # triton_kernels.py:451-522), on a 256-row sample in fp32, scaled to all S rows
+    torch.set_num_threads(os.cpu_count() or 1)
+    xs = x[0][:256].float().cpu()
+    wc, bc = w.float().cpu(), bias.float().cpu()
+    c0 = time.perf_counter()
+    n_rep = 0
+    while time.perf_counter() - c0 < 3.0:
+        torch.addmm(bc, xs, wc.T)
+        n_rep += 1
+    cpu_row_s = (time.perf_counter() - c0) / (n_rep * 256)
+    cpu_step_s = cpu_row_s * S * B
+    pk = peaks()
+    ach = flops / (kms * 1e-3) / 1e12
+    return {
+        "metric": "masked QKV projection TFLOP/s", "value": round(flops / (ms * 1e-3) / 1e12, 1), "unit": "TFLOP/s",
+        "higher_is_better": True, "ms_per_step": round(ms, 4), "steps": steps, "dtype": "bf16",
+        "config": {"workload": f"c4 projection: {B} sequences x {S} tokens, hidden {hid} -> {nout} (q, k, v rows of "
+                               f"W), bias, bf16, the attention component's compute rows ({int(rows.sum())} of "
+                               f"{B * S}); TFLOP/s by 2 x compute rows x {hid} x {nout}",
+                   "max_abs_err_vs_fp32": err, "reuse_rows_zero": zero_ok, "status": int(status.item()),
+                   "step_includes": "zero-filled output, mask to rows, row gather, GEMM + bias + scatter"},
+        "roofline": {"bound": "tensor", "kernel": "gemm_rows_kernel<bf16> (tcgen05, 128 x 256 tiles)",
+                     "achieved": round(ach, 1), "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+                     "frac": round(ach / pk["bf16_tflops"], 4), "kernel_ms": round(kms, 4), "traffic": None,
+                     "peak_source": pk["source"]},
+        "cpu_baseline": {"value": round(flops / cpu_step_s / 1e12, 5), "unit": "TFLOP/s",
+                         "cores": torch.get_num_threads(), "kind": "port",
+                         "sample": f"torch.addmm over a 256-row fp32 sample ({n_rep} repeats, 3 s), scaled to all "
+                                   f"{B * S} rows as the reference multiplies every row; TFLOP/s by compute-row "
+                                   "flops"},
+        "e2e": {"value": round(flops / (e2e_ms * 1e-3) / 1e12, 1), "unit": "TFLOP/s",
+                "h2d_bytes_per_step": int(sum(h.numel() for h in hm)), "d2h_bytes_per_step": 4},
+        "gpu_launches": steps * B * 3,
+    }
+
+
+# ---------------------------------------------------------------------------
 # Chunk-hash alignment (the step before the inject: which donor chunk feeds which target chunk)
 # ---------------------------------------------------------------------------
 AL_VOCAB = 128256  # Llama-3 vocabulary: token ids are int64 in [0, AL_VOCAB)
@@ -1192,7 +1291,7 @@ def main() -> int:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-components", action="store_true", help="skip the search / attention components")
-    ap.add_argument("--only", choices=["all", "search", "attention", "c5", "alignment"], default="all",
+    ap.add_argument("--only", choices=["all", "search", "attention", "c5", "alignment", "projection"], default="all",
                     help="print only that component's line")
     ap.add_argument("--attn-batch", type=int, default=A_B, help="attention batch (c4: 4)")
     ap.add_argument("--attn-seq", type=int, default=A_S, help="attention context (c4: 32768)")
@@ -1209,13 +1308,15 @@ def main() -> int:
             print(json.dumps(line), flush=True)
         return 0
     world, rank, local = dist_setup(args.gpus)
-    if args.only in ("search", "attention", "c5", "alignment"):
+    if args.only in ("search", "attention", "c5", "alignment", "projection"):
         if args.only == "search" and world > 1:
             res = run_search_sharded(args, world, rank, local)
         elif args.only == "c5":
             res = run_c5(args, world, rank, local)
         elif args.only == "alignment":
             res = run_alignment(args, local) if rank == 0 else None
+        elif args.only == "projection":
+            res = run_projection(args, local) if rank == 0 else None
         elif rank == 0:
             res = run_search(args, local) if args.only == "search" else run_attention(args, local)
         else:
@@ -1234,7 +1335,7 @@ def main() -> int:
             line["cpu_baseline"] = cpu_baseline()
         if world == 1 and not args.no_components:
             line["components"] = {"search": run_search(args, local), "attention": run_attention(args, local),
-                                  "alignment": run_alignment(args, local)}
+                                  "projection": run_projection(args, local), "alignment": run_alignment(args, local)}
     if not args.no_components:
         c5 = run_c5(args, world, rank, local)
         if line is not None:
