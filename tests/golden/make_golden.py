@@ -286,6 +286,53 @@ def main() -> int:
 
     reuse_case("reuse_fallback", 41, 64, 5 * 64 + 7, 3 * 64, 2 * 64 + 5)
     reuse_case("reuse_short", 42, 256, 900, 100, 50)
+
+    # --- the SGLang integration's donor store (radix_backend.py:124-211) ---
+    import semblend.integration.sglang.radix_backend as rb
+
+    def radix_case(name, seed, n_ops, max_entries, min_sim):
+        """A replayable run of add_donor / find_donor: re-added keys, evictions,
+        exclusions and exactly tied embeddings; `result` is the id of the found
+        donor's token sequence (-1: none), its similarity in `result_sim`."""
+        rng = np.random.default_rng(seed)
+        dim = 64
+        centers = rng.standard_normal((6, dim)).astype(np.float32)
+        store = rb._SemBlendDonorStore(max_entries=max_entries, min_similarity=min_sim)
+        seqs, ops, seq_id, embs, excl, result, result_sim = [], [], [], [], [], [], []
+        for step in range(n_ops):
+            if step % 5 == 4:  # a lookup
+                q = (centers[int(rng.integers(0, 6))] + 0.3 * rng.standard_normal(dim)).astype(np.float32)
+                if rng.random() < 0.25:  # far from every donor: no match above the threshold
+                    q = rng.standard_normal(dim).astype(np.float32)
+                ex = int(rng.integers(0, len(seqs))) if seqs and rng.random() < 0.4 else -1
+                hit = store.find_donor(q, tuple(seqs[ex]) if ex >= 0 else None)
+                res = -1 if hit is None else next(i for i, t in enumerate(seqs) if tuple(t) == hit.token_ids)
+                sim = float(np.dot(hit.embedding, q / (np.linalg.norm(q) + 1e-10))) if hit is not None else 0.0
+                ops.append(1), seq_id.append(ex), embs.append(q), excl.append(ex)
+                result.append(res), result_sim.append(sim)
+                continue
+            if seqs and rng.random() < 0.15:  # re-add an existing sequence: moves it to the end
+                sid = int(rng.integers(0, len(seqs)))
+                emb = rng.standard_normal(dim).astype(np.float32)
+            else:
+                toks = [int(x) for x in rng.integers(0, 50000, int(rng.integers(200, 400)))]
+                if seqs and rng.random() < 0.1:  # same first 256 ids as an earlier sequence
+                    toks = seqs[-1][:256] + toks[:50]
+                seqs.append(toks)
+                sid = len(seqs) - 1
+                emb = (centers[int(rng.integers(0, 6))] + 0.3 * rng.standard_normal(dim)).astype(np.float32)
+                if rng.random() < 0.15 and len(embs):  # an exactly tied embedding
+                    emb = embs[-1].copy()
+            store.add_donor(tuple(seqs[sid]), emb)
+            ops.append(0), seq_id.append(sid), embs.append(emb), excl.append(-1)
+            result.append(-2), result_sim.append(0.0)
+        lens = np.array([len(t) for t in seqs], np.int64)
+        flat = np.array([x for t in seqs for x in t], np.int32)
+        save(name, op=np.array(ops, np.int64), seq=np.array(seq_id, np.int64), vec=np.stack(embs),
+             result=np.array(result, np.int64), result_sim=np.array(result_sim, np.float64),
+             seq_lens=lens, seq_tokens=flat, max_entries=max_entries, min_similarity=min_sim)
+
+    radix_case("radix_store", 51, 400, 40, 0.6)
     print("wrote", sorted(p.name for p in HERE.glob("*.npz")), "plans.json")
     return 0
 

@@ -148,3 +148,40 @@ def test_reuse_ratio_oracle_matches_reference(name):
     assert oal.estimate_reuse_ratio(donor, target, chunk) == pytest.approx(float(g["estimate"]), abs=0)
     if name.startswith("reuse"):  # these goldens exercise the fallback: no full chunk in common
         assert not (oal.chunk_matches(donor, target, chunk, False) >= 0).any()
+
+
+def radix_replay(store_add, store_find, g):
+    """Replay the golden add_donor / find_donor run; yields (step, found sequence id or -1,
+    similarity of the found donor or None) for every lookup."""
+    lens = g["seq_lens"].numpy()
+    flat = g["seq_tokens"].numpy()
+    offs = np.concatenate([[0], np.cumsum(lens)])
+    seqs = [tuple(int(x) for x in flat[offs[i] : offs[i + 1]]) for i in range(len(lens))]
+    index = {}
+    for i, t in enumerate(seqs):
+        index.setdefault(t, i)
+    op, seq, vec = g["op"].numpy(), g["seq"].numpy(), g["vec"].numpy()
+    for step in range(op.shape[0]):
+        if op[step] == 0:
+            store_add(seqs[seq[step]], vec[step])
+        else:
+            ex = seqs[seq[step]] if seq[step] >= 0 else None
+            toks, sim = store_find(vec[step], ex)
+            yield step, (-1 if toks is None else index[tuple(toks)]), sim
+
+
+def test_radix_oracle_matches_reference():
+    """The SGLang donor store loop (radix_backend.py:144-211), restated in the
+    oracle, against the reference run on the same operations."""
+    from oracle import search as osearch
+
+    g = load_golden("radix_store")
+    ref = osearch.RadixStore(max_entries=int(g["max_entries"]), min_similarity=float(g["min_similarity"]))
+    result, result_sim = g["result"].numpy(), g["result_sim"].numpy()
+    n = 0
+    for step, got, sim in radix_replay(ref.add_donor, ref.find_donor, g):
+        assert got == result[step], step
+        if got >= 0:
+            assert sim == result_sim[step]
+        n += 1
+    assert n == int((g["op"].numpy() == 1).sum()) and (result[g["op"].numpy() == 1] == -1).any()

@@ -286,6 +286,38 @@ def test_radix_store_matches_reference_loop():
                 assert got.token_ids == want or abs(got_sim - want_sim) <= 1e-6
 
 
+def test_radix_store_matches_reference_golden():
+    """The reference's own add_donor / find_donor run (goldens made by the
+    reference): the same donor found at every lookup, up to similarities equal
+    within 1e-6 (ties and the threshold)."""
+    from semblend_b200.radix_store import RadixDonorStore
+    from tests.test_oracle_golden import radix_replay
+
+    g = load_golden("radix_store")
+    dim = g["vec"].shape[1]
+    thr = float(g["min_similarity"])
+    ours = RadixDonorStore(max_entries=int(g["max_entries"]), min_similarity=thr, embedding_dim=dim, device=DEV)
+
+    def find(q, ex):
+        e = ours.find_donor(q, ex)
+        if e is None:
+            return None, None
+        qn = q / (np.linalg.norm(q) + 1e-10)
+        return e.token_ids, float(np.dot(e.embedding, qn))
+
+    result, result_sim = g["result"].numpy(), g["result_sim"].numpy()
+    for step, got, sim in radix_replay(ours.add_donor, find, g):
+        want = result[step]
+        if got == want:
+            continue
+        if want < 0:  # we found one the reference did not: only at the threshold
+            assert sim <= thr + 1e-6, step
+        elif got < 0:
+            assert result_sim[step] <= thr + 1e-6, step
+        else:  # a different donor: an exact tie
+            assert abs(sim - result_sim[step]) <= 1e-6, step
+
+
 def test_cagra_factory_is_the_exact_store():
     """make_donor_store(use_cagra=True) answers like DonorStore (the exact search
     replaces cuVS CAGRA); no index rebuild between adds and finds."""
