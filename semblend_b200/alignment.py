@@ -35,6 +35,23 @@ def _tokens(t, device) -> torch.Tensor:
     return x.contiguous()
 
 
+def _device(device, *seqs) -> torch.device:
+    """The CUDA device to run on: ``device``, else the first CUDA tensor's,
+    else the current one; raises NativeLibraryError without a CUDA device."""
+    if device is None:
+        first = next((x for x in seqs if isinstance(x, torch.Tensor) and x.is_cuda), None)
+        if first is not None:
+            return first.device
+        if not torch.cuda.is_available():
+            raise _lib.NativeLibraryError("no CUDA device: the semblend_b200 kernels run on CUDA devices only "
+                                          "(there is no CPU implementation)")
+        return torch.device("cuda", torch.cuda.current_device())
+    device = torch.device(device)
+    if device.type != "cuda":
+        raise _lib.NativeLibraryError(f"device {device}: the semblend_b200 kernels run on CUDA devices only")
+    return device
+
+
 def chunk_digests(tokens: torch.Tensor, chunk_size: int = DEFAULT_CHUNK_SIZE) -> torch.Tensor:
     """First 128 bits of SHA-256 of every full chunk (token ids as little-endian
     uint32), ``[n_full_chunks, 4]`` int32 holding the big-endian words."""
@@ -80,9 +97,7 @@ def chunk_alignment(donor_tokens, target_tokens, chunk_size: int = DEFAULT_CHUNK
     """Exact chunk alignment on the device (compute_chunk_alignment's
     matching, alignment.py:181-252), without a host synchronisation."""
     gate = _CONTEXT_GATE_ENABLED if context_gate is None else bool(context_gate)
-    if device is None:
-        device = target_tokens.device if isinstance(target_tokens, torch.Tensor) and target_tokens.is_cuda else \
-            torch.device("cuda", torch.cuda.current_device())
+    device = _device(device, target_tokens, donor_tokens)
     d = _tokens(donor_tokens, device)
     t = _tokens(target_tokens, device)
     nd_full = d.shape[0] // chunk_size
@@ -129,9 +144,7 @@ def chunk_alignment_batch(donors, targets, chunk_size: int = DEFAULT_CHUNK_SIZE,
     c = int(chunk_size)
     if c <= 0:
         raise ValueError(f"chunk_size must be positive, got {chunk_size}")
-    if device is None:
-        first = next((x for x in targets + donors if isinstance(x, torch.Tensor) and x.is_cuda), None)
-        device = first.device if first is not None else torch.device("cuda", torch.cuda.current_device())
+    device = _device(device, *targets, *donors)
     ds = [_tokens(x, device) for x in donors]
     ts = [_tokens(x, device) for x in targets]
     dtype = ds[0].dtype if all(x.dtype == ds[0].dtype for x in ds + ts) else torch.int64
@@ -178,9 +191,7 @@ def estimate_chunk_reuse(donor_tokens, target_tokens, chunk_size: int = DEFAULT_
 def token_overlap(donor_tokens, target_tokens, device=None) -> torch.Tensor:
     """Multiset overlap (sum over ids of min(donor count, target count)) as a
     device int64 scalar ``[1]`` (``sb_token_overlap``; no host synchronisation)."""
-    if device is None:
-        first = next((x for x in (target_tokens, donor_tokens) if isinstance(x, torch.Tensor) and x.is_cuda), None)
-        device = first.device if first is not None else torch.device("cuda", torch.cuda.current_device())
+    device = _device(device, target_tokens, donor_tokens)
     d, t = _tokens(donor_tokens, device), _tokens(target_tokens, device)
     lib = _lib.load()
     nbytes = lib.sb_token_overlap_workspace_bytes(d.shape[0], t.shape[0])

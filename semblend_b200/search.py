@@ -44,6 +44,8 @@ class DeviceDonorMatrix:
     def __init__(self, max_entries: int, dim: int, device: torch.device | str | int | None = None,
                  shadow_dtype: torch.dtype = torch.float16):
         if device is None:
+            if not torch.cuda.is_available():
+                raise _lib.NativeLibraryError("DeviceDonorMatrix needs a CUDA device (there is no CPU search path)")
             device = torch.device("cuda", torch.cuda.current_device())
         self.device = torch.device(device) if not isinstance(device, int) else torch.device("cuda", device)
         if self.device.type != "cuda":
