@@ -370,7 +370,9 @@ SB_API int sb_chunk_align(const uint32_t *donor_digests, int32_t n_donor_chunks,
  * count (-1 if its offsets are inconsistent or it has more than
  * max_target_chunks full target chunks; nothing else is written for it).
  * max_target_chunks (<= 65536) is the largest t1 - t0.  Positions are
- * relative to each request's own sequences. */
+ * relative to each request's own sequences; each donor's chunk count times
+ * chunk must fit in int32 (the caller's offsets are not range-checked beyond
+ * the per-request consistency above). */
 SB_API int sb_chunk_align_batch(const uint32_t *donor_digests, const uint32_t *target_digests,
                                 const int32_t *offsets, int32_t n_requests, int32_t max_target_chunks,
                                 int32_t chunk, int32_t context_gate, int32_t *match,

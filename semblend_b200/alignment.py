@@ -153,6 +153,8 @@ def chunk_alignment_batch(donors, targets, chunk_size: int = DEFAULT_CHUNK_SIZE,
     nm = [(x.shape[0] + c - 1) // c for x in ts]
     if max(nt) > 65536:
         raise ValueError("a target has more than 65536 chunks")
+    if max(nd) * c > 0x7FFFFFFF:
+        raise ValueError("donor positions must fit in int32")
     # every sequence's full chunks, donors first: chunk boundaries stay at multiples of chunk_size
     parts = [x[: k * c].to(dtype) for x, k in zip(ds, nd)] + [x[: k * c].to(dtype) for x, k in zip(ts, nt)]
     dig = chunk_digests(torch.cat(parts), c)
