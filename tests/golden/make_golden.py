@@ -1,7 +1,8 @@
 """Generate golden fixtures by running the reference implementation itself.
 
-Imports the reference package (SemBlend 0.3.2) from ``$SEMBLEND_REFERENCE``
-(default: ``/root/reference``; it exists only in the build container), runs its
+Imports the reference package (SemBlend 0.3.2) from the checkout named by
+``$SEMBLEND_REFERENCE`` (default: the build container's read-only copy; the
+GPU machines have none), runs its
 CPU code paths on small seeded inputs and writes ``tests/golden/*.npz`` plus
 ``plans.json``.  The fixtures are committed; nothing at test time reads the
 reference.  Re-run with ``python tests/golden/make_golden.py``.
