@@ -102,3 +102,36 @@ def test_compat_install_aliases_reference_names():
         for k in [k for k in sys.modules if k.split(".")[0] in compat.PARENTS]:
             del sys.modules[k]
         sys.modules.update(saved)
+
+
+def test_reference_callers_bind_the_drop_in():
+    """With the reference checkout importable (the build container), the
+    reference's own callers import on top of ``compat.install()`` and bind the
+    B200 functions; ``patch_sglang`` swaps the SGLang donor store."""
+    from tests.golden.make_golden import REF
+
+    if not (REF / "synapse_kv_connector").is_dir():
+        pytest.skip("reference checkout not present")
+    import importlib
+
+    saved = {k: v for k, v in sys.modules.items() if k.split(".")[0] in compat.PARENTS + ("semblend",)}
+    sys.path.insert(0, str(REF))
+    try:
+        compat.install()
+        ap = importlib.import_module("synapse_kv_connector.attention_patch")
+        for name in ("partial_prefill_attention", "scatter_donor_kv", "partial_prefill", "compute_attention_mask"):
+            assert getattr(ap, name).__module__.startswith("semblend_b200."), name
+        for mod in ("synapse_kv_connector.model_runner_hook", "synapse_kv_connector.semblend_connector",
+                    "synapse_kv_connector.pipeline", "semblend.integration.trtllm.pytorch_backend"):
+            importlib.import_module(mod)  # their hot-path imports resolve through the aliases at call time
+        from semblend_b200.radix_store import RadixDonorStore
+
+        assert compat.patch_sglang()
+        rb = importlib.import_module("semblend.integration.sglang.radix_backend")
+        assert rb._SemBlendDonorStore is RadixDonorStore
+        compat.uninstall()
+    finally:
+        sys.path.remove(str(REF))
+        for k in [k for k in sys.modules if k.split(".")[0] in compat.PARENTS + ("semblend",)]:
+            del sys.modules[k]
+        sys.modules.update(saved)
