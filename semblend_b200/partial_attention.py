@@ -13,6 +13,7 @@ rope_correction.py:434-435).
 
 from __future__ import annotations
 
+import operator
 from collections import Counter
 from dataclasses import dataclass, field
 from enum import Enum
@@ -148,17 +149,40 @@ def build_multi_donor_attention_plan(target_len: int, slot_actions: list[dict],
     )
 
 
-def compute_attention_mask(plan: PartialAttentionPlan, layer_idx: int) -> np.ndarray:
-    """Bool ``[target_len]``: True where the layer recomputes the position
-    (partial_attention.py:233-270); all True for unknown or full layers."""
+_LAYER_CACHE = "_sb_layer_cache"
+
+
+def _partial_layer(plan: PartialAttentionPlan, layer_idx: int):
+    """(mask, pairs) of a partial layer.  Layers whose position lists hold the
+    same PositionMask objects in the same order — every partial layer of a
+    plan from build_attention_plan — share one result, computed on the first
+    call; a list that was since changed no longer matches and is recomputed."""
+    pms = plan.layer_masks[layer_idx].position_masks
+    cache = plan.__dict__.get(_LAYER_CACHE)
+    if cache is None:
+        cache = []
+        object.__setattr__(plan, _LAYER_CACHE, cache)  # frozen dataclass: a private side table
+    for src, mask, pairs in cache:
+        if len(src) == len(pms) and all(map(operator.is_, src, pms)):
+            return mask, pairs
     mask = np.zeros(plan.target_len, dtype=bool)
-    if layer_idx >= len(plan.layer_masks) or plan.layer_masks[layer_idx].recompute_all:
-        mask[:] = True
-        return mask
-    for pm in plan.layer_masks[layer_idx].position_masks:
+    for pm in pms:
         if pm.mode in (AttentionMode.PARTIAL, AttentionMode.FULL) and pm.target_pos < plan.target_len:
             mask[pm.target_pos] = True
-    return mask
+    pairs = [(pm.donor_pos, pm.target_pos) for pm in pms
+             if pm.mode == AttentionMode.REUSE and pm.donor_pos is not None]
+    cache.append((tuple(pms), mask, pairs))
+    return mask, pairs
+
+
+def compute_attention_mask(plan: PartialAttentionPlan, layer_idx: int) -> np.ndarray:
+    """Bool ``[target_len]``: True where the layer recomputes the position
+    (partial_attention.py:233-270); all True for unknown or full layers.  The
+    reference walks the layer's position list on every call; here partial
+    layers sharing one list are walked once per plan."""
+    if layer_idx >= len(plan.layer_masks) or plan.layer_masks[layer_idx].recompute_all:
+        return np.ones(plan.target_len, dtype=bool)
+    return _partial_layer(plan, layer_idx)[0].copy()
 
 
 def compute_donor_kv_indices(plan: PartialAttentionPlan, layer_idx: int) -> list[tuple[int, int]]:
@@ -166,8 +190,7 @@ def compute_donor_kv_indices(plan: PartialAttentionPlan, layer_idx: int) -> list
     (partial_attention.py:273-303); empty for unknown or full layers."""
     if layer_idx >= len(plan.layer_masks) or plan.layer_masks[layer_idx].recompute_all:
         return []
-    return [(pm.donor_pos, pm.target_pos) for pm in plan.layer_masks[layer_idx].position_masks
-            if pm.mode == AttentionMode.REUSE and pm.donor_pos is not None]
+    return list(_partial_layer(plan, layer_idx)[1])
 
 
 # ---------------------------------------------------------------------------

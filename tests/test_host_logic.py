@@ -135,3 +135,28 @@ def test_reference_callers_bind_the_drop_in():
         for k in [k for k in sys.modules if k.split(".")[0] in compat.PARENTS + ("semblend",)]:
             del sys.modules[k]
         sys.modules.update(saved)
+
+
+def test_layer_results_shared_and_invalidated():
+    """Partial layers of one plan share one walk of their position list; a
+    layer list changed afterwards is walked again (results always equal a
+    fresh walk)."""
+    acts = [{"action": "copy_from_donor", "targetPos": i, "donorPos": 100 + i} for i in range(8)]
+    acts += [{"action": "placeholder", "targetPos": i} for i in range(8, 12)]
+    plan = pa.build_attention_plan("d", 12, 200, list(range(8)), list(range(8, 12)), acts,
+                                   [{"recomputeAll": False}, {"recomputeAll": True}], num_layers=4)
+    want_pairs = [(100 + i, i) for i in range(8)]
+    for layer in (0, 2, 3):
+        assert pa.compute_donor_kv_indices(plan, layer) == want_pairs
+        assert pa.compute_attention_mask(plan, layer).tolist() == [False] * 8 + [True] * 4
+    assert pa.compute_donor_kv_indices(plan, 1) == [] and pa.compute_attention_mask(plan, 1).all()
+    # returned objects are copies: mutating them does not leak into later calls
+    pa.compute_donor_kv_indices(plan, 0).clear()
+    pa.compute_attention_mask(plan, 0)[:] = True
+    assert pa.compute_donor_kv_indices(plan, 2) == want_pairs
+    assert pa.compute_attention_mask(plan, 2).sum() == 4
+    # a caller edits one layer's list: that layer is recomputed, the others keep theirs
+    plan.layer_masks[3].position_masks[0] = pa.PositionMask(target_pos=0, mode=pa.AttentionMode.PARTIAL)
+    assert pa.compute_donor_kv_indices(plan, 3) == want_pairs[1:]
+    assert pa.compute_attention_mask(plan, 3).tolist() == [True] + [False] * 7 + [True] * 4
+    assert pa.compute_donor_kv_indices(plan, 0) == want_pairs
