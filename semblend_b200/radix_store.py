@@ -22,6 +22,7 @@ from .search import DeviceDonorMatrix
 
 KEY_TOKENS = 256  # radix_backend.py:165: the first 256 token ids are the dedup key
 _FETCH = 8  # candidates per query: the excluded entry plus exact ties of the best
+_FETCH_MAX = 32  # the search's largest k: more exact ties than this resolve by slot order
 
 
 class _DonorEntry:
@@ -88,21 +89,28 @@ class RadixDonorStore:
             return None
         q = np.asarray(query_embedding, dtype=np.float32)
         q = q / (np.linalg.norm(q) + 1e-10)
-        k = min(_FETCH, len(self._entries))
-        ids, scores = self._matrix.search(torch.from_numpy(q).reshape(1, -1), k, self._min_similarity)
-        ids, scores = ids[0].cpu().tolist(), scores[0].cpu().tolist()
+        qt = torch.from_numpy(q).reshape(1, -1)
         exclude = exclude_tokens[:KEY_TOKENS] if exclude_tokens else None
-        best, best_sim = None, self._min_similarity
-        for slot, sim in zip(ids, scores):
-            if slot < 0:
-                break
-            entry = self._slot_entry[slot]
-            if entry is None or (exclude is not None and entry.token_ids[:KEY_TOKENS] == exclude):
-                continue
-            # strictly above the running best; on an exact tie the earlier-added entry wins
-            if sim > best_sim or (best is not None and sim == best_sim and entry.seq < best.seq):
-                best, best_sim = entry, sim
-        return best
+        n = len(self._entries)
+        k = min(_FETCH, n)
+        while True:
+            ids, scores = self._matrix.search(qt, k, self._min_similarity)
+            ids, scores = ids[0].cpu().tolist(), scores[0].cpu().tolist()
+            best, best_sim = None, self._min_similarity
+            for slot, sim in zip(ids, scores):
+                if slot < 0:
+                    break
+                entry = self._slot_entry[slot]
+                if entry is None or (exclude is not None and entry.token_ids[:KEY_TOKENS] == exclude):
+                    continue
+                # strictly above the running best; on an exact tie the earlier-added entry wins
+                if sim > best_sim or (best is not None and sim == best_sim and entry.seq < best.seq):
+                    best, best_sim = entry, sim
+            # the search orders ties by slot, not by age: when the tie reaches the last fetched
+            # candidate, fetch more so the earliest-added tied entry is among them
+            if best is None or k >= min(n, _FETCH_MAX) or ids[-1] < 0 or scores[-1] != best_sim:
+                return best
+            k = min(n, _FETCH_MAX, 4 * k)
 
 
 # the reference's class name, for callers that construct it directly

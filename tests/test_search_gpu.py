@@ -286,6 +286,33 @@ def test_radix_store_matches_reference_loop():
                 assert got.token_ids == want or abs(got_sim - want_sim) <= 1e-6
 
 
+def test_radix_store_ties_beyond_the_first_candidates():
+    """Twelve exactly tied donors whose slots (recycled after evictions) are not
+    in insertion order: the earliest-added one wins, as in the reference's loop."""
+    from semblend_b200.radix_store import RadixDonorStore
+
+    rng = np.random.default_rng(23)
+    dim = 64
+    ref = osearch.RadixStore(max_entries=16, min_similarity=0.5)
+    ours = RadixDonorStore(max_entries=16, min_similarity=0.5, embedding_dim=dim, device=DEV)
+    tied = rng.standard_normal(dim).astype(np.float32)
+    for i in range(16):  # fill the store, then let the tied donors take recycled slots in mixed order
+        emb = rng.standard_normal(dim).astype(np.float32)
+        ref.add_donor((i,), emb)
+        ours.add_donor((i,), emb)
+    for j in range(12):
+        toks = (1000 + j,)
+        if j % 3 == 0:  # touch an old entry so evictions do not follow slot order
+            ref.add_donor((13 - j // 3,), tied)
+            ours.add_donor((13 - j // 3,), tied)
+        ref.add_donor(toks, tied)
+        ours.add_donor(toks, tied)
+    for ex in (None, (1000,), (1003,)):
+        want, _ = ref.find_donor(tied, ex)
+        got = ours.find_donor(tied, ex)
+        assert want is not None and got is not None and got.token_ids == want, (ex, got.token_ids, want)
+
+
 def test_radix_store_matches_reference_golden():
     """The reference's own add_donor / find_donor run (goldens made by the
     reference): the same donor found at every lookup, up to similarities equal
