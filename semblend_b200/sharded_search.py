@@ -30,10 +30,12 @@ def shard_bounds(n_rows: int, world: int) -> list[tuple[int, int]]:
 class ShardedDonorMatrix:
     """Row-sharded donor matrix; ``search`` returns the global top-k on every rank.
 
-    ``local_search(queries, k, thr, id_offset) -> (ids, scores)`` and
-    ``merge(ids [W, Q, k], scores [W, Q, k]) -> (ids, scores)`` default to the
-    GPU kernels; they are parameters so the exchange and merge logic can run
-    on CPU process groups too.
+    ``local_search(queries, k, thr, id_offset, capacity) -> (ids, scores,
+    status)`` (status as ``sb_cosine_topk`` sets it: bit 0 = capacity
+    overflow, >= 2 = a wait timed out) and ``merge(ids [W, Q, k], scores
+    [W, Q, k]) -> (ids, scores)`` default to the GPU kernels; they are
+    parameters so the exchange, retry and merge logic can run on CPU process
+    groups too.
     """
 
     def __init__(self, n_rows: int, dim: int, group=None, device=None, shadow_dtype=torch.float16,
@@ -93,10 +95,10 @@ class ShardedDonorMatrix:
         sc_v = send[8 * qk : 12 * qk].view(torch.float32).view(nq, kk)
         st_v = send[12 * qk : 12 * qk + 4].view(torch.int32)
         if self._local_search is not None:
-            ids, scores = self._local_search(queries, kk, min_similarity, self.row_begin)
+            ids, scores, st = self._local_search(queries, kk, min_similarity, self.row_begin, capacity)
             ids_v.copy_(ids)
             sc_v.copy_(scores)
-            st_v.zero_()
+            st_v.fill_(int(st))
         else:
             m = self.local
             q = queries.to(device=m.device, dtype=torch.float32).contiguous()

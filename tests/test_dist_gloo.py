@@ -60,16 +60,37 @@ def _worker(rank, world, port, mode, result_path):
         E, Q = _data()
         a, b = shard_bounds(E.shape[0], world)[rank]
 
-        def local_search(queries, k, thr, offset):
+        calls = []
+
+        def local_search(queries, k, thr, offset, capacity):
+            calls.append(capacity)
             ids, sc = osearch.topk_batch(E[a:b], np.ones(b - a, bool), queries.numpy(), thr, k)
             ids = np.where(ids >= 0, ids + offset, -1)
-            return torch.from_numpy(ids), torch.from_numpy(sc)
+            status = 0
+            if mode == "overflow" and rank == 1 and capacity < 1000:
+                status = 1  # this shard had more screening candidates than the capacity
+            if mode == "timeout" and rank == 0:
+                status = 2  # a kernel wait gave up on this shard
+            return torch.from_numpy(ids), torch.from_numpy(sc), status
 
         m = ShardedDonorMatrix(E.shape[0], E.shape[1], local_search=local_search, merge=_cpu_merge)
         assert (m.row_begin, m.row_end) == (a, b)
         if mode == "die" and rank == 1:
             os._exit(3)  # leaves without joining the collective
-        ids, sc = m.search(torch.from_numpy(Q), 5, 0.5)
+        if mode == "timeout":  # every rank sees the failing shard's status and raises
+            from semblend_b200._lib import NativeLibraryError
+
+            try:
+                m.search(torch.from_numpy(Q), 5, 0.5, capacity=64)
+            except NativeLibraryError:
+                if rank == 0:
+                    torch.save({"raised": True}, result_path)
+                dist.destroy_process_group()
+                return
+            raise AssertionError("no error for a timed-out shard")
+        ids, sc = m.search(torch.from_numpy(Q), 5, 0.5, capacity=64)
+        if mode == "overflow":  # both ranks retried together: 64 -> 256 -> 1024
+            assert calls == [64, 256, 1024], calls
         batched = m.search_batches([torch.from_numpy(Q)] * 2, 5, 0.5)
         for bi, bs, bst in batched:
             assert torch.equal(bi, ids) and torch.equal(bs, sc) and int(bst.abs().sum()) == 0
@@ -106,6 +127,20 @@ def test_sharded_search_equals_single_search(tmp_path):
     np.testing.assert_allclose(got_s, want_s, atol=1e-6)
     diff = got_i != want_i
     assert np.all(np.abs(got_s[diff] - want_s[diff]) <= 1e-6)  # ids differ only on ties
+
+
+def test_capacity_overflow_on_one_shard_retries_on_every_rank(tmp_path):
+    res, codes = _run("overflow", tmp_path)
+    assert codes == [0, 0], res.get("error")
+    E, Q = _data()
+    want_i, want_s = osearch.topk_batch(E, np.ones(E.shape[0], bool), Q, 0.5, 5)
+    np.testing.assert_allclose(res["scores"].numpy(), want_s, atol=1e-6)
+
+
+def test_timed_out_shard_raises_on_every_rank(tmp_path):
+    res, codes = _run("timeout", tmp_path)
+    assert codes == [0, 0], res.get("error")
+    assert res.get("raised") is True
 
 
 def test_dead_rank_surfaces_as_an_error_not_a_hang(tmp_path):
