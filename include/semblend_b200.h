@@ -164,7 +164,8 @@ SB_API int sb_inject_many(const sb_inject_desc *descs, int32_t n_desc,
                           const sb_inject_params *params, void *table, int64_t table_bytes,
                           uint64_t *err_counter, void *stream);
 
-/* Bytes of workspace sb_permute_paged needs for n_pairs pairs. */
+/* Bytes of workspace sb_permute_paged needs for n_pairs pairs; -1 for an
+ * invalid argument or a size that overflows int64. */
 SB_API int64_t sb_permute_workspace_bytes(int64_t n_pairs, int32_t n_layers,
                                           int32_t n_heads, int32_t head_dim,
                                           int32_t dtype);
@@ -197,12 +198,15 @@ SB_API int sb_permute_paged(const sb_rows *cache, const void *src_pos,
  * rows are snapshotted into a fixed SB_PERMUTE_NOALLOC_SCRATCH_BYTES device
  * array inside this library (held on every GPU that loads it until exit).
  * Returns SB_ERR_TOO_LARGE, launching nothing, when
- * sb_permute_workspace_bytes(...) exceeds that size.  It allocates nothing.
- * The first call on a device resolves the array's device address, so make
- * that call before any stream capture.  All calls share the one array: calls
- * whose executions overlap on the GPU (other streams, other threads) race on
- * it and must be serialised by the caller.  No counterpart in the reference
- * (its permutation allocates with torch). */
+ * sb_permute_workspace_bytes(...) exceeds that size (or overflows).  It
+ * allocates nothing.  The first call in each CUDA context (the device's
+ * primary context, or a driver-API context current on the calling thread)
+ * resolves the array's device address in that context; make that call before
+ * any stream capture.  A context destroyed and created again (cudaDeviceReset)
+ * counts as a new context.  All calls share the one array, which keeps the
+ * last call's rows: calls whose executions overlap on the GPU (other streams,
+ * other threads) race on it and must be serialised by the caller.  No
+ * counterpart in the reference (its permutation allocates with torch). */
 SB_API int sb_permute_paged_noalloc(const sb_rows *cache, const void *src_pos,
                                     const void *dst_pos, int64_t n_pairs, int32_t pos_dtype,
                                     const sb_inject_params *params, uint64_t *err_counter,

@@ -116,17 +116,21 @@ def _paged_pairs(d_pos, t_pos, bt, bs, nb, src_len):
 
 
 def rope_correct_scatter_paged(kv_cache, donor_kv, block_table, donor_positions, target_positions,
-                               rope_base=10000.0, rotary_style="interleaved", layout="canonical"):
+                               rope_base=10000.0, rotary_style="interleaved", layout="canonical",
+                               return_applied=False, inplace=False):
     """rope_correction.py:285-328 (CPU path) with the Triton skip conditions.
-    Returns an updated copy of ``kv_cache``."""
-    out = kv_cache.clone()
+    Returns an updated copy of ``kv_cache`` (``kv_cache`` itself, updated, with
+    ``inplace`` — the reference's CPU path writes in place); with
+    ``return_applied`` also the number of pairs that were applied (in range,
+    last write per target row)."""
+    out = kv_cache if inplace else kv_cache.clone()
     cv = canonical_view(out, layout)
     nb, _, _, bs, D = cv.shape
     inv = inv_freq(rope_base, D)
     pairs = _paged_pairs(donor_positions.tolist(), target_positions.tolist(),
                          block_table.tolist(), bs, nb, donor_kv.shape[2])
     if not pairs:
-        return out
+        return (out, 0) if return_applied else out
     d = torch.tensor([p[0] for p in pairs])
     pb = torch.tensor([p[2] for p in pairs])
     off = torch.tensor([p[3] for p in pairs])
@@ -135,7 +139,7 @@ def rope_correct_scatter_paged(kv_cache, donor_kv, block_table, donor_positions,
     cos, sin = _per_scalar_tables([float(p[1] - p[0]) for p in pairs], inv)
     kr = _rotate(k, cos[:, None, :], sin[:, None, :])
     cv[pb, 0, :, off, :] = from_interleaved(kr, rotary_style).to(out.dtype)
-    return out
+    return (out, len(pairs)) if return_applied else out
 
 
 def scatter_donor_kv_paged(kv_cache, donor_kv, block_table, donor_positions, target_positions,

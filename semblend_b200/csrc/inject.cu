@@ -23,6 +23,8 @@
 #include <mutex>
 #include <vector>
 
+#include <cuda.h>
+
 #include "common.cuh"
 #include "prof.cuh"
 
@@ -400,9 +402,14 @@ int plan_inject(const sb_inject_desc *descs, int n_desc, const sb_inject_params 
   if (tiles > 0x7fffffffLL) return SB_ERR_TOO_LARGE;
   // Aim for ~16 waves of resident CTAs so the last wave's imbalance is small,
   // while keeping at least 8 rows per thread to amortise the cos/sin set-up.
+  // A launch with fewer pair tiles than two waves of resident CTAs (one
+  // layer of a few thousand pairs) would leave SMs idle at 8 rows per
+  // thread: there each thread keeps only the rows it has in flight at once.
+  const int64_t slots = (int64_t)sm_count() * SB_INJECT_MIN_BLOCKS;
+  const int64_t min_rows = tiles >= 2 * slots ? 8 : kUnroll;
   const int64_t target = (int64_t)sm_count() * (2048 / kThreads) * 16;
   int64_t chunks = std::max<int64_t>(1, (target + tiles - 1) / tiles);
-  chunks = std::min<int64_t>(chunks, std::max<int64_t>(1, (C.n_units + 7) / 8));
+  chunks = std::min<int64_t>(chunks, std::max<int64_t>(1, (C.n_units + min_rows - 1) / min_rows));
   chunks = std::min<int64_t>(chunks, 65535);
   int64_t upc = (C.n_units + chunks - 1) / chunks;
   chunks = (C.n_units + upc - 1) / upc;
@@ -520,7 +527,11 @@ extern "C" SB_API int64_t sb_permute_workspace_bytes(int64_t n_pairs, int32_t n_
                                                      int32_t dtype) {
   const int es = sb::elem_bytes(dtype);
   if (es == 0 || n_pairs < 0 || n_layers <= 0 || n_heads <= 0 || head_dim <= 0) return -1;
-  return n_pairs * (int64_t)n_layers * 2 * n_heads * head_dim * es;
+  // n_pairs * n_layers * 2 * n_heads * head_dim * es, rejected (-1) if it overflows int64
+  int64_t b = n_pairs;
+  for (const int64_t f : {(int64_t)n_layers, (int64_t)2, (int64_t)n_heads, (int64_t)head_dim, (int64_t)es})
+    if (__builtin_mul_overflow(b, f, &b)) return -1;
+  return b;
 }
 
 extern "C" SB_API int sb_permute_paged(const sb_rows *cache, const void *src_pos,
@@ -594,8 +605,69 @@ static __device__ __align__(256) unsigned char g_permute_scratch[SB_PERMUTE_NOAL
 
 namespace sb {
 namespace {
+// The array's device address is resolved once per CUDA context.  Contexts are
+// told apart by cuCtxGetId, an id the driver never reuses within a process, so
+// a context destroyed and created again (cudaDeviceReset) or a driver-API
+// context of the caller's own on the same device resolves the address anew.
+typedef CUresult (*ctx_get_current_fn)(CUcontext *);
+typedef CUresult (*ctx_get_id_fn)(CUcontext, unsigned long long *);
+constexpr int kScratchSlots = 64;
 std::mutex g_scratch_mu;
-void *g_scratch_ptr[64] = {};  // device address of g_permute_scratch, per device ordinal
+unsigned long long g_scratch_ctx[kScratchSlots] = {};  // context id + 1 (0 = empty slot)
+void *g_scratch_ptr[kScratchSlots] = {};
+int g_scratch_next = 0;
+
+template <typename F>
+F driver_fn(const char *name) {
+  void *p = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  if (cudaGetDriverEntryPoint(name, &p, cudaEnableDefault, &q) != cudaSuccess ||
+      q != cudaDriverEntryPointSuccess)
+    return nullptr;
+  return reinterpret_cast<F>(p);
+}
+
+// The device address of g_permute_scratch in the calling thread's current
+// context (the device's primary context if none is current yet).
+int scratch_address(void **out) {
+  static ctx_get_current_fn get_current = driver_fn<ctx_get_current_fn>("cuCtxGetCurrent");
+  static ctx_get_id_fn get_id = driver_fn<ctx_get_id_fn>("cuCtxGetId");
+  if (get_current == nullptr || get_id == nullptr) return SB_ERR_UNSUPPORTED;
+  CUcontext ctx = nullptr;
+  if (get_current(&ctx) != CUDA_SUCCESS) return SB_ERR_CUDA;
+  void *p = nullptr;
+  cudaError_t e = cudaSuccess;
+  if (ctx == nullptr) {
+    // no context current yet: this runtime call makes the device's primary context current
+    e = cudaGetSymbolAddress(&p, g_permute_scratch);
+    if (e != cudaSuccess || get_current(&ctx) != CUDA_SUCCESS || ctx == nullptr) {
+      set_last_cuda_error(e);
+      return SB_ERR_CUDA;
+    }
+  }
+  unsigned long long id = 0;
+  if (get_id(ctx, &id) != CUDA_SUCCESS) return SB_ERR_CUDA;
+  std::lock_guard<std::mutex> lk(g_scratch_mu);
+  for (int i = 0; i < kScratchSlots; ++i) {
+    if (g_scratch_ctx[i] == id + 1) {
+      *out = g_scratch_ptr[i];
+      return SB_OK;
+    }
+  }
+  if (p == nullptr) {
+    // first call in this context: the host-side symbol is only a stand-in and must never reach a kernel
+    e = cudaGetSymbolAddress(&p, g_permute_scratch);
+    if (e != cudaSuccess || p == nullptr) {
+      set_last_cuda_error(e);
+      return SB_ERR_CUDA;
+    }
+  }
+  g_scratch_ctx[g_scratch_next] = id + 1;
+  g_scratch_ptr[g_scratch_next] = p;
+  g_scratch_next = (g_scratch_next + 1) % kScratchSlots;
+  *out = p;
+  return SB_OK;
+}
 }  // namespace
 }  // namespace sb
 
@@ -608,29 +680,9 @@ extern "C" SB_API int sb_permute_paged_noalloc(const sb_rows *cache, const void 
                                                   params->dtype);
   if (need < 0) return SB_ERR_INVALID_ARGUMENT;
   if (need > SB_PERMUTE_NOALLOC_SCRATCH_BYTES) return SB_ERR_TOO_LARGE;
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) {
-    sb::set_last_cuda_error(e);
-    return SB_ERR_CUDA;
-  }
-  if (dev < 0 || dev >= 64) return SB_ERR_UNSUPPORTED;
   void *scratch = nullptr;
-  {
-    // First call on this device: resolve the array's device address (the
-    // host-side symbol is only a stand-in and must never reach a kernel).
-    std::lock_guard<std::mutex> lk(sb::g_scratch_mu);
-    if (sb::g_scratch_ptr[dev] == nullptr) {
-      void *p = nullptr;
-      e = cudaGetSymbolAddress(&p, g_permute_scratch);
-      if (e != cudaSuccess || p == nullptr) {
-        sb::set_last_cuda_error(e);
-        return SB_ERR_CUDA;
-      }
-      sb::g_scratch_ptr[dev] = p;
-    }
-    scratch = sb::g_scratch_ptr[dev];
-  }
+  const int s = sb::scratch_address(&scratch);
+  if (s != SB_OK) return s;
   // Rows are snapshotted for every pair before any is read back, and pairs
   // whose source was out of range are skipped rather than read, so the
   // scratch needs no clearing between calls.

@@ -1,11 +1,11 @@
 """Generate golden fixtures by running the reference implementation itself.
 
 Imports the reference package (SemBlend 0.3.2) from the checkout named by
-``$SEMBLEND_REFERENCE`` (default: the build container's read-only copy; the
-GPU machines have none), runs its
+``$SEMBLEND_REFERENCE`` (required: there is no default location, and the GPU
+machines have no checkout), runs its
 CPU code paths on small seeded inputs and writes ``tests/golden/*.npz`` plus
 ``plans.json``.  The fixtures are committed; nothing at test time reads the
-reference.  Re-run with ``python tests/golden/make_golden.py``.
+reference.  Re-run with ``SEMBLEND_REFERENCE=<checkout> python tests/golden/make_golden.py``.
 
 bf16 tensors are stored as their int16 bit patterns with a ``<name>__bf16``
 key suffix (numpy has no bfloat16).
@@ -22,7 +22,7 @@ import numpy as np
 import torch
 
 HERE = Path(__file__).resolve().parent
-REF = Path(os.environ.get("SEMBLEND_REFERENCE", "/root/reference"))
+REF = Path(os.environ["SEMBLEND_REFERENCE"]) if os.environ.get("SEMBLEND_REFERENCE") else None
 
 
 def _np(t: torch.Tensor) -> tuple[str, np.ndarray]:
@@ -47,6 +47,10 @@ def gen(seed: int) -> torch.Generator:
 
 
 def main() -> int:
+    if REF is None or not (REF / "semblend_core").is_dir():
+        print("make_golden: set SEMBLEND_REFERENCE to a SemBlend 0.3.2 checkout (the directory holding "
+              "semblend_core/)", file=sys.stderr)
+        return 2
     sys.path.insert(0, str(REF))
     import semblend_core.donor_store as ds
     import semblend_core.partial_attention as pa

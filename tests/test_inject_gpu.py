@@ -433,3 +433,25 @@ def test_inject_plan_one_launch_matches_per_layer_oracle(multi, as_list):
         else:
             assert torch.equal(got[layer][:, 1], want[layer][:, 1])
             assert_rope_close(got[layer][:, 0].contiguous(), want[layer][:, 0].contiguous(), "neox")
+
+
+# ----------------------------------------------------------------------------
+# BASELINE configs[0] (c1) at full size
+# ----------------------------------------------------------------------------
+def test_c1_full_size_matches_oracle():
+    """c1 exactly as configured: fp32 donor K/V [4096 tokens, 4 KV heads, 128],
+    16 permuted 256-token chunks, neox RoPE theta 1e6, block 16, 256 of 1024
+    blocks.  V and untouched rows bit-exact, K within 1e-5 relative at the
+    RoPE pair's magnitude, all 4096 pairs applied."""
+    import bench
+
+    donor, cache, bt, d, t = bench.make_c1_inputs(bench.SEED + 1)
+    want, applied = orope.rope_correct_scatter_paged(cache, donor, bt, d, t, 1e6, "neox", return_applied=True)
+    assert applied == 4096
+    c = cache.to(DEV)
+    out = rc.rope_correct_scatter_paged(c, donor.to(DEV), bt.to(DEV), d.to(DEV), t.to(DEV), rope_base=1e6,
+                                        rotary_style="neox")
+    assert out is c
+    _split_check(out, want, style="neox")
+    _untouched_exact(out, cache, bt, t)
+    assert _lib.skipped_pairs(DEV) == 0
