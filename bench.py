@@ -563,7 +563,10 @@ def run_c1(args, local: int) -> dict:
         n_cpu += 1
     nbytes = algorithmic_bytes(C1_TOKENS, 1, N_KV_HEADS, HEAD_DIM, 4, C1_BLOCKS)
     pk = peaks()
-    ach = nbytes / (kt.mean_ms * 1e-3) / 1e9
+    # a launch of a few microseconds is timed from the graph (kernel + the gap to the next
+    # launch, an upper bound on the kernel's time); events around one eager launch add their own
+    # overhead and are reported beside it
+    ach = nbytes / (ms_call * 1e-3) / 1e9
     deltas = (t_h - d_h).numpy()
     return {
         "component": "c1_inject",
@@ -580,8 +583,9 @@ def run_c1(args, local: int) -> dict:
                          "bar": "V bit-exact, K within 1e-5 relative at its RoPE pair's magnitude"},
         "roofline": {"bound": "hbm", "kernel": "inject_kernel<float, 4>", "achieved": round(ach, 1),
                      "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": round(ach / pk["hbm_gbs"], 4),
-                     "kernel_ms": round(kt.mean_ms, 5), "algorithmic_bytes_per_launch": nbytes, "traffic": None,
-                     "peak_source": pk["source"]},
+                     "kernel_ms": round(ms_call, 5), "kernel_time": "per call inside the CUDA graph (kernel + "
+                     "launch gap)", "eager_event_ms": round(kt.mean_ms, 5),
+                     "algorithmic_bytes_per_launch": nbytes, "traffic": None, "peak_source": pk["source"]},
         "e2e": {"value": round(nbytes / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
                 "h2d_bytes_per_step": int(hd.numel() * 4 + ht.numel() * 4 + hb.numel() * 4),
                 "d2h_bytes_per_step": 8, "api": "semblend_b200.rope_correction.rope_correct_scatter_paged",
@@ -1025,6 +1029,90 @@ def run_attention(args, local: int) -> dict:
     }
 
 
+def run_attention_sharded(args, world: int, rank: int, local: int) -> dict | None:
+    """c4 split over `world` GPUs by (batch element, KV head) units with no
+    collective (strong scaling): heads first (N | 4: 4/N KV heads and their 28/4
+    query heads each, every batch element), then batch elements (N = 8: one KV
+    head x 2 batch elements).  Every rank builds the same inputs and runs its
+    share in one launch; value = the step's flops over the slowest rank's time."""
+    from oracle import attention as oatt
+    from semblend_b200 import _lib
+    from semblend_b200 import triton_kernels as tk
+
+    dev = torch.device("cuda", local)
+    B, S = args.attn_batch, args.attn_seq
+    h0, h1, b0, b1 = c2_partition(world, rank, n_layers=B, n_heads=A_HKV)
+    g = A_HQ // A_HKV
+    rng = np.random.default_rng(SEED + 5)
+    masks = np.stack([make_attention_mask(rng, S) for _ in range(B)])
+    gen = torch.Generator(device=dev).manual_seed(SEED + 5)
+    scale = 1.0 / np.sqrt(A_D)
+    q = (torch.randn(B, A_HQ, S, A_D, generator=gen, device=dev) * scale).to(torch.bfloat16)
+    k = (torch.randn(B, A_HKV, S, A_D, generator=gen, device=dev) * scale).to(torch.bfloat16)
+    v = (torch.randn(B, A_HKV, S, A_D, generator=gen, device=dev) * scale).to(torch.bfloat16)
+    rows, counts = tk.mask_to_rows(torch.from_numpy(masks).to(dev))
+    out = torch.zeros_like(q)
+    qs, ks, vs, os_ = (q[b0:b1, g * h0:g * h1], k[b0:b1, h0:h1], v[b0:b1, h0:h1], out[b0:b1, g * h0:g * h1])
+    rs, cs = rows[b0:b1], counts[b0:b1]
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+
+    def step():
+        tk.gqa_partial_attention(qs, ks, vs, rs, cs, os_, max_rows=S, status=status)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    steps = max(5, args.steps // 10)
+    stream = torch.cuda.current_stream(dev)
+    barrier(world)
+    torch.cuda.synchronize(dev)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with _lib.KernelTimer(steps) as kt:
+        t0.record(stream)
+        for _ in range(steps):
+            step()
+        t1.record(stream)
+        torch.cuda.synchronize(dev)
+    barrier(world)
+    ms = max_over_ranks(t0.elapsed_time(t1) / steps, world)
+    kms = max_over_ranks(kt.mean_ms, world)
+    st = int(status.item())
+    # parity: 64 seeded rows of the rank's first batch element, its query heads, against the fp32 oracle
+    pos = np.nonzero(masks[b0])[0]
+    sample = np.sort(np.random.default_rng(SEED + rank).choice(pos, 64, replace=False))
+    qc = q[b0, g * h0:g * h1].float().cpu()
+    kk = oatt.expand_kv_heads(k[b0, h0:h1].float().cpu(), g * (h1 - h0))
+    vv = oatt.expand_kv_heads(v[b0, h0:h1].float().cpu(), g * (h1 - h0))
+    want = oatt.partial_prefill_attention_blocked(qc, kk, vv, torch.from_numpy(sample), block=8)
+    got = out[b0, g * h0:g * h1][:, torch.from_numpy(sample).to(dev), :].float().cpu()
+    err = float((got - want).abs().max())
+    ok = min_over_ranks(int(err <= 2e-2 and st == 0), world)
+    flops = attention_flops(masks, A_HQ, A_D)
+    rank_flops = attention_flops(masks[b0:b1], g * (h1 - h0), A_D)
+    kms_rank0 = kt.mean_ms
+    del q, k, v, out
+    torch.cuda.empty_cache()
+    if rank != 0:
+        return None
+    pk = peaks()
+    ach = rank_flops / (kms_rank0 * 1e-3) / 1e12
+    return {
+        "component": "c4_attention_sharded",
+        "metric": "partial-prefill attention TFLOP/s", "value": round(flops / (ms * 1e-3) / 1e12, 2),
+        "unit": "TFLOP/s", "n_gpus": world, "scaling": "strong", "ms_per_step": round(ms, 4), "steps": steps,
+        "matches_oracle": bool(ok),
+        "config": {"workload": f"c4 split over {world} GPUs by (batch element, KV head): rank 0 owns KV heads "
+                               f"[{h0}, {h1}) x batch [{b0}, {b1}); no collective",
+                   "flops_per_step": flops, "slowest_rank_kernel_ms": round(kms, 4)},
+        "roofline": {"bound": "tensor", "achieved": round(ach, 1), "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+                     "frac": round(ach / pk["bf16_tflops"], 4), "peak_source": pk["source"],
+                     "kernel": "attn_tc_kernel<bf16> on rank 0's share", "kernel_ms": round(kms_rank0, 4),
+                     "traffic": None},
+        "oracle_check": f"rank 0: max |gpu - fp32 oracle| = {err:.2e} over 64 rows x {g * (h1 - h0)} heads "
+                        "(bar 2e-2); every rank checked",
+        "gpu_launches": steps,
+    }
+
 # ---------------------------------------------------------------------------
 # Component: end-to-end reuse step on the Llama-3-70B geometry (configs[4], c5)
 # ---------------------------------------------------------------------------
@@ -1085,7 +1173,7 @@ def c5_cpu_and_check(m, queries, plan, pool, tables, nblk, cache, q, k, v, out, 
     Qs = queries[:4].cpu().numpy()
     c0 = time.perf_counter()
     osearch.topk_batch(E, valid, Qs, S_THR, S_K)
-    search_s = (time.perf_counter() - c0) / 4 * C5_REQ
+    search_s = (time.perf_counter() - c0) / 4 * queries.shape[0]
     # inject: request 0's donors at layer 0 (every pair), K/V of the target rows against the GPU cache
     r, layer = 0, 0
     bt = torch.from_numpy(tables[r].astype(np.int64))
@@ -1140,8 +1228,9 @@ def run_c5(args, world: int, rank: int, local: int) -> dict | None:
     from semblend_b200.search import DeviceDonorMatrix, cosine_topk_async
 
     dev = torch.device("cuda", local)
+    n_req, n_pool = args.c5_requests, args.c5_pool
     rng = np.random.default_rng(SEED + 7)  # the same workload on every rank
-    req_len, donor_len = c5_lengths(rng, C5_REQ), c5_lengths(rng, C5_POOL)
+    req_len, donor_len = c5_lengths(rng, n_req), c5_lengths(rng, n_pool)
     plan, masks_l = c5_plan(rng, req_len, donor_len)
     s_max = int(req_len.max())
     hq, hkv = C5_HQ // C5_TP, C5_HKV // C5_TP
@@ -1152,7 +1241,7 @@ def run_c5(args, world: int, rank: int, local: int) -> dict | None:
     pool_blocks = int(nblk.sum() * 1.1)
     perm = rng.permutation(pool_blocks)
     offs = np.concatenate([[0], np.cumsum(nblk)])
-    tables = [perm[offs[r] : offs[r + 1]].astype(np.int32) for r in range(C5_REQ)]
+    tables = [perm[offs[r] : offs[r + 1]].astype(np.int32) for r in range(n_req)]
     cache = torch.empty(C5_L, pool_blocks, 2, hkv, BLOCK, C5_D, dtype=torch.bfloat16, device=dev)
     cache.normal_(generator=gen)
     pool = []
@@ -1179,18 +1268,18 @@ def run_c5(args, world: int, rank: int, local: int) -> dict | None:
     m.write_range(0, emb)
     del emb
     qg = torch.Generator(device=dev).manual_seed(SEED + 9)
-    queries = m.emb[torch.randint(0, C5_SEARCH_ROWS, (C5_REQ,), generator=qg, device=dev)] + \
-        0.05 * torch.randn(C5_REQ, S_DIM, generator=qg, device=dev)
-    s_out = (torch.empty(C5_REQ, S_K, dtype=torch.int64, device=dev),
-             torch.empty(C5_REQ, S_K, dtype=torch.float32, device=dev))
+    queries = m.emb[torch.randint(0, C5_SEARCH_ROWS, (n_req,), generator=qg, device=dev)] + \
+        0.05 * torch.randn(n_req, S_DIM, generator=qg, device=dev)
+    s_out = (torch.empty(n_req, S_K, dtype=torch.int64, device=dev),
+             torch.empty(n_req, S_K, dtype=torch.float32, device=dev))
     s_status = torch.zeros(1, dtype=torch.int32, device=dev)
 
     # attention operands of one layer (the 80 layers reuse them: same shapes, same cost)
     scale = 1.0 / np.sqrt(C5_D)
-    q = (torch.randn(C5_REQ, hq, s_max, C5_D, generator=gen, device=dev) * scale).to(torch.bfloat16)
-    k = (torch.randn(C5_REQ, hkv, s_max, C5_D, generator=gen, device=dev) * scale).to(torch.bfloat16)
-    v = (torch.randn(C5_REQ, hkv, s_max, C5_D, generator=gen, device=dev) * scale).to(torch.bfloat16)
-    masks = np.zeros((C5_REQ, s_max), bool)
+    q = (torch.randn(n_req, hq, s_max, C5_D, generator=gen, device=dev) * scale).to(torch.bfloat16)
+    k = (torch.randn(n_req, hkv, s_max, C5_D, generator=gen, device=dev) * scale).to(torch.bfloat16)
+    v = (torch.randn(n_req, hkv, s_max, C5_D, generator=gen, device=dev) * scale).to(torch.bfloat16)
+    masks = np.zeros((n_req, s_max), bool)
     for r, mk in enumerate(masks_l):
         masks[r, : mk.shape[0]] = mk
     mask_d = torch.from_numpy(masks).to(dev)
@@ -1239,12 +1328,25 @@ def run_c5(args, world: int, rank: int, local: int) -> dict | None:
     step_ms = max_over_ranks(t0.elapsed_time(t1) / steps, world)
     parts = [max_over_ranks(x / steps, world) for x in parts]
     st_s, st_a, skipped = int(s_status.item()), int(a_status.item()), _lib.skipped_pairs(dev, reset=True)
+    # each part's kernels alone, timed by library events on the launch stream (the in-step
+    # brackets above also hold host work such as building the inject's 186 descriptors)
+    kern = []
+    for fn, n_launch in ((lambda: cosine_topk_async(m.emb, m.emb16, m.valid, m.stats, queries, S_K, S_THR,
+                                                    status=s_status, workspace_owner=m, out=s_out), 1),
+                         (lambda: rc.inject_donors(cache, inj, rope_base=C5_THETA, rotary_style="neox"), 1),
+                         (lambda: tk.gqa_partial_attention(q, k, v, rows, counts, out, max_rows=s_max,
+                                                           status=a_status), C5_L)):
+        with _lib.KernelTimer(steps * n_launch) as kt:
+            for _ in range(steps * n_launch):
+                fn()
+            torch.cuda.synchronize(dev)
+        kern.append(max_over_ranks(kt.total_ms / steps, world))
 
     # end to end: this step's pair lists, block tables, queries and masks from pinned host
     # memory; search ids and the skipped-pair count back to the host
     hq_host = queries.cpu().pin_memory()
     hmask = torch.from_numpy(masks).pin_memory()
-    hres = torch.empty(C5_REQ, S_K, dtype=torch.int64).pin_memory()
+    hres = torch.empty(n_req, S_K, dtype=torch.int64).pin_memory()
     hskip = torch.empty(1, dtype=torch.int64).pin_memory()
     h2d = (sum(h.numel() * h.element_size() for h in host_pos) + sum(h.numel() * 4 for h in host_bt)
            + hq_host.numel() * 4 + hmask.numel())
@@ -1278,7 +1380,7 @@ def run_c5(args, world: int, rank: int, local: int) -> dict | None:
 
     inj_bytes = algorithmic_bytes(n_pairs, C5_L, hkv, C5_D, 2, int(nblk.sum()))
     attn_flops = C5_L * attention_flops(masks, hq, C5_D)
-    search_flops = 2.0 * C5_SEARCH_ROWS * C5_REQ * S_DIM
+    search_flops = 2.0 * C5_SEARCH_ROWS * n_req * S_DIM
     cpu, chk = (None, None)
     if rank == 0:
         cpu, chk = c5_cpu_and_check(m, queries, plan, pool, tables, nblk, cache, q, k, v, out, masks, hq, hkv,
@@ -1289,7 +1391,7 @@ def run_c5(args, world: int, rank: int, local: int) -> dict | None:
         return None
     pk = peaks()
     tokens = int(req_len.sum())
-    att_tf = attn_flops / (parts[2] * 1e-3) / 1e12
+    att_tf = attn_flops / (kern[2] * 1e-3) / 1e12
     return {
         "component": "c5_step",
         "matches_oracle": chk["matches_oracle"] and st_s == 0 and st_a == 0 and skipped == 0,
@@ -1302,21 +1404,25 @@ def run_c5(args, world: int, rank: int, local: int) -> dict | None:
         "n_gpus": world,
         "scaling": "weak (each rank one of the 8 TP ranks' KV heads; 8 GPUs run the whole TP-8 step)",
         "steps": steps,
-        "config": {"workload": f"c5: Llama-3-70B geometry (80 L, 64 q / 8 KV heads, D 128, theta 5e5, bf16), "
-                               f"TP 8 -> {hq} q heads / {hkv} KV head per rank; {C5_REQ} requests, lognormal "
+        "config": {"workload": f"c5{'' if (n_req, n_pool) == (C5_REQ, C5_POOL) else ' (reduced)'}: Llama-3-70B geometry (80 L, 64 q / 8 KV heads, D 128, theta 5e5, bf16), "
+                               f"TP 8 -> {hq} q heads / {hkv} KV head per rank; {n_req} requests, lognormal "
                                f"lengths (median 8K, 4K-32K; {tokens:,} tokens), 2-4 donors each from a pool of "
-                               f"{C5_POOL} at 256-token chunks, 10-20% recompute (last chunk always); search "
+                               f"{n_pool} at 256-token chunks, 10-20% recompute (last chunk always); search "
                                f"{C5_SEARCH_ROWS:,} x 384, 64 queries, top-8",
                    "pairs": n_pairs, "descriptors": len(inj), "compute_rows": int(masks.sum()),
                    "attention_operands": "one layer's dense Q/K/V reused by the 80 layer launches",
                    "status": {"search": st_s, "attention": st_a, "skipped_pairs": skipped}},
         "components_ms": {"search": round(parts[0], 4), "inject": round(parts[1], 4),
-                          "attention_80_layers": round(parts[2], 3)},
+                          "attention_80_layers": round(parts[2], 3),
+                          "note": "in-step event brackets around each part's API calls (host work included)"},
+        "kernel_ms": {"screen": round(kern[0], 4), "inject": round(kern[1], 4), "attention_80_layers": round(kern[2], 3),
+                      "note": "each part's dominant kernels alone, library events on the launch stream"},
         "roofline": {
-            "search": {"bound": "tensor", "achieved": round(search_flops / (parts[0] * 1e-3) / 1e12, 1),
-                       "unit": "TFLOP/s", "frac": round(search_flops / (parts[0] * 1e-3) / 1e12 / pk["bf16_tflops"], 4)},
-            "inject": {"bound": "hbm", "achieved": round(inj_bytes / (parts[1] * 1e-3) / 1e9, 1), "unit": "GB/s",
-                       "frac": round(inj_bytes / (parts[1] * 1e-3) / 1e9 / pk["hbm_gbs"], 4),
+            "search": {"bound": "tensor", "achieved": round(search_flops / (kern[0] * 1e-3) / 1e12, 1),
+                       "unit": "TFLOP/s", "frac": round(search_flops / (kern[0] * 1e-3) / 1e12 / pk["bf16_tflops"], 4),
+                       "note": "64 queries: one query tile, latency-bound"},
+            "inject": {"bound": "hbm", "achieved": round(inj_bytes / (kern[1] * 1e-3) / 1e9, 1), "unit": "GB/s",
+                       "peak": pk["hbm_gbs"], "frac": round(inj_bytes / (kern[1] * 1e-3) / 1e9 / pk["hbm_gbs"], 4),
                        "algorithmic_bytes": inj_bytes},
             "attention": {"bound": "tensor", "achieved": round(att_tf, 1), "unit": "TFLOP/s",
                           "peak": pk["bf16_tflops_sustained"], "frac": round(att_tf / pk["bf16_tflops_sustained"], 4),
@@ -1324,7 +1430,7 @@ def run_c5(args, world: int, rank: int, local: int) -> dict | None:
                           "note": "80 launches inside a ~0.2 s step: measured against the sustained bf16 peak"},
             "peak_source": pk["source"]},
         "e2e": {"value": round(e2e_ms, 3), "unit": "ms", "h2d_bytes_per_step": int(h2d),
-                "d2h_bytes_per_step": C5_REQ * S_K * 8 + 8},
+                "d2h_bytes_per_step": n_req * S_K * 8 + 8},
         "gpu_launches": steps * (3 + 1 + C5_L),
         "clocks": clk,
     }
@@ -1711,6 +1817,8 @@ def main() -> int:
     ap.add_argument("--search-rows", type=int, default=S_ROWS, help="donor rows of the search (c3: 1048576)")
     ap.add_argument("--requests", type=int, default=N_REQ, help="requests per step (c2: 8)")
     ap.add_argument("--layers", type=int, default=N_LAYERS, help="layers (c2: 28)")
+    ap.add_argument("--c5-requests", type=int, default=C5_REQ, help="c5 requests (64)")
+    ap.add_argument("--c5-pool", type=int, default=C5_POOL, help="c5 donor pool (64)")
     ap.add_argument("--check-slices", type=int, default=3, help="(request, layer) slices of c2 checked per rank")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
@@ -1726,6 +1834,8 @@ def main() -> int:
     if args.only != "all":
         if args.only == "search" and world > 1:
             res = run_search_sharded(args, world, rank, local)
+        elif args.only == "attention" and world > 1:
+            res = run_attention_sharded(args, world, rank, local)
         elif args.only == "c5":
             res = run_c5(args, world, rank, local)
         elif rank != 0:
@@ -1750,6 +1860,7 @@ def main() -> int:
             emit_component(run_c5(args, world, rank, local), summary, "c5_step")
             if world > 1:
                 emit_component(run_search_sharded(args, world, rank, local), summary, "c3_search_sharded")
+                emit_component(run_attention_sharded(args, world, rank, local), summary, "c4_attention_sharded")
         if line is not None:
             failed += [k for k, v in summary.items() if v.get("ok") is False]
             if not line["matches_oracle"]:

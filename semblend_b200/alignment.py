@@ -221,6 +221,25 @@ def estimate_reuse_ratio(donor_tokens, target_tokens, chunk_size: int = DEFAULT_
     return float(matched.item()) / max(a.target_len, 1)
 
 
+def estimate_reuse_ratio_batch(donors, target_tokens, chunk_size: int = DEFAULT_CHUNK_SIZE,
+                               device=None) -> list[float]:
+    """:func:`estimate_reuse_ratio` of several donors against one target: one
+    batched chunk alignment (``sb_chunk_align_batch``), one token-overlap
+    launch per donor, and a single host synchronisation for all of them (the
+    reference calls its estimate once per candidate, donor_store.py:256-262,
+    :359-365)."""
+    donors = list(donors)
+    if not donors:
+        return []
+    device = _device(device, target_tokens, *donors)
+    t = _tokens(target_tokens, device)
+    res = chunk_alignment_batch(donors, [t] * len(donors), chunk_size, context_gate=False, device=device)
+    ov = torch.cat([token_overlap(d, t, device=device) for d in donors])
+    n_pairs = torch.cat([a.n_pairs for a in res])
+    matched = torch.where(n_pairs > 0, n_pairs, ov).cpu().tolist()
+    return [m / max(int(t.shape[0]), 1) for m in matched]
+
+
 @dataclass(frozen=True)
 class SlotAction:
     """The reference's SlotAction (alignment.py:100-104): ``action`` is
@@ -278,5 +297,6 @@ __all__ = [
     "compute_chunk_alignment",
     "estimate_chunk_reuse",
     "estimate_reuse_ratio",
+    "estimate_reuse_ratio_batch",
     "token_overlap",
 ]

@@ -21,6 +21,7 @@
 #include <algorithm>
 #include <cstring>
 #include <mutex>
+#include <type_traits>
 #include <vector>
 
 #include <cuda.h>
@@ -178,11 +179,28 @@ __global__ void __launch_bounds__(kThreads, SB_INJECT_MIN_BLOCKS)
   const int tpr = C.tpr;
   const int pl = threadIdx.x / tpr;
   const int slice = threadIdx.x - pl * tpr;
-  if (pl >= C.pairs_per_tile) return;
-
   const int64_t tile = blockIdx.x;
   int64_t first;
-  const sb_inject_desc &d = find_desc(L, tile, first);
+  // A descriptor in the kernel parameters is read from the constant bank.  One
+  // in a device table sits in global memory, which the row loop's stores could
+  // alias as far as the compiler knows, so it would be read again for every
+  // row: the CTA's descriptor (all its pairs share one) is copied to shared
+  // memory first.
+  __shared__ sb_inject_desc s_desc;
+  __shared__ int64_t s_first;
+  const sb_inject_desc *dp;
+  if constexpr (std::is_same<LT, InjectLaunchTable>::value) {
+    if (threadIdx.x == 0) {
+      s_desc = find_desc(L, tile, s_first);
+    }
+    __syncthreads();
+    dp = &s_desc;
+    first = s_first;
+  } else {
+    dp = &find_desc(L, tile, first);
+  }
+  const sb_inject_desc &d = *dp;
+  if (pl >= C.pairs_per_tile) return;
   const int64_t pair = (tile - first) * C.pairs_per_tile + pl;
   if (pair >= d.n_pairs) return;
 
@@ -242,27 +260,33 @@ __global__ void __launch_bounds__(kThreads, SB_INJECT_MIN_BLOCKS)
   }
 
   const int H = P.n_heads;
-  const int64_t ua = (int64_t)blockIdx.y * C.units_per_chunk;
-  const int64_t ub = min(ua + (int64_t)C.units_per_chunk, C.n_units);
+  // units are numbered (layer, kv, head) with the head fastest; n_units < 2^31
+  const int ua = (int)((int64_t)blockIdx.y * C.units_per_chunk);
+  const int nrow = (int)min((int64_t)C.units_per_chunk, C.n_units - ua);
   const int64_t sdim = d.src.stride_dim, ddim = d.dst.stride_dim;
+  // (layer, kv, head) cursor of the next row, advanced one unit per row
+  int h = ua % H, kvi = (ua / H) % C.n_kv_sel, l = (ua / H) / C.n_kv_sel;
 
 #pragma unroll 1
-  for (int64_t u0 = ua; u0 < ub; u0 += kUnroll) {
+  for (int i0 = 0; i0 < nrow; i0 += kUnroll) {
     Vec<T, VEC> va[kUnroll], vb[kUnroll];
     T *dptr[kUnroll];
     bool krow[kUnroll];
 #pragma unroll
     for (int r = 0; r < kUnroll; ++r) {
-      const int64_t u = u0 + r;
       dptr[r] = nullptr;
       krow[r] = false;
-      if (u < ub) {
-        const int h = (int)(u % H);
-        const int64_t rest = u / H;
-        const int kv = C.kv_first + (int)(rest % C.n_kv_sel);
-        const int l = (int)(rest / C.n_kv_sel);
+      if (i0 + r < nrow) {
+        const int kv = C.kv_first + kvi;
         const T *s = layer_base<T>(d.src, l) + kv * d.src.stride_kv + h * d.src.stride_head + soff;
         T *t = layer_base<T>(d.dst, l) + kv * d.dst.stride_kv + h * d.dst.stride_head + doff;
+        if (++h == H) {
+          h = 0;
+          if (++kvi == C.n_kv_sel) {
+            kvi = 0;
+            ++l;
+          }
+        }
         if (VEC == 1) {
           va[r].e[0] = s[oa * sdim];
           vb[r].e[0] = s[ob * sdim];
@@ -391,6 +415,7 @@ int plan_inject(const sb_inject_desc *descs, int n_desc, const sb_inject_params 
   C.n_kv_sel = params->kv_select == SB_KV_BOTH ? 2 : 1;
   C.kv_first = params->kv_select == SB_KV_V ? 1 : 0;
   C.n_units = (int64_t)params->n_layers * C.n_kv_sel * params->n_heads;
+  if (C.n_units > 0x7fffffffLL) return SB_ERR_TOO_LARGE;  // the kernel counts units in int32
   int64_t tiles = 0;
   for (int i = 0; i < n_desc; ++i) {
     tile_start[i] = tiles;
@@ -403,13 +428,19 @@ int plan_inject(const sb_inject_desc *descs, int n_desc, const sb_inject_params 
   // Aim for ~16 waves of resident CTAs so the last wave's imbalance is small,
   // while keeping at least 8 rows per thread to amortise the cos/sin set-up.
   // A launch with fewer pair tiles than two waves of resident CTAs (one
-  // layer of a few thousand pairs) would leave SMs idle at 8 rows per
-  // thread: there each thread keeps only the rows it has in flight at once.
+  // layer of a few thousand pairs) would leave SMs idle at 8 rows per thread:
+  // there the units are split into as many chunks as fit in one wave, down
+  // to the rows a thread keeps in flight at once.
   const int64_t slots = (int64_t)sm_count() * SB_INJECT_MIN_BLOCKS;
-  const int64_t min_rows = tiles >= 2 * slots ? 8 : kUnroll;
-  const int64_t target = (int64_t)sm_count() * (2048 / kThreads) * 16;
-  int64_t chunks = std::max<int64_t>(1, (target + tiles - 1) / tiles);
-  chunks = std::min<int64_t>(chunks, std::max<int64_t>(1, (C.n_units + min_rows - 1) / min_rows));
+  int64_t chunks;
+  if (tiles >= 2 * slots) {
+    const int64_t target = (int64_t)sm_count() * (2048 / kThreads) * 16;
+    chunks = std::max<int64_t>(1, (target + tiles - 1) / tiles);
+    chunks = std::min<int64_t>(chunks, std::max<int64_t>(1, (C.n_units + 7) / 8));
+  } else {
+    chunks = std::max<int64_t>(1, slots / tiles);
+    chunks = std::min<int64_t>(chunks, std::max<int64_t>(1, (C.n_units + kUnroll - 1) / kUnroll));
+  }
   chunks = std::min<int64_t>(chunks, 65535);
   int64_t upc = (C.n_units + chunks - 1) / chunks;
   chunks = (C.n_units + upc - 1) / upc;

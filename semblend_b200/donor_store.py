@@ -7,11 +7,12 @@ for missing embeddings, the valid mask; donor_store.py:130-168) is kept
 verbatim in meaning on the host, and every row write is mirrored into a
 :class:`~semblend_b200.search.DeviceDonorMatrix` on the GPU.  The cosine /
 threshold / top-k stage of ``find_donor`` and ``find_donors`` (:205-229,
-:323-341) runs as the exact tensor-core search kernel; the token-level
-rescoring that follows (Jaccard pre-filter, ``estimate_reuse_ratio``,
-``compute_alignment``) is unchanged host logic and uses the reference's
-alignment module when it is installed (pass ``alignment=`` to supply it
-otherwise).
+:323-341) runs as the exact tensor-core search kernel, for any ``top_k``; the
+candidates' reuse estimates (``estimate_reuse_ratio``, :256-262, :359-365)
+run on the device for all candidates at once; the Jaccard pre-filter stays
+host logic, and the winners' ``compute_alignment`` is the reference's when its
+package is installed, else the device chunk alignment.  ``alignment=
+(estimate_reuse_ratio, compute_alignment)`` overrides both.
 
 :meth:`DonorStore.search_batch` exposes the cosine stage for a batch of
 queries (the form the benchmark and batched schedulers use).
@@ -34,12 +35,19 @@ logger = logging.getLogger(__name__)
 DEFAULT_CHUNK_SIZE = 256  # semblend_core/alignment.py:35
 
 
-def _reference_alignment():
+def _compute_alignment():
+    """The reference's compute_alignment when its package is installed (exact
+    chunks, then its fuzzy / Levenshtein fallbacks: token-level host work);
+    otherwise the exact chunk alignment on the device, which is the
+    reference's primary path (alignment.py:820-831)."""
     try:
-        from semblend_core.alignment import compute_alignment, estimate_reuse_ratio
+        from semblend_core.alignment import compute_alignment
     except ImportError:
-        return None
-    return estimate_reuse_ratio, compute_alignment
+        from .alignment import compute_chunk_alignment
+
+        def compute_alignment(donor_tokens, target_tokens, chunk_size=DEFAULT_CHUNK_SIZE):
+            return compute_chunk_alignment(donor_tokens, target_tokens, chunk_size)
+    return compute_alignment
 
 
 def _reference_indexes(max_entries: int, chunk_size: int, chunk_index):
@@ -127,16 +135,23 @@ class DonorStore:
         """Host copy of the row matrix (for inspection; synchronises)."""
         return self._matrix.emb.cpu().numpy()
 
-    def _align(self):
-        if self._alignment is None:
-            self._alignment = _reference_alignment()
-            if self._alignment is None:
-                raise ImportError(
-                    "DonorStore token-level rescoring needs semblend_core.alignment "
-                    "(install the reference package) or an alignment=(estimate_reuse_ratio, "
-                    "compute_alignment) pair"
-                )
-        return self._alignment
+    def _compute_alignment_fn(self):
+        if self._alignment is not None:
+            return self._alignment[1]
+        return _compute_alignment()
+
+    def _reuse_ratios(self, donors: list[DonorNode], query_tokens: list[int]) -> list[float]:
+        """estimate_reuse_ratio of each candidate donor against the query: one
+        batched device call, or the caller's function per donor."""
+        if not donors:
+            return []
+        if self._alignment is not None:
+            est = self._alignment[0]
+            return [est(d.token_ids, query_tokens, chunk_size=self._chunk_size) for d in donors]
+        from .alignment import estimate_reuse_ratio_batch
+
+        return estimate_reuse_ratio_batch([d.token_ids for d in donors], query_tokens, self._chunk_size,
+                                          device=self._matrix.device)
 
     # -- row bookkeeping (donor_store.py:130-168) ---------------------------------
     def add_donor(self, node: DonorNode) -> None:
@@ -190,26 +205,40 @@ class DonorStore:
         return self._matrix.search(queries, k, thr)
 
     def _cosine_candidates(self, query_embedding, fetch_k: int):
+        """The fetch_k most similar valid rows at or above the threshold (all
+        of them when fewer pass), as the reference's argpartition keeps
+        (donor_store.py:222-226, :335-341); here in (similarity desc, row asc)
+        order."""
         if fetch_k <= 0:
             return np.empty(0, np.int64), np.empty(0, np.float32)
-        ids, sims = self._matrix.search(np.asarray(query_embedding, dtype=np.float32), min(fetch_k, 32),
+        ids, sims = self._matrix.search(np.asarray(query_embedding, dtype=np.float32), int(fetch_k),
                                         self._min_similarity)
         ids = ids[0].cpu().numpy()
         sims = sims[0].cpu().numpy()
         keep = ids >= 0
         return ids[keep], sims[keep]
 
-    def _token_score(self, donor, query_set, query_tokens, min_reuse_ratio):
-        donor_set = set(donor.token_ids)
-        union = len(query_set | donor_set)
-        jaccard = len(query_set & donor_set) / union if union > 0 else 0.0
-        if jaccard < min_reuse_ratio:
-            return None
-        estimate_reuse_ratio, _ = self._align()
-        reuse = estimate_reuse_ratio(donor.token_ids, query_tokens, chunk_size=self._chunk_size)
-        if reuse < min_reuse_ratio:
-            return None
-        return reuse
+    def _scored_candidates(self, cand, sims, query_tokens, min_reuse_ratio):
+        """(similarity, donor, reuse) of the candidates that pass the Jaccard
+        pre-filter and the reuse estimate (donor_store.py:240-262, :351-365)."""
+        idx_to_id = {v: k for k, v in self._id_to_idx.items()}
+        query_set = set(query_tokens)
+        kept = []
+        for storage_idx, sim in zip(cand.tolist(), sims.tolist()):
+            donor_id = idx_to_id.get(int(storage_idx))
+            if donor_id is None:
+                continue
+            donor = self._entries.get(donor_id)
+            if donor is None or donor.token_ids == query_tokens:
+                continue
+            donor_set = set(donor.token_ids)
+            union = len(query_set | donor_set)
+            jaccard = len(query_set & donor_set) / union if union > 0 else 0.0
+            if jaccard < min_reuse_ratio:
+                continue
+            kept.append((float(sim), donor))
+        reuses = self._reuse_ratios([d for _, d in kept], query_tokens)
+        return [(sim, donor, reuse) for (sim, donor), reuse in zip(kept, reuses) if reuse >= min_reuse_ratio]
 
     def find_donor(self, query_embedding, query_tokens: list[int], top_k: int = 5,
                    min_reuse_ratio: float = 0.5) -> DonorMatch | None:
@@ -224,26 +253,15 @@ class DonorStore:
         cand, sims = self._cosine_candidates(query_embedding, top_k)
         if cand.shape[0] == 0:
             return None
-        idx_to_id = {v: k for k, v in self._id_to_idx.items()}
-        query_set = set(query_tokens)
         best, best_score = None, 0.0
-        for storage_idx, sim in zip(cand.tolist(), sims.tolist()):
-            donor_id = idx_to_id.get(int(storage_idx))
-            if donor_id is None:
-                continue
-            donor = self._entries.get(donor_id)
-            if donor is None or donor.token_ids == query_tokens:
-                continue
-            reuse = self._token_score(donor, query_set, query_tokens, min_reuse_ratio)
-            if reuse is None:
-                continue
-            score = float(sim) * reuse
+        for sim, donor, reuse in self._scored_candidates(cand, sims, query_tokens, min_reuse_ratio):
+            score = sim * reuse
             if score > best_score:
-                best_score, best = score, (float(sim), donor)
+                best_score, best = score, (sim, donor)
         match = None
         if best is not None:
             sim, donor = best
-            _, compute_alignment = self._align()
+            compute_alignment = self._compute_alignment_fn()
             alignment = compute_alignment(donor.token_ids, query_tokens, chunk_size=self._chunk_size)
             if alignment.reuse_ratio >= min_reuse_ratio:
                 match = DonorMatch(donor=donor, similarity=sim, alignment=alignment)
@@ -264,25 +282,14 @@ class DonorStore:
         cand, sims = self._cosine_candidates(query_embedding, top_k * 2)
         if cand.shape[0] == 0:
             return []
-        idx_to_id = {v: k for k, v in self._id_to_idx.items()}
         now = time.monotonic()
-        query_set = set(query_tokens)
         scored = []
-        for storage_idx, sim in zip(cand.tolist(), sims.tolist()):
-            donor_id = idx_to_id.get(int(storage_idx))
-            if donor_id is None:
-                continue
-            donor = self._entries.get(donor_id)
-            if donor is None or donor.token_ids == query_tokens:
-                continue
-            reuse = self._token_score(donor, query_set, query_tokens, min_reuse_ratio)
-            if reuse is None:
-                continue
+        for sim, donor, reuse in self._scored_candidates(cand, sims, query_tokens, min_reuse_ratio):
             age = now - donor.timestamp
             recency_bonus = max(0.0, 0.01 * (1.0 - age / 60.0))
-            scored.append((float(sim) * reuse + recency_bonus, float(sim), donor))
+            scored.append((sim * reuse + recency_bonus, sim, donor))
         scored.sort(key=lambda x: x[0], reverse=True)
-        _, compute_alignment = self._align()
+        compute_alignment = self._compute_alignment_fn()
         matches = []
         for _, sim, donor in scored[:top_k]:
             alignment = compute_alignment(donor.token_ids, query_tokens, chunk_size=self._chunk_size)
@@ -308,7 +315,7 @@ class DonorStore:
             if jaccard >= min_jaccard:
                 scored.append((jaccard, donor))
         scored.sort(key=lambda x: x[0], reverse=True)
-        _, compute_alignment = self._align()
+        compute_alignment = self._compute_alignment_fn()
         matches = []
         for jaccard, donor in scored[: top_k * 2]:
             alignment = compute_alignment(donor.token_ids, query_tokens, chunk_size=self._chunk_size)

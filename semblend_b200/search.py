@@ -23,6 +23,7 @@ import torch
 from . import _lib
 
 DEFAULT_CAPACITY = 4096  # screening candidates kept per query before rescoring
+MAX_K = 32  # the largest k of one sb_cosine_topk call
 
 
 def _pad64(d: int) -> int:
@@ -118,7 +119,12 @@ class DeviceDonorMatrix:
     def search(self, queries, k: int, min_similarity: float, *, n_rows: int | None = None,
                id_offset: int = 0, capacity: int = DEFAULT_CAPACITY) -> tuple[torch.Tensor, torch.Tensor]:
         """Top-``k`` rows per query (see module docstring); returns device
-        tensors ``ids [Q, k]`` (int64, ``+ id_offset``) and ``scores [Q, k]``."""
+        tensors ``ids [Q, k]`` (int64, ``+ id_offset``) and ``scores [Q, k]``.
+
+        Any ``k``: beyond the kernel's ``MAX_K`` per call, each query is
+        searched in passes of ``MAX_K`` with the rows already returned masked
+        out of a scratch copy of the valid mask, so the passes concatenate
+        into the exact (similarity desc, row asc) order."""
         q = torch.as_tensor(queries)
         if q.ndim == 1:
             q = q.unsqueeze(0)
@@ -126,10 +132,34 @@ class DeviceDonorMatrix:
             raise ValueError(f"query dim {q.shape[-1]} != store dim {self.dim}")
         q = q.to(device=self.device, dtype=torch.float32, non_blocking=True).contiguous()
         n_rows = self.max_entries if n_rows is None else int(n_rows)
+        if k > MAX_K:
+            res = [self._search_wide(q[i : i + 1], k, min_similarity, n_rows, id_offset, capacity)
+                   for i in range(q.shape[0])]
+            return torch.cat([r[0] for r in res]), torch.cat([r[1] for r in res])
         return cosine_topk(
             self.emb, self.emb16, self.valid, self.stats, q, k, min_similarity, n_rows=n_rows,
             id_offset=id_offset, capacity=capacity, status=self._status, workspace_owner=self,
         )
+
+    def _search_wide(self, q: torch.Tensor, k: int, min_similarity: float, n_rows: int, id_offset: int,
+                     capacity: int) -> tuple[torch.Tensor, torch.Tensor]:
+        """One query's top-``k`` for ``k > MAX_K`` (see :meth:`search`)."""
+        mask = self.valid.clone()
+        ids = torch.full((1, k), -1, dtype=torch.int64, device=self.device)
+        scores = torch.full((1, k), float("-inf"), dtype=torch.float32, device=self.device)
+        got = 0
+        while got < k:
+            kk = min(MAX_K, k - got)
+            i, s = cosine_topk(self.emb, self.emb16, mask, self.stats, q, kk, min_similarity, n_rows=n_rows,
+                               id_offset=id_offset, capacity=capacity, status=self._status, workspace_owner=self)
+            ids[:, got : got + kk] = i
+            scores[:, got : got + kk] = s
+            got += kk
+            hit = i[i >= 0]
+            if hit.numel() < kk:  # fewer rows than asked reach the threshold: none is left
+                break
+            mask.index_fill_(0, hit - id_offset, 0)
+        return ids, scores
 
 
 def _workspace(owner, nbytes: int, device: torch.device) -> torch.Tensor:

@@ -373,3 +373,122 @@ def test_cagra_factory_is_the_exact_store():
             rb = b.find_donors(q, [1, 2, 3], top_k=3)
             assert ra
             assert [m.donor.request_id for m in ra] == [m.donor.request_id for m in rb]
+
+
+# ----------------------------------------------------------------------------
+# k beyond one kernel call, and the store's candidate widths
+# ----------------------------------------------------------------------------
+@pytest.mark.parametrize("k", [33, 40, 70, 100])
+def test_wide_search_matches_oracle(k):
+    """k > 32 runs in passes with the returned rows masked out; the result is
+    the oracle's exact top-k (ties within 1e-6 aside), with invalid rows and
+    the threshold respected."""
+    E, centers, rng = clustered(12000, 384, 12, seed=30 + k)
+    valid = rng.random(12000) > 0.1
+    Q = queries_for(centers, rng, 12, 384)
+    m = build(E, valid)
+    before = m.valid.clone()
+    ids, s = m.search(Q, k, 0.6)
+    assert ids.shape == (12, k) and torch.equal(m.valid, before)  # the store's mask is untouched
+    assert_topk_equivalent(E, valid, Q, 0.6, ids.cpu().numpy(), s.cpu().numpy(), k)
+
+
+class _Aligned:
+    reuse_ratio = 1.0
+
+
+def test_find_donors_top_k_20_fetches_40_candidates():
+    """find_donors(top_k=20) scores the 40 most similar donors above the
+    threshold (donor_store.py:335-341); the old 32-candidate cap lost the
+    ones ranked 33-40.  Donors ranked 1-25 are filtered by their reuse, so
+    exactly those ranked 26-40 must come back, best first."""
+    rng = np.random.default_rng(40)
+    dim = 64
+    base = rng.standard_normal(dim).astype(np.float32)
+    embs = base + 0.25 * rng.standard_normal((120, dim)).astype(np.float32)
+    query = base + 0.05 * rng.standard_normal(dim).astype(np.float32)
+    valid = np.ones(120, bool)
+    want_ids, want_sims = osearch.cosine_candidates(embs, valid, query, 0.6, 40)
+    want_ids, want_sims = osearch.sort_candidates(want_ids, want_sims)
+    assert want_ids.shape[0] == 40
+    blocked = set(want_ids[:25].tolist())
+
+    def est(donor_tokens, query_tokens, chunk_size=256):
+        return 0.0 if donor_tokens[0] in blocked else 1.0
+
+    store = ds.DonorStore(max_entries=200, embedding_dim=dim, min_similarity=0.6, device=DEV,
+                          alignment=(est, lambda *a, **k: _Aligned()))
+    store.add_donors([ds.DonorNode(f"d{i}", [i], embs[i], timestamp=-1e9) for i in range(120)])
+    ms = store.find_donors(query, query_tokens=[-1], top_k=20, min_reuse_ratio=0.5)
+    assert [m.donor.request_id for m in ms] == [f"d{i}" for i in want_ids[25:40]]
+    np.testing.assert_allclose([m.similarity for m in ms], want_sims[25:40], atol=TOL)
+
+
+def _token_cases(rng, chunk):
+    """A query and donors that share reordered whole chunks with it, share only
+    tokens (the multiset fallback), share nothing, or are shorter than a chunk."""
+    q = rng.integers(0, 5000, 8 * chunk)
+    chunks = [q[i * chunk:(i + 1) * chunk] for i in range(8)]
+    donors = [
+        np.concatenate([chunks[3], chunks[4], chunks[5], rng.integers(0, 5000, chunk), chunks[0], chunks[1]]),
+        np.concatenate([chunks[6], chunks[7]]),
+        rng.permutation(q)[: 5 * chunk],            # same tokens, no whole chunk
+        rng.integers(5000, 9000, 6 * chunk),        # nothing in common
+        q[: chunk // 2].copy(),                     # shorter than one chunk
+        np.concatenate([chunks[2], chunks[2], chunks[2]]),  # a chunk repeated
+    ]
+    return q, donors
+
+
+def test_estimate_reuse_ratio_batch_matches_oracle():
+    from oracle import alignment as oal
+    from semblend_b200.alignment import estimate_reuse_ratio, estimate_reuse_ratio_batch
+
+    rng = np.random.default_rng(41)
+    q, donors = _token_cases(rng, 64)
+    got = estimate_reuse_ratio_batch([d.tolist() for d in donors], q.tolist(), 64, device=DEV)
+    want = [oal.estimate_reuse_ratio(d.tolist(), q.tolist(), 64) for d in donors]
+    assert got == pytest.approx(want, abs=0) and 0 < min(w for w in want if w > 0) < max(want)
+    assert [estimate_reuse_ratio(d.tolist(), q.tolist(), 64, device=DEV) for d in donors] == got
+
+
+def test_donor_store_reuse_on_device_matches_oracle():
+    """With no alignment override, the store estimates every candidate's reuse
+    on the device (one batched call) and aligns the winners on the device;
+    the matches equal the oracle's walk of the same steps: cosine top-2k,
+    Jaccard pre-filter, estimate_reuse_ratio, sim x reuse order, and the exact
+    chunk alignment's reuse as the final filter."""
+    from oracle import alignment as oal
+
+    chunk = 64
+    rng = np.random.default_rng(42)
+    q, donors = _token_cases(rng, chunk)
+    dim = 32
+    base = rng.standard_normal(dim).astype(np.float32)
+    embs = base + 0.2 * rng.standard_normal((len(donors), dim)).astype(np.float32)
+    query = base.copy()
+    store = ds.DonorStore(max_entries=16, embedding_dim=dim, min_similarity=0.6, chunk_size=chunk, device=DEV)
+    store.add_donors([ds.DonorNode(f"d{i}", d.tolist(), embs[i], timestamp=-1e9) for i, d in enumerate(donors)])
+    ms = store.find_donors(query, q.tolist(), top_k=3, min_reuse_ratio=0.2)
+
+    cand, sims = osearch.cosine_candidates(embs, np.ones(len(donors), bool), query, 0.6, 6)
+    qset = set(q.tolist())
+    scored = []
+    for i, s in zip(cand.tolist(), sims.tolist()):
+        dset = set(donors[i].tolist())
+        if len(qset & dset) / len(qset | dset) < 0.2:
+            continue
+        r = oal.estimate_reuse_ratio(donors[i].tolist(), q.tolist(), chunk)
+        if r >= 0.2:
+            scored.append((s * r, s, i))
+    scored.sort(key=lambda x: x[0], reverse=True)
+    want = []
+    for _, s, i in scored[:3]:
+        m = oal.chunk_matches(donors[i].tolist(), q.tolist(), chunk, True)
+        if (m >= 0).sum() * chunk / len(q) >= 0.2:
+            want.append((f"d{i}", s))
+    assert want, "the case must produce matches"
+    assert [m.donor.request_id for m in ms] == [w[0] for w in want]
+    np.testing.assert_allclose([m.similarity for m in ms], [w[1] for w in want], atol=TOL)
+    for m in ms:
+        assert m.alignment.reuse_ratio >= 0.2

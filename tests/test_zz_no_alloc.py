@@ -27,6 +27,7 @@ def _case(seed: int, dtype: torch.dtype, H: int, n_pairs: int, style: str):
     cache = torch.randn(nb, 2, H, bs, D, generator=g).to(dtype).to(DEV)
     bt = torch.randperm(nb, generator=g)[:40].to(torch.int32).to(DEV)
     perm = np.random.default_rng(seed).permutation(40 * bs)[:n_pairs]
+    assert perm.shape[0] == n_pairs, "the C calls read n_pairs positions: the arrays must hold that many"
     src = torch.from_numpy(np.sort(perm).astype(np.int32)).to(DEV)
     dst = torch.from_numpy(perm.astype(np.int32)).to(DEV)  # sources overlap targets
     rows, (n_layers, _, nh, _, hd), keep = _rows.paged_rows(cache, bt, "canonical")
@@ -81,7 +82,7 @@ def test_noalloc_second_call_with_skipped_pairs_and_layers():
     the stale scratch."""
     lib = _lib.load()
     stream = _lib.stream_ptr(DEV)
-    _run_both(seed=4, dtype=torch.bfloat16, H=4, n_pairs=700, style="neox")  # fills the scratch
+    _run_both(seed=4, dtype=torch.bfloat16, H=4, n_pairs=640, style="neox")  # fills the scratch
 
     g = torch.Generator().manual_seed(5)
     L, nb, H, bs, D, n_log = 3, 48, 2, 16, 128, 30
