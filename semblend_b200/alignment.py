@@ -286,6 +286,46 @@ def compute_chunk_alignment(donor_tokens, target_tokens, chunk_size: int = DEFAU
                            exact_chunks=sum(1 for m in match if m >= 0))
 
 
+def _token_set_alignment(donor_tokens, target_tokens) -> AlignmentResult:
+    """The reference's alignment when no whole chunk matches and rapidfuzz is
+    absent (alignment.py:852-853 -> :945-1020): each target token takes the
+    earliest unused donor position holding the same id.  Host logic, as in the
+    reference: it only runs for a store's winning candidates."""
+    free: dict[int, list[int]] = {}
+    for pos, tok in enumerate(donor_tokens):
+        free.setdefault(int(tok), []).append(pos)
+    taken: dict[int, int] = {}
+    actions: list[SlotAction] = []
+    n_reused = 0
+    for t_pos, tok in enumerate(target_tokens):
+        tok = int(tok)
+        cands = free.get(tok)
+        i = taken.get(tok, 0)
+        if cands is not None and i < len(cands):
+            taken[tok] = i + 1
+            actions.append(SlotAction("copy_from_donor", t_pos, cands[i]))
+            n_reused += 1
+        else:
+            actions.append(SlotAction("recompute", t_pos))
+    n = len(target_tokens)
+    return AlignmentResult(reuse_ratio=n_reused / max(n, 1), slot_actions=actions, edit_distance=n - n_reused,
+                           donor_len=len(donor_tokens), target_len=n)
+
+
+def compute_alignment(donor_tokens, target_tokens, chunk_size: int = DEFAULT_CHUNK_SIZE) -> AlignmentResult:
+    """compute_alignment (alignment.py:790-837) without its fuzzy-chunk stage:
+    the exact chunk alignment on the device, and when it reuses nothing, the
+    token-set alignment the reference falls back to without rapidfuzz.  (The
+    reference's fuzzy chunk matching, on by default there, is token-level
+    host work outside this library.)"""
+    res = compute_chunk_alignment(donor_tokens, target_tokens, chunk_size)
+    if res.reuse_ratio > 0:
+        return res
+    d = donor_tokens.tolist() if isinstance(donor_tokens, torch.Tensor) else list(donor_tokens)
+    t = target_tokens.tolist() if isinstance(target_tokens, torch.Tensor) else list(target_tokens)
+    return _token_set_alignment(d, t)
+
+
 __all__ = [
     "AlignmentResult",
     "DEFAULT_CHUNK_SIZE",
@@ -294,6 +334,7 @@ __all__ = [
     "chunk_alignment",
     "chunk_alignment_batch",
     "chunk_digests",
+    "compute_alignment",
     "compute_chunk_alignment",
     "estimate_chunk_reuse",
     "estimate_reuse_ratio",

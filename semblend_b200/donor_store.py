@@ -11,7 +11,7 @@ threshold / top-k stage of ``find_donor`` and ``find_donors`` (:205-229,
 candidates' reuse estimates (``estimate_reuse_ratio``, :256-262, :359-365)
 run on the device for all candidates at once; the Jaccard pre-filter stays
 host logic, and the winners' ``compute_alignment`` is the reference's when its
-package is installed, else the device chunk alignment.  ``alignment=
+package is installed, else :func:`semblend_b200.alignment.compute_alignment`.  ``alignment=
 (estimate_reuse_ratio, compute_alignment)`` overrides both.
 
 :meth:`DonorStore.search_batch` exposes the cosine stage for a batch of
@@ -36,17 +36,15 @@ DEFAULT_CHUNK_SIZE = 256  # semblend_core/alignment.py:35
 
 
 def _compute_alignment():
-    """The reference's compute_alignment when its package is installed (exact
-    chunks, then its fuzzy / Levenshtein fallbacks: token-level host work);
-    otherwise the exact chunk alignment on the device, which is the
-    reference's primary path (alignment.py:820-831)."""
+    """The reference's compute_alignment when its package is installed (fuzzy
+    chunks, exact chunks, then its Levenshtein / token-set fallbacks:
+    token-level host work); otherwise this library's: exact chunks on the
+    device, then the token-set fallback (alignment.py:790-837 without the
+    fuzzy stage)."""
     try:
         from semblend_core.alignment import compute_alignment
     except ImportError:
-        from .alignment import compute_chunk_alignment
-
-        def compute_alignment(donor_tokens, target_tokens, chunk_size=DEFAULT_CHUNK_SIZE):
-            return compute_chunk_alignment(donor_tokens, target_tokens, chunk_size)
+        from .alignment import compute_alignment
     return compute_alignment
 
 

@@ -22,7 +22,15 @@ Additions, all keyword-only with reference-compatible defaults:
 * ``rotary_style="interleaved" | "neox"`` — the reference rotates interleaved
   pairs ``(2i, 2i+1)``; Qwen/Llama checkpoints served by vLLM use neox
   half-rotation pairs ``(i, i + D/2)``.
-* ``layout="canonical" | "vllm" | "trtllm" | "auto"`` for paged caches.
+* ``layout="auto" | "canonical" | "vllm" | "trtllm"`` for paged caches.  The
+  default ``"auto"`` reads a per-layer cache as the reference's canonical
+  ``[num_blocks, 2, H, block_size, D]`` unless that reading is impossible
+  (dimension 1 is not 2) and the shape is vLLM's ``[2, num_blocks,
+  block_size, H, D]`` (the reference's own detection, rope_correction.py:740).
+  So every call the canonical reading accepts behaves as in the reference, and
+  the vLLM hook's calls, which pass vLLM caches without a layout
+  (model_runner_hook.py:538-555) and fail in the reference's permutation
+  (rope_correction.py:432 unpacks the shape as canonical), are served.
 * :func:`inject_donors` — every layer and every request of a step in one
   launch (the reference issues one launch per layer per request).
 """
@@ -36,6 +44,7 @@ import numpy as np
 import torch
 
 from . import _lib, _rows
+from .position_mapping import DevicePositionMapping
 
 HAS_TRITON = False  # kept for import compatibility; no Triton is used
 
@@ -117,7 +126,7 @@ def rope_correct_scatter_paged(
     head_dim: int | None = None,
     *,
     rotary_style: str = "interleaved",
-    layout: str = "canonical",
+    layout: str = "auto",
 ) -> torch.Tensor:
     """Scatter donor KV into a paged cache with RoPE correction on K.
 
@@ -229,24 +238,36 @@ def _upload_pairs(pairs: np.ndarray, device: torch.device) -> tuple[torch.Tensor
 
 
 def _permute(kv_cache, block_table, permutation, rope_base, mode, rotary_style, layout, fn):
-    pairs = _host_pairs(permutation)
-    if pairs.shape[0] == 0:
-        return
+    on_device = isinstance(permutation, DevicePositionMapping)
+    if on_device:
+        if permutation.donor_positions.numel() == 0:
+            return
+    else:
+        pairs = _host_pairs(permutation)
+        if pairs.shape[0] == 0:
+            return
     _lib.require_cuda(kv_cache, "kv_cache")
     layout = _rows.resolve_layout(kv_cache, layout)
     dev = kv_cache.device
     bt = _rows.device_index_tensor(block_table, dev, "block_table")
     rows, (n_layers, _, nh, bs, hd), keep = _rows.paged_rows(kv_cache, bt, layout)
-    n_logical = bt.shape[0]
-    if pairs.min() < 0 or (pairs // bs).max() >= n_logical:
-        bad = pairs[(pairs < 0).any(axis=1) | ((pairs // bs) >= n_logical).any(axis=1)][0]
-        raise IndexError(
-            f"{fn}: position pair {tuple(int(v) for v in bad)} is outside the block table "
-            f"({n_logical} blocks of {bs})"
-        )
-    pairs = _last_per_target(pairs)
-    sp, tp = _upload_pairs(pairs, dev)
-    n = pairs.shape[0]
+    if on_device:
+        # pairs stay on the device: out-of-range ones (and -1 padding) are skipped and counted
+        if permutation.device != dev:
+            raise ValueError(f"{fn}: the position mapping is on {permutation.device}, the cache on {dev}")
+        sp, tp = permutation.donor_positions, permutation.target_positions
+        n = sp.shape[0]
+    else:
+        n_logical = bt.shape[0]
+        if pairs.min() < 0 or (pairs // bs).max() >= n_logical:
+            bad = pairs[(pairs < 0).any(axis=1) | ((pairs // bs) >= n_logical).any(axis=1)][0]
+            raise IndexError(
+                f"{fn}: position pair {tuple(int(v) for v in bad)} is outside the block table "
+                f"({n_logical} blocks of {bs})"
+            )
+        pairs = _last_per_target(pairs)
+        sp, tp = _upload_pairs(pairs, dev)
+        n = pairs.shape[0]
     p = _rows.params(
         n_layers=n_layers, n_heads=nh, head_dim=hd, dtype=kv_cache.dtype, rotary_style=rotary_style,
         k_angle=_MODES[mode], kv_select=_lib.SB_KV_BOTH,
@@ -271,7 +292,7 @@ def permute_paged_kv_with_rope(
     rope_base: float = 10000.0,
     *,
     rotary_style: str = "interleaved",
-    layout: str = "canonical",
+    layout: str = "auto",
 ) -> None:
     """Permute KV rows inside a paged cache in place, rotating K by
     ``RoPE(target - source)``.
@@ -280,6 +301,10 @@ def permute_paged_kv_with_rope(
     snapshotted before any write, so sources may overlap targets.  Positions
     outside the block table raise ``IndexError`` as the reference's indexing
     does; when a target appears more than once the last pair wins.
+    ``permutation`` may also be a
+    :class:`~semblend_b200.position_mapping.DevicePositionMapping`: its pairs
+    stay on the device, out-of-range pairs and -1 padding are skipped and
+    counted instead of raising, and each target must appear once.
     """
     _permute(kv_cache, block_table, permutation, rope_base, "delta", rotary_style, layout,
              "permute_paged_kv_with_rope")
@@ -292,7 +317,7 @@ def nope_permute_paged_kv(
     rope_base: float = 10000.0,
     *,
     rotary_style: str = "interleaved",
-    layout: str = "canonical",
+    layout: str = "auto",
 ) -> None:
     """NoPE two-step correction: strip ``RoPE(source)`` then apply
     ``RoPE(target)`` to K, copy V.
@@ -366,6 +391,13 @@ class DonorInjection:
     donor_positions: torch.Tensor
     target_positions: torch.Tensor
 
+    @classmethod
+    def from_mapping(cls, donor_kv: torch.Tensor, block_table: torch.Tensor,
+                     mapping: DevicePositionMapping) -> DonorInjection:
+        """The job of one donor's device position mapping (its -1 padding,
+        if any, is skipped by the kernel and counted as skipped pairs)."""
+        return cls(donor_kv, block_table, mapping.donor_positions, mapping.target_positions)
+
 
 def inject_donors(
     kv_cache: torch.Tensor | Sequence[torch.Tensor],
@@ -374,7 +406,7 @@ def inject_donors(
     *,
     mode: str = "delta",
     rotary_style: str = "interleaved",
-    layout: str = "canonical",
+    layout: str = "auto",
 ) -> None:
     """Inject several requests' donor KV into a multi-layer paged cache.
 
@@ -436,7 +468,7 @@ def inject_plan(
     *,
     mode: str = "delta",
     rotary_style: str = "interleaved",
-    layout: str = "canonical",
+    layout: str = "auto",
 ) -> int:
     """Inject one request's donor rows for every partial layer of a
     :class:`~semblend_b200.partial_attention.PartialAttentionPlan` in one launch.

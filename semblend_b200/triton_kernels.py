@@ -65,7 +65,7 @@ def scatter_donor_kv_paged(
     donor_positions: torch.Tensor,
     target_positions: torch.Tensor,
     *,
-    layout: str = "canonical",
+    layout: str = "auto",
 ) -> torch.Tensor:
     """Copy donor K,V rows into a paged cache through the block table.
 

@@ -160,3 +160,50 @@ def test_layer_results_shared_and_invalidated():
     assert pa.compute_donor_kv_indices(plan, 3) == want_pairs[1:]
     assert pa.compute_attention_mask(plan, 3).tolist() == [True] + [False] * 7 + [True] * 4
     assert pa.compute_donor_kv_indices(plan, 0) == want_pairs
+
+
+def test_position_mapping_host_classes():
+    """The host PositionMapping / MultiDonorPositionMapping keep the
+    reference's fields and properties (pipeline.py:62-80,
+    multi_donor_types.py:50-78); the device form needs a CUDA device."""
+    from semblend_b200 import _lib
+    from semblend_b200.position_mapping import DevicePositionMapping, MultiDonorPositionMapping, PositionMapping
+
+    assert PositionMapping().num_pairs == 0 and not PositionMapping().needs_correction
+    pm = PositionMapping([0, 1, 2, 3], [2, 3, 0, 1])
+    assert pm.num_pairs == 4 and pm.needs_correction
+    md = MultiDonorPositionMapping(("x", "y", "x"), (0, 1, 2), (0, 5, 2))
+    assert md.needs_correction and md.num_pairs == 3
+    sub = md.for_donor("x")
+    assert sub.donor_positions == (0, 2) and sub.target_positions == (0, 2) and not sub.needs_correction
+    with pytest.raises(_lib.NativeLibraryError):
+        DevicePositionMapping(torch.zeros(2, dtype=torch.int32), torch.zeros(2, dtype=torch.int32), 2)
+
+
+def test_token_set_alignment_matches_reference():
+    """The no-rapidfuzz fallback of compute_alignment restated for the store
+    (alignment.py:945-1020) gives the reference's slot actions."""
+    from tests.golden.make_golden import REF
+
+    if REF is None or not (REF / "semblend_core").is_dir():
+        pytest.skip("no reference checkout named by SEMBLEND_REFERENCE")
+    sys.path.insert(0, str(REF))
+    try:
+        import importlib
+
+        ref = importlib.import_module("semblend_core.alignment")
+        from semblend_b200.alignment import _token_set_alignment
+
+        rng = np.random.default_rng(5)
+        for n_d, n_t, vocab in ((300, 250, 50), (10, 40, 8), (0, 5, 3), (64, 0, 9)):
+            d = rng.integers(0, vocab, n_d).tolist()
+            t = rng.integers(0, vocab, n_t).tolist()
+            a, b = _token_set_alignment(d, t), ref._token_set_alignment(d, t)
+            assert a.reuse_ratio == b.reuse_ratio and a.edit_distance == b.edit_distance
+            assert [(x.action, x.target_pos, x.donor_pos) for x in a.slot_actions] == \
+                [(str(x.action.value) if hasattr(x.action, "value") else x.action, x.target_pos, x.donor_pos)
+                 for x in b.slot_actions]
+    finally:
+        sys.path.remove(str(REF))
+        for k in [k for k in sys.modules if k.split(".")[0] == "semblend_core"]:
+            del sys.modules[k]
