@@ -326,6 +326,16 @@ def run_ours(args, world, rank, local) -> dict | None:
     total_ms = max_over_ranks(t0.elapsed_time(t1), world)
     kernel_ms_max = max_over_ranks(kt.mean_ms, world)
 
+    # --- A/B: the same launches with the source rows staged through 1-D bulk copies ---
+    for _ in range(2):
+        rc.inject_donors(cache, injections, rope_base=ROPE_THETA, rotary_style="neox", staging="bulk")
+    torch.cuda.synchronize(dev)
+    with _lib.KernelTimer(args.steps) as kt_bulk:
+        for _ in range(args.steps):
+            rc.inject_donors(cache, injections, rope_base=ROPE_THETA, rotary_style="neox", staging="bulk")
+        torch.cuda.synchronize(dev)
+    bulk_ms_max = max_over_ranks(kt_bulk.mean_ms, world)
+
     # --- end to end through the public API with host buffers ---
     h2d = sum(h.numel() * h.element_size() for h in host_pos) + sum(h.numel() * h.element_size() for h in host_bt)
     status = torch.empty(1, dtype=torch.int64).pin_memory()
@@ -400,6 +410,11 @@ def run_ours(args, world, rank, local) -> dict | None:
             "algorithmic_bytes_per_launch": rank_bytes,
             "kernel": "inject_kernel<bf16, 8> (slowest rank; CUDA events on the launch stream)",
             "kernel_ms": round(kernel_ms_max, 4),
+            "staging_ab": {"bulk_staged_kernel_ms": round(bulk_ms_max, 4),
+                           "bulk_staged_frac": round(rank_bytes / (bulk_ms_max * 1e-3) / 1e9 / pk["hbm_gbs"], 4),
+                           "note": "inject_bulk_kernel (SB_INJECT_BULK_STAGED: source rows through 1-D "
+                                   "cp.async.bulk into a 3-stage shared-memory ring) on the same step; the "
+                                   "direct path above is the default"},
         },
         "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": 8, "api": "semblend_b200.rope_correction.inject_donors",
@@ -775,6 +790,7 @@ def run_search_sharded(args, world: int, rank: int, local: int) -> dict | None:
     emb, queries = make_search_inputs(dev, SEED + 3, n_rows=n_rows)
     m = ShardedDonorMatrix(n_rows, S_DIM, device=dev)
     m.write_range(0, emb)
+    e_host = emb.cpu().numpy() if rank == 0 else None  # rank 0 checks merged results against the oracle
     del emb
     torch.cuda.empty_cache()
 
@@ -850,11 +866,23 @@ def run_search_sharded(args, world: int, rank: int, local: int) -> dict | None:
     fill = float((ids >= 0).float().mean().item())
     if rank != 0:
         return None
+    # the merged result of 8 sampled queries against the oracle (the reference's per-query stage)
+    from oracle import search as osearch
+
+    sample = np.random.default_rng(SEED).choice(S_QUERIES, 8, replace=False)
+    ids_o, sc_o = osearch.topk_batch(e_host, np.ones(n_rows, bool), queries.cpu().numpy()[sample], S_THR, S_K)
+    ids_g, sc_g = ids.cpu().numpy()[sample], sc.cpu().numpy()[sample]
+    agree = int(sum(
+        np.array_equal(ids_o[j][ids_o[j] >= 0], ids_g[j][ids_g[j] >= 0])
+        or np.allclose(sc_o[j][: (ids_o[j] >= 0).sum()], sc_g[j][: (ids_o[j] >= 0).sum()], atol=1e-6)
+        for j in range(len(sample))))
     pk = peaks()
     flops_rank = 2.0 * (m.row_end - m.row_begin) * S_QUERIES * S_DIM
     achieved = flops_rank / (kms * 1e-3) / 1e12
     return {
         "component": "c3_search_sharded",
+        "matches_oracle": bool(agree == len(sample) and st == 0),
+        "oracle_check": f"{agree}/{len(sample)} sampled queries of the merged result equivalent to the oracle's",
         "metric": "donor search q/s",
         "value": round(S_QUERIES / (ms * 1e-3), 1),
         "unit": "q/s",
@@ -1077,6 +1105,28 @@ def run_attention_sharded(args, world: int, rank: int, local: int) -> dict | Non
     ms = max_over_ranks(t0.elapsed_time(t1) / steps, world)
     kms = max_over_ranks(kt.mean_ms, world)
     st = int(status.item())
+    kms_rank0 = kt.mean_ms
+    # end to end: the rank's compute masks from pinned host memory in, its row counts out
+    hmask = torch.from_numpy(masks[b0:b1].copy()).pin_memory()
+    dmask = torch.empty(hmask.shape, dtype=torch.bool, device=dev)
+    hcnt = torch.empty(b1 - b0, dtype=torch.int32).pin_memory()
+
+    def e2e_step():
+        dmask.copy_(hmask, non_blocking=True)
+        r_, c_ = tk.mask_to_rows(dmask)
+        tk.gqa_partial_attention(qs, ks, vs, r_, c_, os_, max_rows=S, status=status)
+        hcnt.copy_(c_, non_blocking=True)
+
+    e2e_step()
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / steps, world)
     # parity: 64 seeded rows of the rank's first batch element, its query heads, against the fp32 oracle
     pos = np.nonzero(masks[b0])[0]
     sample = np.sort(np.random.default_rng(SEED + rank).choice(pos, 64, replace=False))
@@ -1089,7 +1139,6 @@ def run_attention_sharded(args, world: int, rank: int, local: int) -> dict | Non
     ok = min_over_ranks(int(err <= 2e-2 and st == 0), world)
     flops = attention_flops(masks, A_HQ, A_D)
     rank_flops = attention_flops(masks[b0:b1], g * (h1 - h0), A_D)
-    kms_rank0 = kt.mean_ms
     del q, k, v, out
     torch.cuda.empty_cache()
     if rank != 0:
@@ -1110,6 +1159,9 @@ def run_attention_sharded(args, world: int, rank: int, local: int) -> dict | Non
                      "traffic": None},
         "oracle_check": f"rank 0: max |gpu - fp32 oracle| = {err:.2e} over 64 rows x {g * (h1 - h0)} heads "
                         "(bar 2e-2); every rank checked",
+        "e2e": {"value": round(flops / (e2e_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
+                "h2d_bytes_per_step": int(hmask.numel()), "d2h_bytes_per_step": 4 * (b1 - b0),
+                "api": "semblend_b200.triton_kernels.gqa_partial_attention (rank's mask in, its row counts out)"},
         "gpu_launches": steps,
     }
 
@@ -1334,6 +1386,8 @@ def run_c5(args, world: int, rank: int, local: int) -> dict | None:
     for fn, n_launch in ((lambda: cosine_topk_async(m.emb, m.emb16, m.valid, m.stats, queries, S_K, S_THR,
                                                     status=s_status, workspace_owner=m, out=s_out), 1),
                          (lambda: rc.inject_donors(cache, inj, rope_base=C5_THETA, rotary_style="neox"), 1),
+                         (lambda: rc.inject_donors(cache, inj, rope_base=C5_THETA, rotary_style="neox",
+                                                   staging="bulk"), 1),
                          (lambda: tk.gqa_partial_attention(q, k, v, rows, counts, out, max_rows=s_max,
                                                            status=a_status), C5_L)):
         with _lib.KernelTimer(steps * n_launch) as kt:
@@ -1341,6 +1395,7 @@ def run_c5(args, world: int, rank: int, local: int) -> dict | None:
                 fn()
             torch.cuda.synchronize(dev)
         kern.append(max_over_ranks(kt.total_ms / steps, world))
+    kern = [kern[0], kern[1], kern[3], kern[2]]  # screen, inject (direct), attention, inject (bulk-staged)
 
     # end to end: this step's pair lists, block tables, queries and masks from pinned host
     # memory; search ids and the skipped-pair count back to the host
@@ -1416,6 +1471,7 @@ def run_c5(args, world: int, rank: int, local: int) -> dict | None:
                           "attention_80_layers": round(parts[2], 3),
                           "note": "in-step event brackets around each part's API calls (host work included)"},
         "kernel_ms": {"screen": round(kern[0], 4), "inject": round(kern[1], 4), "attention_80_layers": round(kern[2], 3),
+                      "inject_bulk_staged": round(kern[3], 4),
                       "note": "each part's dominant kernels alone, library events on the launch stream"},
         "roofline": {
             "search": {"bound": "tensor", "achieved": round(search_flops / (kern[0] * 1e-3) / 1e12, 1),

@@ -112,6 +112,15 @@ typedef struct sb_inject_desc {
  * rows were snapshotted out of dst and are read back by pair index). */
 #define SB_DESC_CHECK_SRC_IN_DST 1
 
+/* sb_inject_params.flags: stage the source rows in shared memory through
+ * 1-D bulk copies (cp.async.bulk, one per run of contiguous rows, a 3-stage
+ * ring per CTA) instead of direct 16-byte loads.  Applies when every row is a
+ * whole number of 16-byte vectors at 16-byte aligned addresses (otherwise the
+ * direct path runs); same results.  Off by default: on B200 the direct path
+ * is faster on the reference's workloads except for whole-chunk reuse (see
+ * the bench's A/B). */
+#define SB_INJECT_BULK_STAGED 1
+
 /* Parameters shared by every descriptor of one call. */
 typedef struct sb_inject_params {
   int32_t n_layers;
@@ -121,7 +130,7 @@ typedef struct sb_inject_params {
   int32_t rotary_style; /* SB_ROTARY_* */
   int32_t k_angle;      /* SB_ANGLE_* for K rows; V rows are always copied */
   int32_t kv_select;    /* SB_KV_* */
-  int32_t reserved;
+  int32_t flags;        /* SB_INJECT_* bits (0: the default path) */
   int64_t const_delta;    /* for SB_ANGLE_CONST */
   const float *inv_freq;  /* device, head_dim/2 floats; unused for SB_ANGLE_NONE */
 } sb_inject_params;

@@ -33,6 +33,7 @@ SB_KV_K, SB_KV_V, SB_KV_BOTH = 1, 2, 3
 SB_MAX_INJECT_DESC = 64
 SB_PERMUTE_NOALLOC_SCRATCH_BYTES = 32 << 20
 SB_DESC_CHECK_SRC_IN_DST = 1
+SB_INJECT_BULK_STAGED = 1
 
 _DTYPES = {torch.float32: SB_DTYPE_F32, torch.float16: SB_DTYPE_F16, torch.bfloat16: SB_DTYPE_BF16}
 _INDEX_DTYPES = {torch.int32: SB_INDEX_I32, torch.int64: SB_INDEX_I64}
@@ -83,7 +84,7 @@ class SbInjectParams(ctypes.Structure):
         ("rotary_style", ctypes.c_int32),
         ("k_angle", ctypes.c_int32),
         ("kv_select", ctypes.c_int32),
-        ("reserved", ctypes.c_int32),
+        ("flags", ctypes.c_int32),
         ("const_delta", ctypes.c_int64),
         ("inv_freq", ctypes.c_void_p),
     ]

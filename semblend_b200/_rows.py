@@ -192,8 +192,12 @@ def params(
     kv_select: int,
     inv_freq: torch.Tensor | None,
     const_delta: int = 0,
+    staging: str = "direct",
 ) -> _lib.SbInjectParams:
+    if staging not in ("direct", "bulk"):
+        raise ValueError(f"staging must be 'direct' or 'bulk', got {staging!r}")
     p = _lib.SbInjectParams()
+    p.flags = _lib.SB_INJECT_BULK_STAGED if staging == "bulk" else 0
     p.n_layers = n_layers
     p.n_heads = n_heads
     p.head_dim = head_dim

@@ -39,9 +39,13 @@ constexpr int kBM = 128;
 constexpr int kBN = 128;
 constexpr int kD = 128;
 // One pair of exponentials in every SB_ATTN_POLY_EVERY is evaluated as a
-// polynomial on the FMA pipe instead of MUFU (0: all on MUFU).
+// polynomial on the FMA pipe instead of MUFU (0: all on MUFU).  All on MUFU
+// measured fastest on B200 (c4 1,103 against 1,036-1,041 TFLOP/s for 1 in 4,
+// 997 for 1 in 2; a c5 layer 978 against 923-929 and 877): the polynomial's
+// 12 instructions a pair load the FMA pipe and the issue slots more than the
+// MUFU time they save.
 #ifndef SB_ATTN_POLY_EVERY
-#define SB_ATTN_POLY_EVERY 4
+#define SB_ATTN_POLY_EVERY 0
 #endif
 constexpr int kPolyEvery = SB_ATTN_POLY_EVERY;
 

@@ -28,6 +28,7 @@
 
 #include "common.cuh"
 #include "prof.cuh"
+#include "tcgen05.cuh"
 
 namespace sb {
 namespace {
@@ -313,6 +314,229 @@ __global__ void __launch_bounds__(kThreads, SB_INJECT_MIN_BLOCKS)
   }
 }
 
+// ---------------------------------------------------------------------------
+// Bulk-copy-staged variant.  The same work split as inject_kernel (a CTA owns a
+// tile of pairs and a chunk of (layer, kv, head) units, a consumer thread owns
+// one pair and the two 16-byte halves of its RoPE pairs), but the source rows
+// reach shared memory through 1-D cp.async.bulk copies issued by one producer
+// thread: for every unit, the tile's source rows (one copy per run of
+// contiguous rows: chunk-shifted donors give runs of up to the whole tile) land
+// in a ring of kBulkStages stages of 8 KB, so each CTA keeps up to
+// kBulkStages x 8 KB of reads in flight without holding them in registers.
+// Consumers rotate K in registers and store 16-byte vectors to the destination
+// rows.  Selected by SB_INJECT_BULK_STAGED when every row is a whole number of
+// 16-byte vectors at 16-byte aligned addresses (the copies' alignment rule).
+// Measured against the direct path on B200: slower on c2 (1.93-1.96 against
+// 1.77 ms: a 32-pair tile there breaks into ~5 runs at the recompute holes,
+// and the donor chunks that overlap are served by L2 either way) and on c1,
+// within 3 % faster on c5 (whole 256-token chunks: one copy a unit).  Every wait is bounded: a
+// stalled pipeline (never expected: producer and consumers are the same CTA)
+// gives up, counts the tile's pairs as skipped, and the producer waits for the
+// copies it has in flight before the CTA exits.
+// ---------------------------------------------------------------------------
+#ifndef SB_INJECT_BULK_STAGES
+#define SB_INJECT_BULK_STAGES 3
+#endif
+constexpr int kBulkStages = SB_INJECT_BULK_STAGES;
+constexpr int kBulkConsumers = kThreads;             // 8 warps, as inject_kernel
+constexpr int kBulkThreads = kBulkConsumers + 32;    // + the producer warp
+constexpr int kStageBytes = kBulkConsumers * 32;     // pairs of a tile x row bytes (2 x 16 B per thread)
+constexpr long long kBulkWaitCycles = 1LL << 31;     // about a second
+constexpr size_t kBulkDynSmem = (size_t)kBulkStages * kStageBytes + 128;
+
+__device__ __forceinline__ void bulk_load(void *smem_dst, const void *gmem_src, uint32_t bytes, uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          tc::smem_u32(smem_dst)),
+      "l"(gmem_src), "r"(bytes), "r"(tc::smem_u32(bar))
+      : "memory");
+}
+
+template <typename T, typename LT, bool NOPE>
+__global__ void __launch_bounds__(kBulkThreads, SB_INJECT_MIN_BLOCKS)
+    inject_bulk_kernel(const __grid_constant__ LT L) {
+  constexpr int VEC = 16 / (int)sizeof(T);
+  extern __shared__ uint8_t bulk_smem_raw[];
+  uint8_t *stages = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(bulk_smem_raw) + 127) & ~uintptr_t(127));
+  __shared__ uint64_t full[kBulkStages], empty[kBulkStages];
+  __shared__ int abort_flag;
+  __shared__ int64_t pair_soff[kBulkConsumers];
+  __shared__ int32_t run_p0[kBulkConsumers], run_len[kBulkConsumers];
+  __shared__ uint8_t pair_ok[kBulkConsumers];
+  __shared__ sb_inject_desc s_desc;
+  __shared__ int64_t s_first;
+
+  const InjectCommon &C = L.c;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int64_t tile = blockIdx.x;
+  if (threadIdx.x == 0) {
+    s_desc = find_desc(L, tile, s_first);
+    for (int i = 0; i < kBulkStages; ++i) {
+      tc::mbar_init(&full[i], 1);
+      tc::mbar_init(&empty[i], kBulkConsumers / 32);
+    }
+    abort_flag = 0;
+    tc::fence_mbar_init();
+  }
+  __syncthreads();
+  const sb_inject_desc &d = s_desc;
+  const sb_inject_params &P = C.p;
+  const int D = P.head_dim;
+  const int row_bytes = D * (int)sizeof(T);
+  const int H = P.n_heads;
+  const int ua = (int)((int64_t)blockIdx.y * C.units_per_chunk);
+  const int nrow = (int)min((int64_t)C.units_per_chunk, C.n_units - ua);
+  const tc::Abort ab{&abort_flag, nullptr};
+
+  // ---- per-pair rows (consumer threads), as inject_kernel ----
+  const int tpr = C.tpr;
+  const int pl = threadIdx.x / tpr;
+  const int slice = threadIdx.x - pl * tpr;
+  bool ok = false;
+  int64_t sp = 0, tp = 0, soff = 0, doff = 0;
+  // when tpr does not divide the block (head_dim 96: 6 threads a pair, 42 pairs), the last
+  // threads own no pair; they still take part in every barrier
+  if (warp < kBulkConsumers / 32 && pl < C.pairs_per_tile) {
+    const int64_t pair = (tile - s_first) * C.pairs_per_tile + pl;
+    if (pair < d.n_pairs) {
+      sp = load_index(d.src_pos, pair, d.pos_dtype);
+      tp = load_index(d.dst_pos, pair, d.pos_dtype);
+      const int64_t srow = d.src_row == SB_ROW_AT_PAIR ? pair : (d.src_row == SB_ROW_AT_DST_POS ? tp : sp);
+      const int64_t drow = d.dst_row == SB_ROW_AT_PAIR ? pair : (d.dst_row == SB_ROW_AT_SRC_POS ? sp : tp);
+      int64_t chk = 0;
+      ok = resolve_row(d.src, srow, soff) && resolve_row(d.dst, drow, doff);
+      if (ok && (d.flags & SB_DESC_CHECK_SRC_IN_DST)) ok = resolve_row(d.dst, sp, chk);
+      if (!ok && blockIdx.y == 0 && slice == 0 && C.err != nullptr) atomicAdd(C.err, 1ull);
+    }
+    if (slice == 0) {
+      pair_ok[pl] = ok ? 1 : 0;
+      pair_soff[pl] = soff;
+    }
+  }
+  __syncthreads();
+
+  if (warp == kBulkConsumers / 32) {
+    // ------------------------------ producer ------------------------------
+    if (lane == 0) {
+      // runs of valid pairs whose source rows follow each other in memory
+      const bool contig = d.src.stride_pos == D && d.src.stride_dim == 1;
+      int n_runs = 0;
+      uint32_t tx = 0;
+      for (int p = 0; p < C.pairs_per_tile; ++p) {
+        if (!pair_ok[p]) continue;
+        tx += (uint32_t)row_bytes;
+        if (n_runs > 0 && contig && run_p0[n_runs - 1] + run_len[n_runs - 1] == p &&
+            pair_soff[p] == pair_soff[run_p0[n_runs - 1]] + (int64_t)run_len[n_runs - 1] * D) {
+          ++run_len[n_runs - 1];
+        } else {
+          run_p0[n_runs] = p;
+          run_len[n_runs] = 1;
+          ++n_runs;
+        }
+      }
+      int h = ua % H, kvi = (ua / H) % C.n_kv_sel, l = (ua / H) / C.n_kv_sel;
+      int issued = 0;
+      for (int i = 0; i < nrow; ++i) {
+        const int st = i % kBulkStages;
+        if (i >= kBulkStages && !tc::mbar_wait(&empty[st], ((i / kBulkStages) - 1) & 1, ab, 1, kBulkWaitCycles))
+          break;
+        const int kv = C.kv_first + kvi;
+        const T *base = layer_base<T>(d.src, l) + kv * d.src.stride_kv + h * d.src.stride_head;
+        if (++h == H) {
+          h = 0;
+          if (++kvi == C.n_kv_sel) {
+            kvi = 0;
+            ++l;
+          }
+        }
+        tc::mbar_arrive_expect_tx(&full[st], tx);
+        uint8_t *stage = stages + (size_t)st * kStageBytes;
+        for (int r = 0; r < n_runs; ++r) {
+          const T *src = base + pair_soff[run_p0[r]];
+          // the copy's alignment rule (16-byte addresses and sizes) holds by the launch's choice
+          // of this kernel; a row that broke it is left out and its stage never completes
+          if ((reinterpret_cast<uintptr_t>(src) & 15) == 0)
+            bulk_load(stage + (size_t)run_p0[r] * row_bytes, src, (uint32_t)(run_len[r] * row_bytes), &full[st]);
+        }
+        ++issued;
+      }
+      // the copies in flight land before the CTA can exit (only an abort leaves any)
+      const int from = issued > kBulkStages ? issued - kBulkStages : 0;
+      volatile int never = 0;
+      const tc::Abort drain{&never, nullptr};
+      for (int i = from; i < issued; ++i)
+        tc::mbar_wait(&full[i % kBulkStages], (i / kBulkStages) & 1, drain, 0, kBulkWaitCycles);
+    }
+    return;
+  }
+
+  // ------------------------------ consumers ------------------------------
+  const bool neox = P.rotary_style == SB_ROTARY_NEOX;
+  int oa, ob;
+  if (neox) {
+    oa = slice * VEC;
+    ob = D / 2 + slice * VEC;
+  } else {
+    oa = 2 * slice * VEC;
+    ob = oa + VEC;
+  }
+  const bool rot = P.k_angle != SB_ANGLE_NONE && (P.kv_select & SB_KV_K);
+  float c1[VEC], s1[VEC], c2[NOPE ? VEC : 1], s2[NOPE ? VEC : 1];
+#pragma unroll
+  for (int e = 0; e < VEC; ++e) c1[e] = 1.f, s1[e] = 0.f;
+#pragma unroll
+  for (int e = 0; e < (NOPE ? VEC : 1); ++e) c2[e] = 1.f, s2[e] = 0.f;
+  if (rot && ok) {
+    float m1, m2 = 0.f;
+    if (P.k_angle == SB_ANGLE_DELTA) {
+      m1 = (float)(tp - sp);
+    } else if (P.k_angle == SB_ANGLE_CONST) {
+      m1 = (float)P.const_delta;
+    } else {
+      m1 = (float)sp;
+      m2 = (float)tp;
+    }
+    const int f0 = slice * VEC;
+#pragma unroll
+    for (int e = 0; e < VEC; ++e) {
+      const float f = P.inv_freq[f0 + e];
+      sincos_f32(__fmul_rn(m1, f), s1[e], c1[e]);
+      if (NOPE) sincos_f32(__fmul_rn(m2, f), s2[e], c2[e]);
+    }
+  }
+  int h = ua % H, kvi = (ua / H) % C.n_kv_sel, l = (ua / H) / C.n_kv_sel;
+  bool stalled = false;
+#pragma unroll 1
+  for (int i = 0; i < nrow; ++i) {
+    const int st = i % kBulkStages;
+    if (!tc::mbar_wait(&full[st], (i / kBulkStages) & 1, ab, 2, kBulkWaitCycles)) {
+      stalled = true;
+      break;
+    }
+    const int kv = C.kv_first + kvi;
+    if (ok) {
+      const uint8_t *row = stages + (size_t)st * kStageBytes + (size_t)pl * row_bytes;
+      Vec<T, VEC> va, vb;
+      va = *reinterpret_cast<const Vec<T, VEC> *>(row + oa * (int)sizeof(T));
+      vb = *reinterpret_cast<const Vec<T, VEC> *>(row + ob * (int)sizeof(T));
+      if (rot && kv == 0) rotate_vectors<T, VEC, NOPE>(va, vb, neox, c1, s1, c2, s2);
+      T *t = layer_base<T>(d.dst, l) + kv * d.dst.stride_kv + h * d.dst.stride_head + doff;
+      store_vec(t + oa, va);
+      store_vec(t + ob, vb);
+    }
+    if (++h == H) {
+      h = 0;
+      if (++kvi == C.n_kv_sel) {
+        kvi = 0;
+        ++l;
+      }
+    }
+    __syncwarp();
+    if (lane == 0) tc::mbar_arrive(&empty[st]);
+  }
+  if (stalled && ok && slice == 0 && C.err != nullptr) atomicAdd(C.err, 1ull);
+}
+
 int sm_count() {
   int dev = 0, n = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return 148;
@@ -353,11 +577,18 @@ int pick_vec(const sb_inject_desc *descs, int n, int D, int es) {
 
 template <typename T, int VEC, typename LT>
 int launch_typed(const LT &L, dim3 grid, cudaStream_t st) {
+  const bool nope = L.c.p.k_angle == SB_ANGLE_NOPE && (L.c.p.kv_select & SB_KV_K);
   const int slot = prof_before(st);
-  if (L.c.p.k_angle == SB_ANGLE_NOPE && (L.c.p.kv_select & SB_KV_K))
+  if ((L.c.p.flags & SB_INJECT_BULK_STAGED) && VEC * (int)sizeof(T) == 16) {
+    if (nope)
+      inject_bulk_kernel<T, LT, true><<<grid, kBulkThreads, kBulkDynSmem, st>>>(L);
+    else
+      inject_bulk_kernel<T, LT, false><<<grid, kBulkThreads, kBulkDynSmem, st>>>(L);
+  } else if (nope) {
     inject_kernel<T, VEC, LT, true><<<grid, kThreads, 0, st>>>(L);
-  else
+  } else {
     inject_kernel<T, VEC, LT, false><<<grid, kThreads, 0, st>>>(L);
+  }
   prof_after(slot, st);
   return launch_status();
 }
@@ -392,6 +623,7 @@ int validate_params(const sb_inject_params *p) {
     return SB_ERR_INVALID_ARGUMENT;
   if (p->k_angle < SB_ANGLE_NONE || p->k_angle > SB_ANGLE_CONST) return SB_ERR_INVALID_ARGUMENT;
   if (p->kv_select < 1 || p->kv_select > 3) return SB_ERR_INVALID_ARGUMENT;
+  if (p->flags & ~SB_INJECT_BULK_STAGED) return SB_ERR_INVALID_ARGUMENT;
   if (p->k_angle != SB_ANGLE_NONE && (p->kv_select & SB_KV_K) && p->inv_freq == nullptr)
     return SB_ERR_INVALID_ARGUMENT;
   return SB_OK;

@@ -127,6 +127,7 @@ def rope_correct_scatter_paged(
     *,
     rotary_style: str = "interleaved",
     layout: str = "auto",
+    staging: str = "direct",
 ) -> torch.Tensor:
     """Scatter donor KV into a paged cache with RoPE correction on K.
 
@@ -135,7 +136,8 @@ def rope_correct_scatter_paged(
     and V is copied; ``kv_cache`` ``[num_blocks, 2, H, block_size, D]`` (or
     the ``layout`` given) is modified in place and returned.
     ``donor_kv`` is ``[2, H, donor_len, D]``; ``block_table`` maps the
-    request's logical blocks to physical blocks.
+    request's logical blocks to physical blocks.  ``staging="bulk"`` selects
+    the bulk-copy-staged kernel (same results).
     """
     if donor_positions.shape[0] == 0:
         return kv_cache
@@ -156,7 +158,7 @@ def rope_correct_scatter_paged(
     p = _rows.params(
         n_layers=1, n_heads=nh, head_dim=hd, dtype=kv_cache.dtype, rotary_style=rotary_style,
         k_angle=_lib.SB_ANGLE_DELTA, kv_select=_lib.SB_KV_BOTH,
-        inv_freq=_lib.inv_freq(rope_base, hd, dev),
+        inv_freq=_lib.inv_freq(rope_base, hd, dev), staging=staging,
     )
     _launch([desc], p, dev, "rope_correct_scatter_paged")
     del keep
@@ -407,6 +409,7 @@ def inject_donors(
     mode: str = "delta",
     rotary_style: str = "interleaved",
     layout: str = "auto",
+    staging: str = "direct",
 ) -> None:
     """Inject several requests' donor KV into a multi-layer paged cache.
 
@@ -415,7 +418,9 @@ def inject_donors(
     ``layout`` or a list of ``L`` per-layer tensors (vLLM's ``kv_caches``).
     ``mode`` is ``"delta"`` (``RoPE(target - donor)``, as
     :func:`rope_correct_scatter_paged`), ``"nope"`` (strip, then apply) or
-    ``"copy"`` (as ``scatter_donor_kv_paged``).
+    ``"copy"`` (as ``scatter_donor_kv_paged``).  ``staging="bulk"`` stages the
+    source rows in shared memory through 1-D bulk copies instead of direct
+    16-byte loads (same results; see ``SB_INJECT_BULK_STAGED``).
     """
     if not injections:
         return
@@ -453,7 +458,7 @@ def inject_donors(
     p = _rows.params(
         n_layers=n_layers, n_heads=nh, head_dim=hd, dtype=first.dtype, rotary_style=rotary_style,
         k_angle=_MODES[mode], kv_select=_lib.SB_KV_BOTH,
-        inv_freq=_lib.inv_freq(rope_base, hd, dev) if mode != "copy" else None,
+        inv_freq=_lib.inv_freq(rope_base, hd, dev) if mode != "copy" else None, staging=staging,
     )
     _launch(descs, p, dev, "inject_donors")
     del keep

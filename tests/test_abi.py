@@ -82,3 +82,14 @@ def test_struct_layouts_match_header(tmp_path):
         assert ctypes.sizeof(cls) == layout[c], (c, ctypes.sizeof(cls), layout[c])
         for f in cls._fields_:
             assert getattr(cls, f[0]).offset == layout[f"{c}.{f[0]}"], (c, f[0])
+
+
+def test_inject_params_flags_field():
+    """The params struct's flags word sits where the header puts it (the
+    ctypes mirror and the C layout agree) and only known bits are accepted."""
+    import ctypes
+
+    from semblend_b200 import _lib
+
+    assert _lib.SbInjectParams.flags.offset == 28 and ctypes.sizeof(_lib.SbInjectParams) == 48
+    assert _lib.SB_INJECT_BULK_STAGED == 1

@@ -455,3 +455,78 @@ def test_c1_full_size_matches_oracle():
     _split_check(out, want, style="neox")
     _untouched_exact(out, cache, bt, t)
     assert _lib.skipped_pairs(DEV) == 0
+
+
+# ----------------------------------------------------------------------------
+# The bulk-copy-staged kernel (SB_INJECT_BULK_STAGED) against the direct path
+# ----------------------------------------------------------------------------
+@pytest.mark.parametrize("dtype,D,style,layout", [
+    (torch.bfloat16, 128, "neox", "canonical"), (torch.bfloat16, 96, "neox", "vllm"),
+    (torch.bfloat16, 16, "interleaved", "canonical"), (torch.float16, 64, "interleaved", "trtllm"),
+    (torch.float32, 128, "neox", "canonical"), (torch.float32, 96, "interleaved", "canonical"),
+])
+def test_bulk_staging_equals_direct_path(dtype, D, style, layout):
+    """Same bits as the direct path and within the bar of the oracle, with
+    out-of-range pairs (donor positions past the donor, targets past the
+    table) skipped and counted the same way; D = 96 leaves threads that own
+    no pair."""
+    donor, cache, bt, d, t = _case(11 + D, dtype, H=2, D=D, n_pairs=300, layout=layout)
+    d[::37] = donor.shape[2] + 5
+    t[5::41] = bt.shape[0] * 16 + 3
+    want = orope.rope_correct_scatter_paged(cache, donor, bt, d, t, 1e6, style, layout)
+    outs, skipped = [], []
+    for staging in ("direct", "bulk"):
+        c = cache.to(DEV)
+        _lib.skipped_pairs(DEV, reset=True)
+        rc.rope_correct_scatter_paged(c, donor.to(DEV), bt.to(DEV), d.to(DEV), t.to(DEV), rope_base=1e6,
+                                      rotary_style=style, layout=layout, staging=staging)
+        skipped.append(_lib.skipped_pairs(DEV))
+        outs.append(c.cpu())
+    assert torch.equal(outs[0].view(torch.uint8), outs[1].view(torch.uint8))
+    assert skipped[0] == skipped[1] > 0
+    _split_check(outs[1], want, layout, style)
+    _untouched_exact(outs[1], cache, bt, t, layout)
+
+
+def test_bulk_staging_many_requests_table():
+    """More than 64 requests (the device descriptor table) with chunk-shifted
+    pairs (long runs of contiguous donor rows) and several layers."""
+    g = torch.Generator().manual_seed(31)
+    L, H, D, bs, S = 3, 2, 128, 16, 512
+    n_req = 70
+    cache = torch.randn(L, n_req * (S // bs), 2, H, bs, D, generator=g).to(torch.bfloat16)
+    rng = np.random.default_rng(31)
+    injections, host = [], []
+    perm = rng.permutation(n_req * (S // bs)).astype(np.int32)
+    for r in range(n_req):
+        donor = torch.randn(L, 2, H, S, D, generator=g).to(torch.bfloat16)
+        shift = int(rng.integers(-128, 129))
+        tpos = np.arange(max(0, shift), min(S, S + shift)).astype(np.int32)
+        tpos = tpos[rng.random(tpos.shape[0]) > 0.1]
+        dpos = (tpos - shift).astype(np.int32)
+        bt = torch.from_numpy(perm[r * (S // bs):(r + 1) * (S // bs)].copy())
+        host.append((donor, bt, torch.from_numpy(dpos), torch.from_numpy(tpos)))
+    outs = []
+    for staging in ("direct", "bulk"):
+        c = cache.to(DEV)
+        inj = [rc.DonorInjection(dk.to(DEV), bt.to(DEV), dp.to(DEV), tp.to(DEV)) for dk, bt, dp, tp in host]
+        rc.inject_donors(c, inj, rope_base=1e6, rotary_style="neox", staging=staging)
+        outs.append(c.cpu())
+    assert torch.equal(outs[0].view(torch.uint8), outs[1].view(torch.uint8))
+    donor, bt, dp, tp = host[7]
+    for layer in range(L):
+        want = orope.rope_correct_scatter_paged(cache[layer], donor[layer], bt, dp, tp, 1e6, "neox")
+        rows = bt.long()
+        _split_check(outs[1][layer][rows], want[rows], style="neox")
+
+
+def test_c1_full_size_bulk_staging():
+    import bench
+
+    donor, cache, bt, d, t = bench.make_c1_inputs(bench.SEED + 1)
+    want = orope.rope_correct_scatter_paged(cache, donor, bt, d, t, 1e6, "neox")
+    c = cache.to(DEV)
+    rc.rope_correct_scatter_paged(c, donor.to(DEV), bt.to(DEV), d.to(DEV), t.to(DEV), rope_base=1e6,
+                                  rotary_style="neox", staging="bulk")
+    _split_check(c, want, style="neox")
+    _untouched_exact(c, cache, bt, t)
