@@ -36,6 +36,12 @@ namespace {
 #ifndef SB_INJECT_MIN_BLOCKS
 #define SB_INJECT_MIN_BLOCKS 4  // resident CTAs per SM the register budget targets
 #endif
+#ifndef SB_INJECT_TARGET_WAVES
+#define SB_INJECT_TARGET_WAVES 16  // waves of resident CTAs a large launch aims for
+#endif
+#ifndef SB_INJECT_MIN_ROWS
+#define SB_INJECT_MIN_ROWS 18  // rows per thread at least, in a launch of many pair tiles (swept: 8-18)
+#endif
 #ifndef SB_INJECT_UNROLL
 #define SB_INJECT_UNROLL 2  // rows in flight per thread
 #endif
@@ -173,6 +179,106 @@ __device__ __forceinline__ void rotate_vectors(Vec<T, VEC> &va, Vec<T, VEC> &vb,
   }
 }
 
+// The angles of each pair (the RoPE rotation's theta = m * inv_freq[f] for the
+// pair's position difference, constant or NoPE positions m).
+__device__ __forceinline__ void pair_angles(const sb_inject_params &P, int64_t sp, int64_t tp, float &m1,
+                                           float &m2) {
+  m2 = 0.f;
+  if (P.k_angle == SB_ANGLE_DELTA) {
+    m1 = (float)(tp - sp);
+  } else if (P.k_angle == SB_ANGLE_CONST) {
+    m1 = (float)P.const_delta;
+  } else {
+    m1 = (float)sp;
+    m2 = (float)tp;
+  }
+}
+
+// cos / sin of this thread's VEC frequency slots for its pair's angle(s),
+// computed once per tile for every run of consecutive pairs with the same
+// angles and read from a shared table: chunk-shifted donors give a 32-pair tile
+// one or two runs, so a CTA evaluates a few hundred double-precision sincos
+// instead of one set per thread (2,048 for a 256-thread CTA at VEC 8).
+// The kThreads threads that own the pair slots all call it: it synchronises
+// them with the block barrier, or with named barrier 1 when NAMED (the
+// bulk-staged kernel's consumers, whose producer warp runs on its own).
+// Threads whose pair is not valid get nothing written.
+template <bool NAMED>
+__device__ __forceinline__ void pair_slots_sync() {
+  if (NAMED)
+    asm volatile("bar.sync 1, %0;" ::"n"(kThreads) : "memory");
+  else
+    __syncthreads();
+}
+
+template <int VEC, bool NOPE, bool NAMED>
+__device__ __forceinline__ void tile_angles(const sb_inject_params &P, int ppt, int pl, int slice, bool ok,
+                                            float m1, float m2, float *c1, float *s1, float *c2, float *s2) {
+  constexpr int kA = NOPE ? 2 : 1;
+  __shared__ float key[kA][kThreads];
+  __shared__ uint8_t valid[kThreads];
+  __shared__ int16_t run_of[kThreads];
+  __shared__ float run_key[kA][kThreads];
+  __shared__ int warp_starts[kThreads / 32];
+  __shared__ float2 table[kA][kThreads * VEC];  // (cos, sin) per (run, frequency slot)
+  const int t = threadIdx.x;
+  if (slice == 0 && pl < ppt && t < kThreads) {
+    key[0][pl] = m1;
+    if (NOPE) key[kA - 1][pl] = m2;
+    valid[pl] = ok ? 1 : 0;
+  }
+  pair_slots_sync<NAMED>();
+  // run starts among the tile's valid pair slots, numbered by a block-wide count
+  bool start = false;
+  if (t < ppt && valid[t]) {
+    start = t == 0 || !valid[t - 1] || key[0][t] != key[0][t - 1] || (NOPE && key[kA - 1][t] != key[kA - 1][t - 1]);
+  }
+  const unsigned bal = __ballot_sync(0xffffffffu, start);
+  const int lane = t & 31, w = t >> 5;
+  if (lane == 0 && w < kThreads / 32) warp_starts[w] = __popc(bal);
+  pair_slots_sync<NAMED>();
+  int before = 0, n_runs = 0;
+#pragma unroll
+  for (int i = 0; i < kThreads / 32; ++i) {
+    before += i < w ? warp_starts[i] : 0;
+    n_runs += warp_starts[i];
+  }
+  const int upto = before + __popc(bal & (lane == 31 ? 0xffffffffu : ((2u << lane) - 1u)));
+  if (t < ppt) run_of[t] = (int16_t)(upto - 1);  // -1: an invalid slot before any valid one
+  if (start) {
+    run_key[0][upto - 1] = key[0][t];
+    if (NOPE) run_key[kA - 1][upto - 1] = key[kA - 1][t];
+  }
+  pair_slots_sync<NAMED>();
+  const int half = P.head_dim / 2;
+  for (int e = t; e < n_runs * half; e += kThreads) {
+    const int r = e / half, f = e - r * half;
+    const float inv = P.inv_freq[f];
+    float sv, cv;
+    sincos_f32(__fmul_rn(run_key[0][r], inv), sv, cv);
+    table[0][e] = make_float2(cv, sv);
+    if (NOPE) {
+      sincos_f32(__fmul_rn(run_key[kA - 1][r], inv), sv, cv);
+      table[kA - 1][e] = make_float2(cv, sv);
+    }
+  }
+  pair_slots_sync<NAMED>();
+  if (ok) {
+    const int base = run_of[pl] * half + slice * VEC;
+#pragma unroll
+    for (int e = 0; e < VEC; ++e) {
+      const float2 a = table[0][base + e];
+      c1[e] = a.x;
+      s1[e] = a.y;
+      if (NOPE) {
+        const float2 b = table[kA - 1][base + e];
+        c2[e % (NOPE ? VEC : 1)] = b.x;
+        s2[e % (NOPE ? VEC : 1)] = b.y;
+      }
+    }
+  }
+}
+
 template <typename T, int VEC, typename LT, bool NOPE>
 __global__ void __launch_bounds__(kThreads, SB_INJECT_MIN_BLOCKS)
     inject_kernel(const __grid_constant__ LT L) {
@@ -201,25 +307,25 @@ __global__ void __launch_bounds__(kThreads, SB_INJECT_MIN_BLOCKS)
     dp = &find_desc(L, tile, first);
   }
   const sb_inject_desc &d = *dp;
-  if (pl >= C.pairs_per_tile) return;
+  const sb_inject_params &P = C.p;
+  // no thread leaves before the angle table's barriers: threads past the tile's
+  // pairs, or past the descriptor's last pair, take part with no pair
   const int64_t pair = (tile - first) * C.pairs_per_tile + pl;
-  if (pair >= d.n_pairs) return;
-
-  const int64_t sp = load_index(d.src_pos, pair, d.pos_dtype);
-  const int64_t tp = load_index(d.dst_pos, pair, d.pos_dtype);
-  const int64_t srow =
-      d.src_row == SB_ROW_AT_PAIR ? pair : (d.src_row == SB_ROW_AT_DST_POS ? tp : sp);
-  const int64_t drow =
-      d.dst_row == SB_ROW_AT_PAIR ? pair : (d.dst_row == SB_ROW_AT_SRC_POS ? sp : tp);
-  int64_t soff = 0, doff = 0, chk = 0;
-  bool ok = resolve_row(d.src, srow, soff) && resolve_row(d.dst, drow, doff);
-  if (ok && (d.flags & SB_DESC_CHECK_SRC_IN_DST)) ok = resolve_row(d.dst, sp, chk);
-  if (!ok) {
-    if (blockIdx.y == 0 && slice == 0 && C.err != nullptr) atomicAdd(C.err, 1ull);
-    return;
+  const bool has_pair = pl < C.pairs_per_tile && pair < d.n_pairs;
+  int64_t sp = 0, tp = 0, soff = 0, doff = 0, chk = 0;
+  bool ok = false;
+  if (has_pair) {
+    sp = load_index(d.src_pos, pair, d.pos_dtype);
+    tp = load_index(d.dst_pos, pair, d.pos_dtype);
+    const int64_t srow =
+        d.src_row == SB_ROW_AT_PAIR ? pair : (d.src_row == SB_ROW_AT_DST_POS ? tp : sp);
+    const int64_t drow =
+        d.dst_row == SB_ROW_AT_PAIR ? pair : (d.dst_row == SB_ROW_AT_SRC_POS ? sp : tp);
+    ok = resolve_row(d.src, srow, soff) && resolve_row(d.dst, drow, doff);
+    if (ok && (d.flags & SB_DESC_CHECK_SRC_IN_DST)) ok = resolve_row(d.dst, sp, chk);
+    if (!ok && blockIdx.y == 0 && slice == 0 && C.err != nullptr) atomicAdd(C.err, 1ull);
   }
 
-  const sb_inject_params &P = C.p;
   const int D = P.head_dim;
   const bool neox = P.rotary_style == SB_ROTARY_NEOX;
   int oa, ob;
@@ -241,24 +347,12 @@ __global__ void __launch_bounds__(kThreads, SB_INJECT_MIN_BLOCKS)
   for (int e = 0; e < VEC; ++e) c1[e] = 1.f, s1[e] = 0.f;
 #pragma unroll
   for (int e = 0; e < (NOPE ? VEC : 1); ++e) c2[e] = 1.f, s2[e] = 0.f;
-  if (rot) {
-    float m1, m2 = 0.f;
-    if (P.k_angle == SB_ANGLE_DELTA) {
-      m1 = (float)(tp - sp);
-    } else if (P.k_angle == SB_ANGLE_CONST) {
-      m1 = (float)P.const_delta;
-    } else {
-      m1 = (float)sp;
-      m2 = (float)tp;
-    }
-    const int f0 = slice * VEC;
-#pragma unroll
-    for (int e = 0; e < VEC; ++e) {
-      const float f = P.inv_freq[f0 + e];
-      sincos_f32(__fmul_rn(m1, f), s1[e], c1[e]);
-      if (NOPE) sincos_f32(__fmul_rn(m2, f), s2[e], c2[e]);
-    }
+  if (rot) {  // uniform over the block
+    float m1 = 0.f, m2 = 0.f;
+    if (ok) pair_angles(P, sp, tp, m1, m2);
+    tile_angles<VEC, NOPE, false>(P, C.pairs_per_tile, pl, slice, ok, m1, m2, c1, s1, c2, s2);
   }
+  if (!ok) return;
 
   const int H = P.n_heads;
   // units are numbered (layer, kv, head) with the head fastest; n_units < 2^31
@@ -486,23 +580,10 @@ __global__ void __launch_bounds__(kBulkThreads, SB_INJECT_MIN_BLOCKS)
   for (int e = 0; e < VEC; ++e) c1[e] = 1.f, s1[e] = 0.f;
 #pragma unroll
   for (int e = 0; e < (NOPE ? VEC : 1); ++e) c2[e] = 1.f, s2[e] = 0.f;
-  if (rot && ok) {
-    float m1, m2 = 0.f;
-    if (P.k_angle == SB_ANGLE_DELTA) {
-      m1 = (float)(tp - sp);
-    } else if (P.k_angle == SB_ANGLE_CONST) {
-      m1 = (float)P.const_delta;
-    } else {
-      m1 = (float)sp;
-      m2 = (float)tp;
-    }
-    const int f0 = slice * VEC;
-#pragma unroll
-    for (int e = 0; e < VEC; ++e) {
-      const float f = P.inv_freq[f0 + e];
-      sincos_f32(__fmul_rn(m1, f), s1[e], c1[e]);
-      if (NOPE) sincos_f32(__fmul_rn(m2, f), s2[e], c2[e]);
-    }
+  if (rot) {  // the consumers' barriers of the table (the producer warp has left)
+    float m1 = 0.f, m2 = 0.f;
+    if (ok) pair_angles(P, sp, tp, m1, m2);
+    tile_angles<VEC, NOPE, true>(P, C.pairs_per_tile, pl, slice, ok, m1, m2, c1, s1, c2, s2);
   }
   int h = ua % H, kvi = (ua / H) % C.n_kv_sel, l = (ua / H) / C.n_kv_sel;
   bool stalled = false;
@@ -578,8 +659,15 @@ int pick_vec(const sb_inject_desc *descs, int n, int D, int es) {
 template <typename T, int VEC, typename LT>
 int launch_typed(const LT &L, dim3 grid, cudaStream_t st) {
   const bool nope = L.c.p.k_angle == SB_ANGLE_NOPE && (L.c.p.kv_select & SB_KV_K);
+  const bool bulk = (L.c.p.flags & SB_INJECT_BULK_STAGED) && VEC * (int)sizeof(T) == 16;
+  if (bulk) {
+    // the stage ring plus the static tables exceed 48 KB: opt in once per kernel and device
+    const void *fn = nope ? (const void *)inject_bulk_kernel<T, LT, true> : (const void *)inject_bulk_kernel<T, LT, false>;
+    const int s = ensure_dynamic_smem(fn, (int)kBulkDynSmem);
+    if (s != SB_OK) return s;
+  }
   const int slot = prof_before(st);
-  if ((L.c.p.flags & SB_INJECT_BULK_STAGED) && VEC * (int)sizeof(T) == 16) {
+  if (bulk) {
     if (nope)
       inject_bulk_kernel<T, LT, true><<<grid, kBulkThreads, kBulkDynSmem, st>>>(L);
     else
@@ -666,9 +754,9 @@ int plan_inject(const sb_inject_desc *descs, int n_desc, const sb_inject_params 
   const int64_t slots = (int64_t)sm_count() * SB_INJECT_MIN_BLOCKS;
   int64_t chunks;
   if (tiles >= 2 * slots) {
-    const int64_t target = (int64_t)sm_count() * (2048 / kThreads) * 16;
+    const int64_t target = (int64_t)sm_count() * (2048 / kThreads) * SB_INJECT_TARGET_WAVES;
     chunks = std::max<int64_t>(1, (target + tiles - 1) / tiles);
-    chunks = std::min<int64_t>(chunks, std::max<int64_t>(1, (C.n_units + 7) / 8));
+    chunks = std::min<int64_t>(chunks, std::max<int64_t>(1, C.n_units / SB_INJECT_MIN_ROWS));
   } else {
     chunks = std::max<int64_t>(1, slots / tiles);
     chunks = std::min<int64_t>(chunks, std::max<int64_t>(1, (C.n_units + kUnroll - 1) / kUnroll));

@@ -432,14 +432,25 @@ def inject_donors(
     per_layer = first if isinstance(kv_cache, (list, tuple)) else first[0]
     layout = _rows.resolve_layout(per_layer, layout)
     descs, keep = [], []
-    geom = None
+    geom = template = None
     for inj in injections:
         if inj.donor_positions.shape[0] == 0:
             continue
         bt = _rows.device_index_tensor(inj.block_table, dev, "block_table")
-        dst, g, k = _rows.paged_rows(kv_cache, bt, layout, has_layer_dim=not isinstance(kv_cache, (list, tuple)))
-        keep += k + [bt]
-        geom = g
+        if template is None:
+            # every request shares the cache: its geometry is read once, then each request's
+            # descriptor is the template with that request's block table
+            template, geom, k = _rows.paged_rows(kv_cache, bt, layout,
+                                                 has_layer_dim=not isinstance(kv_cache, (list, tuple)))
+            keep += k
+            dst = template
+        else:
+            dst = _lib.SbRows.from_buffer_copy(template)
+            dst.block_table = bt.data_ptr()
+            dst.n_logical = bt.shape[0]
+            dst.block_table_dtype = _lib.index_code(bt.dtype)
+        keep.append(bt)
+        g = geom
         n_layers, _, nh, _, hd = g
         dk = inj.donor_kv
         has_l = dk.ndim == 5
