@@ -255,7 +255,11 @@ SB_API int64_t sb_cosine_topk_workspace_bytes(int32_t n_queries, int64_t n_rows,
  * screening candidates kept per query.  *status (device int32, zeroed by the
  * caller) gets bit 0 set if some query had more than `capacity` candidates
  * (its results are withheld: retry with a larger capacity) and a value >= 2
- * if a kernel wait timed out.
+ * if a kernel wait timed out.  The screening kernel hands out its work units
+ * from a counter pair inside the library (one of 64 per device, taken round
+ * robin per call and reset by the call's last CTA): at most 64 calls may be in
+ * flight on one device at a time, and the first call on a device looks the
+ * counters up (make it before any stream capture).
  *
  * Replaces the cosine / threshold / top-k stage of DonorStore.find_donors
  * (semblend_core/donor_store.py:323-341) and DonorStore.find_donor (:205-229),

@@ -34,6 +34,8 @@
 // residuals plus the fp32 accumulation error); the row maxima come from
 // sb_search_prepare_rows.
 #include <algorithm>
+#include <atomic>
+#include <mutex>
 #include <cfloat>
 
 #include "common.cuh"
@@ -51,7 +53,10 @@ constexpr int kQBlockBytes = kBM * 128;
 constexpr int kEStageBytes = kBN * 128;
 constexpr int kThreads = 320;        // warp 0 TMA, warp 1 MMA, warps 2-9 epilogue
 constexpr int kMaxTilesPerChunk = 32;  // donor tiles per work unit (chosen per launch, <= this)
-constexpr int kMaxStages = 6;
+#ifndef SB_SCREEN_MAX_STAGES
+#define SB_SCREEN_MAX_STAGES 3  // 3 measured as fast as 4 (2 is 10 % slower); leaves ~34 KB of an SM for other kernels
+#endif
+constexpr int kMaxStages = SB_SCREEN_MAX_STAGES;
 constexpr int kSmemLimit = 232448;
 constexpr long long kWaitCycles = 2000000000LL;  // ~1 s at 1.9 GHz
 
@@ -74,7 +79,18 @@ struct ScreenParams {
   int *lower;
   int2 *cand;  // (row, screening score bits)
   int *status;
+  unsigned *sched;  // [next unit, CTAs finished] of this launch's scheduler slot
 };
+
+// Work units are handed out dynamically: each CTA's producer thread takes the
+// next unit index with an atomic add on a per-launch counter pair in device
+// memory, so a CTA whose SM was busy at launch (the sharded search's
+// all-gather of the previous batch runs beside this kernel) takes fewer units
+// instead of finishing last.  A launch uses one of kSchedSlots slots (round
+// robin on the host); the last CTA to finish resets it, so up to kSchedSlots
+// launches may be in flight on a device at once.
+constexpr int kSchedSlots = 64;
+__device__ unsigned g_screen_sched[kSchedSlots * 2];
 
 template <typename T> struct Half16;
 template <> struct Half16<__nv_bfloat16> {
@@ -188,6 +204,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t *final_bar = q_full + 6;
   uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(q_full + 7);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(q_full + 8);
+  uint64_t *unit_full = q_full + 9;        // [2] unit ring: producer -> MMA thread + epilogue warps
+  uint64_t *unit_empty = q_full + 11;      // [2]
+  volatile int64_t *unit_ring = reinterpret_cast<volatile int64_t *>(q_full + 13);  // [2]
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   if (threadIdx.x == 0) {
@@ -202,6 +221,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc::mbar_init(&acc_empty[0], 8);
     tc::mbar_init(&acc_empty[1], 8);
     tc::mbar_init(final_bar, 1);
+    for (int i = 0; i < 2; ++i) {
+      tc::mbar_init(&unit_full[i], 1);
+      tc::mbar_init(&unit_empty[i], 1 + 8);  // the MMA thread and the 8 epilogue warps
+    }
     *abort_flag = 0;
     tc::fence_mbar_init();
   }
@@ -215,15 +238,38 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = *tmem_holder;
   const tc::Abort ab{abort_flag, P.status};
   pdl_wait();  // query preparation (the previous kernel) has finished and is visible
+  // n-th unit of this CTA (-1: no more work).  A whole warp (epilogue) reads
+  // the slot before lane 0 releases it; the single MMA thread releases it itself.
+  auto pop_unit = [&](uint32_t n, bool whole_warp) -> int64_t {
+    if (!tc::mbar_wait(&unit_full[n & 1], (n >> 1) & 1, ab, 5, kWaitCycles)) return -1;
+    const int64_t u = unit_ring[n & 1];
+    if (whole_warp) __syncwarp();
+    if (!whole_warp || (threadIdx.x & 31) == 0) tc::mbar_arrive(&unit_empty[n & 1]);
+    return u;
+  };
 
   if (warp == 0) {
     if (lane == 0) {
       // ---------------- TMA producer ----------------
       tc::tma_prefetch_desc(&tmQ);
       tc::tma_prefetch_desc(&tmE);
-      uint32_t it = 0, qi = 0;
+      uint32_t it = 0, qi = 0, pushed = 0;
       bool ok = true;
-      for (int64_t u = blockIdx.x; u < P.n_units && ok; u += gridDim.x) {
+      auto push_unit = [&](int64_t u) -> bool {
+        const uint32_t slot = pushed & 1, use = pushed >> 1;
+        if (use > 0 && !tc::mbar_wait(&unit_empty[slot], (use - 1) & 1, ab, 2, kWaitCycles)) return false;
+        unit_ring[slot] = u;
+        tc::mbar_arrive(&unit_full[slot]);
+        ++pushed;
+        return true;
+      };
+      while (ok) {
+        const int64_t u = (int64_t)atomicAdd(P.sched, 1u);
+        if (u >= P.n_units) break;
+        if (!push_unit(u)) {
+          ok = false;
+          break;
+        }
         const int qt = (int)(u % P.n_qtiles);
         const int64_t t0 = (u / P.n_qtiles) * P.tiles_per_chunk;
         const int64_t t1 = min(t0 + P.tiles_per_chunk, P.n_ntiles);
@@ -245,6 +291,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
+      if (ok) push_unit(-1);
       // Let every load this thread issued land before the CTA can exit.
       const uint32_t n_out = it < (uint32_t)P.stages ? it : (uint32_t)P.stages;
       for (uint32_t i = it - n_out; i < it; ++i) {
@@ -266,7 +313,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t idesc = P.idesc;
       uint32_t it = 0, qi = 0, ai = 0;
       bool ok = true;
-      for (int64_t u = blockIdx.x; u < P.n_units && ok; u += gridDim.x) {
+      for (uint32_t n = 0; ok; ++n) {
+        const int64_t u = pop_unit(n, false);
+        if (u < 0) break;
         const int64_t t0 = (u / P.n_qtiles) * P.tiles_per_chunk;
         const int64_t t1 = min(t0 + P.tiles_per_chunk, P.n_ntiles);
         if (!tc::mbar_wait(q_full, qi & 1, ab, 3, kWaitCycles)) break;
@@ -318,7 +367,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int row = quarter * 32 + lane;
     uint32_t ai = 0;
     bool ok = true;
-    for (int64_t u = blockIdx.x; u < P.n_units && ok; u += gridDim.x) {
+    for (uint32_t n = 0; ok; ++n) {
+      const int64_t u = pop_unit(n, true);
+      if (u < 0) break;
       const int qt = (int)(u % P.n_qtiles);
       const int64_t t0 = (u / P.n_qtiles) * P.tiles_per_chunk;
       const int64_t t1 = min(t0 + P.tiles_per_chunk, P.n_ntiles);
@@ -442,6 +493,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc::fence_after_sync();
   if (warp == 1) tc::tmem_dealloc(tmem, 512);
+  if (threadIdx.x == 0) {
+    // every producer of this launch has stopped taking units once all CTAs got here
+    __threadfence();
+    if (atomicAdd(P.sched + 1, 1u) == gridDim.x - 1) {
+      P.sched[0] = 0;
+      P.sched[1] = 0;
+      __threadfence();
+    }
+  }
 }
 
 // Per query (one warp each): the exact k-th best screening score A_k over the
@@ -798,6 +858,33 @@ int sm_count() {
   return n > 0 ? n : 148;
 }
 
+// This launch's scheduler counter pair on the current device (the symbol's
+// address is looked up once per device, with that device current).
+unsigned *screen_sched_slot() {
+  static std::mutex mu;
+  static unsigned *base[64] = {};
+  static std::atomic<unsigned> next{0};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess || dev < 0 || dev >= 64) {
+    set_last_cuda_error(e);
+    return nullptr;
+  }
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (base[dev] == nullptr) {
+      void *p = nullptr;
+      e = cudaGetSymbolAddress(&p, g_screen_sched);
+      if (e != cudaSuccess || p == nullptr) {
+        set_last_cuda_error(e);
+        return nullptr;
+      }
+      base[dev] = static_cast<unsigned *>(p);
+    }
+  }
+  return base[dev] + 2 * (next.fetch_add(1) % kSchedSlots);
+}
+
 template <int KT>
 int launch_screen(const CUtensorMap &tq, const CUtensorMap &te, const ScreenParams &P, int grid, int smem,
                   cudaStream_t st) {
@@ -926,6 +1013,8 @@ extern "C" SB_API int sb_cosine_topk(const float *emb, int64_t ld_emb, const voi
   if (P.stages < 2) return SB_ERR_UNSUPPORTED;
   const int smem = fixed + P.stages * kEStageBytes;
   const int grid = (int)std::min<int64_t>(sm_count(), P.n_units);
+  P.sched = screen_sched_slot();
+  if (P.sched == nullptr) return SB_ERR_CUDA;
   int s;
   if (k <= 8)
     s = launch_screen<8>(tq, te, P, grid, smem, st);

@@ -22,6 +22,21 @@ from ._lib import NativeLibraryError
 from .search import DEFAULT_CAPACITY, DeviceDonorMatrix, cosine_topk_async, merge_topk
 
 
+def _exchange_group(group, cta_policy: int):
+    """A new NCCL group over the ranks of ``group`` with the given CTA policy
+    (collective: every rank of ``group`` calls it).  Falls back to ``group``
+    when this torch build has no communicator options."""
+    try:
+        from torch.distributed import ProcessGroupNCCL
+
+        opts = ProcessGroupNCCL.Options()
+        opts.config.cta_policy = int(cta_policy)
+    except (ImportError, AttributeError):
+        return group
+    ranks = dist.get_process_group_ranks(group) if group is not None else list(range(dist.get_world_size()))
+    return dist.new_group(ranks=ranks, backend="nccl", pg_options=opts)
+
+
 def shard_bounds(n_rows: int, world: int) -> list[tuple[int, int]]:
     """Contiguous, near-equal row ranges ``[(begin, end)]`` for each rank."""
     return [(r * n_rows // world, (r + 1) * n_rows // world) for r in range(world)]
@@ -39,10 +54,16 @@ class ShardedDonorMatrix:
     """
 
     def __init__(self, n_rows: int, dim: int, group=None, device=None, shadow_dtype=torch.float16,
-                 local_search: Callable | None = None, merge: Callable | None = None):
+                 local_search: Callable | None = None, merge: Callable | None = None,
+                 exchange_cta_policy: int | None = 1):
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
+        if (exchange_cta_policy is not None and self.world > 1 and local_search is None
+                and dist.get_backend(group) == "nccl"):
+            # the exchange gets a communicator of its own whose kernels take as few SMs as NCCL
+            # allows (its CTA policy), so they fit beside the next batch's screening kernel
+            self.group = _exchange_group(group, exchange_cta_policy)
         self.n_rows = int(n_rows)
         self.dim = int(dim)
         self.row_begin, self.row_end = shard_bounds(self.n_rows, self.world)[self.rank]
@@ -115,17 +136,50 @@ class ShardedDonorMatrix:
         ids, scores = self._merge(all_ids, all_sc)
         return ids, scores, status
 
+    def _pipeline(self, nq: int, k: int, min_similarity: float, capacity: int):
+        """Buffers of the two in-flight slots of :meth:`search_batches` for one
+        batch shape, kept across calls: the query input, the send record
+        (ids, similarities, status) and the receive table of each slot."""
+        key = (nq, k)
+        cache = self.__dict__.setdefault("_pipes", {})
+        st = cache.get(key)
+        if st is None:
+            dev = self.local.device
+            rec = self._record_bytes(nq, k)
+            st = {"q": [torch.empty(nq, self.dim, dtype=torch.float32, device=dev) for _ in range(2)],
+                  "send": [torch.empty(rec, dtype=torch.uint8, device=dev) for _ in range(2)],
+                  "recv": [torch.empty(self.world * rec, dtype=torch.uint8, device=dev) for _ in range(2)],
+                  "rec": rec}
+            cache[key] = st
+        return st
+
+    def _views(self, send: torch.Tensor, nq: int, k: int):
+        qk = nq * k
+        return (send[: 8 * qk].view(torch.int64).view(nq, k), send[8 * qk : 12 * qk].view(torch.float32).view(nq, k),
+                send[12 * qk : 12 * qk + 4].view(torch.int32))
+
+    def _shard_search(self, q: torch.Tensor, send: torch.Tensor, k: int, min_similarity: float,
+                      capacity: int) -> None:
+        """The shard's search of ``q`` into a send record."""
+        m = self.local
+        ids_v, sc_v, st_v = self._views(send, q.shape[0], k)
+        cosine_topk_async(m.emb, m.emb16, m.valid, m.stats, q, k, min_similarity, n_rows=self.n_local,
+                          id_offset=self.row_begin, capacity=capacity, status=st_v, workspace_owner=m,
+                          out=(ids_v, sc_v))
+
     def search_batches(self, batches, k: int, min_similarity: float, capacity: int = DEFAULT_CAPACITY,
                        on_result=None) -> list[tuple[torch.Tensor, torch.Tensor, torch.Tensor]]:
         """Search a sequence of query batches with two in flight, without a
         host synchronisation: batch i's all-gather and merge run on a second
-        stream while batch i+1 is searched on the current one (the exchange
-        needs few SMs and hides behind the screening kernel).  Returns
+        stream while batch i+1 is searched on the current one.  Returns
         ``(ids, scores, status [W])`` per batch, ready on the current stream.
         ``on_result(i, ids, scores)``, if given, is called on the exchange
         stream right after batch i is merged (e.g. to queue its copy to the
         host).  Batches in pinned host memory are copied to the device on a
-        third stream, each copy overlapping the previous batch's search.
+        third stream, each copy overlapping the previous batch's search.  The
+        slots' buffers are kept across calls for each batch shape: keep such
+        calls on one stream of the device (two calls of one shape must not run
+        concurrently).
         """
         batches = list(batches)
         if self.world == 1 or self._local_search is not None:
@@ -136,6 +190,8 @@ class ShardedDonorMatrix:
                     on_result(i, r[0], r[1])
                 out.append(r)
             return out
+        if not batches:
+            return []
         m = self.local
         dev = m.device
         cur = torch.cuda.current_stream(dev)
@@ -143,16 +199,22 @@ class ShardedDonorMatrix:
             self._xstream = torch.cuda.Stream(dev)
         xs = self._xstream
         kk = int(k)
+        nq = batches[0].shape[0]
+        if any(b.shape != batches[0].shape for b in batches):
+            raise ValueError("search_batches needs batches of one shape")
+        st = self._pipeline(nq, kk, min_similarity, capacity)
+        rec, qk = st["rec"], nq * kk
+        ready = [torch.cuda.Event() for _ in range(2)]
+        done = [torch.cuda.Event() for _ in range(2)]
         results = []
-        sends, recvs, ready, done = [], [], [], []
-        # host batches: copied on a copy stream into two device buffers, each copy
+        # host batches: copied on a copy stream straight into the slots' query buffers, each copy
         # overlapping the previous batch's search
-        host = batches and batches[0].device.type == "cpu"
+        host = batches[0].device.type == "cpu"
         if host:
             if getattr(self, "_cstream", None) is None:
                 self._cstream = torch.cuda.Stream(dev)
             cs = self._cstream
-            qbufs = [torch.empty(batches[0].shape, dtype=torch.float32, device=dev) for _ in range(2)]
+            cs.wait_stream(cur)  # the slots' buffers may still be read by work queued earlier
             copied = [torch.cuda.Event() for _ in range(2)]
             consumed = [torch.cuda.Event() for _ in range(2)]
 
@@ -160,43 +222,30 @@ class ShardedDonorMatrix:
                 with torch.cuda.stream(cs):
                     if j >= 2:
                         cs.wait_event(consumed[j % 2])
-                    qbufs[j % 2].copy_(batches[j], non_blocking=True)
+                    st["q"][j % 2].copy_(batches[j], non_blocking=True)
                     copied[j % 2].record(cs)
 
             stage(0)
         for i, q in enumerate(batches):
+            slot = i % 2
+            if i >= 2:
+                cur.wait_event(done[slot])  # the exchange of batch i - 2 has read this slot
             if host:
                 if i + 1 < len(batches):
                     stage(i + 1)
-                cur.wait_event(copied[i % 2])
-                q = qbufs[i % 2]
-            nq = q.shape[0]
-            qk, rec = nq * kk, self._record_bytes(nq, kk)
-            slot = i % 2
-            if len(sends) <= slot:
-                sends.append(torch.empty(rec, dtype=torch.uint8, device=dev))
-                recvs.append(torch.empty(self.world * rec, dtype=torch.uint8, device=dev))
-                ready.append(torch.cuda.Event())
-                done.append(torch.cuda.Event())
-            send, recv = sends[slot], recvs[slot]
-            if send.numel() < rec:
-                raise ValueError("search_batches needs batches of one shape")
-            if i >= 2:
-                cur.wait_event(done[slot])  # the exchange of batch i - 2 has read this slot
-            ids_v = send[: 8 * qk].view(torch.int64).view(nq, kk)
-            sc_v = send[8 * qk : 12 * qk].view(torch.float32).view(nq, kk)
-            st_v = send[12 * qk : 12 * qk + 4].view(torch.int32)
-            qd = q.to(device=dev, dtype=torch.float32).contiguous()
-            cosine_topk_async(m.emb, m.emb16, m.valid, m.stats, qd, kk, min_similarity, n_rows=self.n_local,
-                              id_offset=self.row_begin, capacity=capacity, status=st_v, workspace_owner=m,
-                              out=(ids_v, sc_v))
+                cur.wait_event(copied[slot])
+                q = st["q"][slot]
+            else:
+                q = q.to(device=dev, dtype=torch.float32).contiguous()
+            self._shard_search(q, st["send"][slot], kk, min_similarity, capacity)
             if host:
-                consumed[i % 2].record(cur)
+                consumed[slot].record(cur)
             ready[slot].record(cur)
+            send, recv = st["send"][slot], st["recv"][slot]
             with torch.cuda.stream(xs):
                 xs.wait_event(ready[slot])
-                dist.all_gather_into_tensor(recv[: self.world * rec], send[:rec], group=self.group)
-                table = recv[: self.world * rec].view(self.world, rec)
+                dist.all_gather_into_tensor(recv, send, group=self.group)
+                table = recv.view(self.world, rec)
                 ids, scores = self._merge(table[:, : 8 * qk].view(torch.int64).view(self.world, nq, kk),
                                           table[:, 8 * qk : 12 * qk].view(torch.float32).view(self.world, nq, kk))
                 status = table[:, 12 * qk : 12 * qk + 4].view(torch.int32).reshape(self.world).clone()

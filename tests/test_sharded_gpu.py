@@ -49,9 +49,12 @@ def _worker(rank, world, port, path):
         m = ShardedDonorMatrix(E.shape[0], E.shape[1], device=dev)
         m.write_range(0, E)
         ids, sc = m.search(Q, 8, 0.6)
-        res = m.search_batches([Q, Q, Q], 8, 0.6)
-        hq = Q.cpu().pin_memory()
-        res_h = m.search_batches([hq, hq, hq], 8, 0.6)
+        # batches alternate two query sets (the second reversed): the replayed shard search must take
+        # each batch's own queries
+        Qr = Q.flip(0).contiguous()
+        res = m.search_batches([Q, Qr, Q], 8, 0.6)
+        hq, hqr = Q.cpu().pin_memory(), Qr.cpu().pin_memory()
+        res_h = m.search_batches([hqr, hq, hqr, hq], 8, 0.6)
         torch.cuda.synchronize(dev)
         out = {"ids": ids.cpu(), "scores": sc.cpu(),
                "batched": [(a.cpu(), b.cpu(), c.cpu()) for a, b, c in res + res_h]}
@@ -88,6 +91,9 @@ def test_two_gpu_sharded_search_equals_single_search(tmp_path):
     full.write_range(0, E)
     want_i, want_s = full.search(Q, 8, 0.6)
     assert torch.equal(res["ids"], want_i.cpu()) and torch.equal(res["scores"], want_s.cpu())
-    for ids, sc, st in res["batched"]:
-        assert torch.equal(ids, want_i.cpu()) and torch.equal(sc, want_s.cpu())
+    wi, ws = want_i.cpu(), want_s.cpu()
+    order = [False, True, False, True, False, True, False]  # reversed query sets in res + res_h
+    assert len(res["batched"]) == len(order)
+    for (ids, sc, st), rev in zip(res["batched"], order):
+        assert torch.equal(ids, wi.flip(0) if rev else wi) and torch.equal(sc, ws.flip(0) if rev else ws)
         assert int(st.abs().sum()) == 0
