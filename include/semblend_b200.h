@@ -272,6 +272,27 @@ SB_API int sb_cosine_topk(const float *emb, int64_t ld_emb, const void *emb16, i
                           int32_t capacity, void *workspace, int64_t workspace_bytes,
                           int32_t *status, void *stream);
 
+/* sb_cosine_topk in two phases, so a pipeline of query batches can rescore
+ * one batch on a second stream while the next batch is screened.
+ * sb_cosine_screen runs query preparation and the tensor-core screening into
+ * the workspace; sb_cosine_rescore then rescores the workspace's candidates
+ * exactly and writes out_ids / out_scores.  Both take the arguments of
+ * sb_cosine_topk that they use, with the same meaning; the rescore must see
+ * the screen's writes to the workspace and to *status (same stream, or an
+ * event between the two streams), and the workspace must not be reused
+ * before the rescore has finished.  Screen then rescore equals one
+ * sb_cosine_topk call with the same arguments.  (No reference counterpart:
+ * the reference searches one query at a time.) */
+SB_API int sb_cosine_screen(const void *emb16, int64_t ld_16, int32_t shadow_dtype,
+                            const uint8_t *valid, int64_t n_rows, int32_t dim, int32_t dim_pad,
+                            const float *stats, const float *queries, int64_t ld_q,
+                            int32_t n_queries, int32_t k, float min_similarity, int32_t capacity,
+                            void *workspace, int64_t workspace_bytes, int32_t *status, void *stream);
+SB_API int sb_cosine_rescore(const float *emb, int64_t ld_emb, int64_t n_rows, int32_t dim,
+                             int32_t dim_pad, int32_t n_queries, int32_t k, float min_similarity,
+                             int64_t id_offset, int64_t *out_ids, float *out_scores, int32_t capacity,
+                             void *workspace, int64_t workspace_bytes, int32_t *status, void *stream);
+
 /* Merge n_lists (<= 16) per-query sorted top-k lists into one
  * [n_queries][k] by (score desc, id asc); ids < 0 are empty.  List l is
  * [n_queries][k] at ids + l * ids_list_stride (elements; >= n_queries * k)

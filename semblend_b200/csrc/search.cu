@@ -927,34 +927,30 @@ extern "C" SB_API int64_t sb_cosine_topk_workspace_bytes(int32_t n_queries, int6
   return sb::carve(nullptr, n_queries, dim, dim_pad, capacity, n_rows).bytes;
 }
 
-extern "C" SB_API int sb_cosine_topk(const float *emb, int64_t ld_emb, const void *emb16, int64_t ld_16,
-                                     int32_t shadow_dtype, const uint8_t *valid, int64_t n_rows, int32_t dim,
-                                     int32_t dim_pad, const float *stats, const float *queries, int64_t ld_q,
-                                     int32_t n_queries, int32_t k, float min_similarity, int64_t id_offset,
-                                     int64_t *out_ids, float *out_scores, int32_t capacity, void *workspace,
-                                     int64_t workspace_bytes, int32_t *status, void *stream) {
-  using namespace sb;
-  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+namespace sb {
+namespace {
+
+// Argument checks shared by the screening and rescoring phases.
+int check_topk_args(int64_t ld_emb, int64_t n_rows, int32_t dim, int32_t dim_pad, int32_t n_queries, int32_t k,
+                    int32_t capacity, const int64_t *out_ids, const float *out_scores, const int32_t *status) {
   if (n_queries < 0 || n_rows < 0 || k < 1 || k > 32 || dim <= 0) return SB_ERR_INVALID_ARGUMENT;
   if (dim_pad < dim || dim_pad % kBK != 0 || dim_pad > 512) return SB_ERR_UNSUPPORTED;
-  if (shadow_dtype != SB_DTYPE_F16 && shadow_dtype != SB_DTYPE_BF16) return SB_ERR_UNSUPPORTED;
   if (capacity < k || capacity > 16384) return SB_ERR_INVALID_ARGUMENT;
   if (n_rows > 0x7fffffffLL) return SB_ERR_TOO_LARGE;
   if (n_queries == 0) return SB_OK;
-  if (queries == nullptr || out_ids == nullptr || out_scores == nullptr || status == nullptr || stats == nullptr)
+  if (ld_emb < dim || status == nullptr || (out_ids == nullptr) != (out_scores == nullptr))
     return SB_ERR_INVALID_ARGUMENT;
-  if (ld_q < dim || ld_emb < dim || ld_16 < dim_pad) return SB_ERR_INVALID_ARGUMENT;
-  if ((reinterpret_cast<uintptr_t>(emb16) % 16) || ((ld_16 * 2) % 16)) return SB_ERR_INVALID_ARGUMENT;
-  Workspace w = carve(workspace, n_queries, dim, dim_pad, capacity, n_rows);
-  if (workspace == nullptr || workspace_bytes < w.bytes) return SB_ERR_WORKSPACE_TOO_SMALL;
-  if (n_rows == 0) {
-    const int64_t n = (int64_t)n_queries * k;
-    fill_empty_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(out_ids, out_scores, n);
-    return launch_status();
-  }
-  if (emb == nullptr || emb16 == nullptr) return SB_ERR_INVALID_ARGUMENT;
-  const bool f16 = shadow_dtype == SB_DTYPE_F16;
+  return SB_OK;
+}
 
+// Query preparation and the tensor-core screening kernel: each query's
+// candidates with their screening scores and its error bound, into the
+// workspace.
+int cosine_screen(const void *emb16, int64_t ld_16, int32_t shadow_dtype, const uint8_t *valid, int64_t n_rows,
+                  int32_t dim, int32_t dim_pad, const float *stats, const float *queries, int64_t ld_q,
+                  int32_t n_queries, int32_t k, float min_similarity, int32_t capacity, const Workspace &w,
+                  int32_t *status, cudaStream_t st) {
+  const bool f16 = shadow_dtype == SB_DTYPE_F16;
   const int64_t n_words = (n_rows + 31) / 32;
   {
     const int threads = 256;
@@ -1022,13 +1018,88 @@ extern "C" SB_API int sb_cosine_topk(const float *emb, int64_t ld_emb, const voi
     s = launch_screen<16>(tq, te, P, grid, smem, st);
   else
     s = launch_screen<32>(tq, te, P, grid, smem, st);
-  if (s != SB_OK) return s;
+  return s;
+}
 
+// Exact rescoring of the screened candidates and top-k selection.
+int cosine_rescore(const float *emb, int64_t ld_emb, int64_t n_rows, int32_t dim, int32_t n_queries, int32_t k,
+                   float min_similarity, int64_t id_offset, int64_t *out_ids, float *out_scores, int32_t capacity,
+                   const Workspace &w, int32_t *status, cudaStream_t st) {
+  if (n_rows == 0) {
+    const int64_t n = (int64_t)n_queries * k;
+    fill_empty_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(out_ids, out_scores, n);
+    return launch_status();
+  }
   const unsigned rs_grid = (unsigned)((n_queries + kRescoreWarps - 1) / kRescoreWarps);
   const int kt = k <= 8 ? 8 : (k <= 16 ? 16 : 32);
   launch_rescore(kt, rs_grid, st, emb, ld_emb, dim, w.qn, w.delta, w.count, w.cand, capacity, min_similarity, k,
                  n_queries, id_offset, out_ids, out_scores, status);
   return launch_status();
+}
+
+}  // namespace
+}  // namespace sb
+
+extern "C" SB_API int sb_cosine_screen(const void *emb16, int64_t ld_16, int32_t shadow_dtype, const uint8_t *valid,
+                                       int64_t n_rows, int32_t dim, int32_t dim_pad, const float *stats,
+                                       const float *queries, int64_t ld_q, int32_t n_queries, int32_t k,
+                                       float min_similarity, int32_t capacity, void *workspace,
+                                       int64_t workspace_bytes, int32_t *status, void *stream) {
+  using namespace sb;
+  int s = check_topk_args(dim, n_rows, dim, dim_pad, n_queries, k, capacity, nullptr, nullptr, status);
+  if (s != SB_OK) return s;
+  if (shadow_dtype != SB_DTYPE_F16 && shadow_dtype != SB_DTYPE_BF16) return SB_ERR_UNSUPPORTED;
+  if (n_queries == 0 || n_rows == 0) return SB_OK;
+  if (queries == nullptr || stats == nullptr || emb16 == nullptr) return SB_ERR_INVALID_ARGUMENT;
+  if (ld_q < dim || ld_16 < dim_pad) return SB_ERR_INVALID_ARGUMENT;
+  if ((reinterpret_cast<uintptr_t>(emb16) % 16) || ((ld_16 * 2) % 16)) return SB_ERR_INVALID_ARGUMENT;
+  const Workspace w = carve(workspace, n_queries, dim, dim_pad, capacity, n_rows);
+  if (workspace == nullptr || workspace_bytes < w.bytes) return SB_ERR_WORKSPACE_TOO_SMALL;
+  return cosine_screen(emb16, ld_16, shadow_dtype, valid, n_rows, dim, dim_pad, stats, queries, ld_q, n_queries, k,
+                       min_similarity, capacity, w, status, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" SB_API int sb_cosine_rescore(const float *emb, int64_t ld_emb, int64_t n_rows, int32_t dim,
+                                        int32_t dim_pad, int32_t n_queries, int32_t k, float min_similarity,
+                                        int64_t id_offset, int64_t *out_ids, float *out_scores, int32_t capacity,
+                                        void *workspace, int64_t workspace_bytes, int32_t *status, void *stream) {
+  using namespace sb;
+  int s = check_topk_args(ld_emb, n_rows, dim, dim_pad, n_queries, k, capacity, out_ids, out_scores, status);
+  if (s != SB_OK) return s;
+  if (n_queries == 0) return SB_OK;
+  if (out_ids == nullptr) return SB_ERR_INVALID_ARGUMENT;
+  const Workspace w = carve(workspace, n_queries, dim, dim_pad, capacity, n_rows);
+  if (n_rows > 0 && (emb == nullptr || workspace == nullptr || workspace_bytes < w.bytes))
+    return emb == nullptr ? SB_ERR_INVALID_ARGUMENT : SB_ERR_WORKSPACE_TOO_SMALL;
+  return cosine_rescore(emb, ld_emb, n_rows, dim, n_queries, k, min_similarity, id_offset, out_ids, out_scores,
+                        capacity, w, status, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" SB_API int sb_cosine_topk(const float *emb, int64_t ld_emb, const void *emb16, int64_t ld_16,
+                                     int32_t shadow_dtype, const uint8_t *valid, int64_t n_rows, int32_t dim,
+                                     int32_t dim_pad, const float *stats, const float *queries, int64_t ld_q,
+                                     int32_t n_queries, int32_t k, float min_similarity, int64_t id_offset,
+                                     int64_t *out_ids, float *out_scores, int32_t capacity, void *workspace,
+                                     int64_t workspace_bytes, int32_t *status, void *stream) {
+  using namespace sb;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  int s = check_topk_args(ld_emb, n_rows, dim, dim_pad, n_queries, k, capacity, out_ids, out_scores, status);
+  if (s != SB_OK) return s;
+  if (shadow_dtype != SB_DTYPE_F16 && shadow_dtype != SB_DTYPE_BF16) return SB_ERR_UNSUPPORTED;
+  if (n_queries == 0) return SB_OK;
+  if (queries == nullptr || out_ids == nullptr || stats == nullptr) return SB_ERR_INVALID_ARGUMENT;
+  if (ld_q < dim || ld_16 < dim_pad) return SB_ERR_INVALID_ARGUMENT;
+  if ((reinterpret_cast<uintptr_t>(emb16) % 16) || ((ld_16 * 2) % 16)) return SB_ERR_INVALID_ARGUMENT;
+  const Workspace w = carve(workspace, n_queries, dim, dim_pad, capacity, n_rows);
+  if (workspace == nullptr || workspace_bytes < w.bytes) return SB_ERR_WORKSPACE_TOO_SMALL;
+  if (n_rows > 0) {
+    if (emb == nullptr || emb16 == nullptr) return SB_ERR_INVALID_ARGUMENT;
+    s = cosine_screen(emb16, ld_16, shadow_dtype, valid, n_rows, dim, dim_pad, stats, queries, ld_q, n_queries, k,
+                      min_similarity, capacity, w, status, st);
+    if (s != SB_OK) return s;
+  }
+  return cosine_rescore(emb, ld_emb, n_rows, dim, n_queries, k, min_similarity, id_offset, out_ids, out_scores,
+                        capacity, w, status, st);
 }
 
 extern "C" SB_API int sb_topk_merge(const int64_t *ids, int64_t ids_list_stride, const float *scores,

@@ -175,12 +175,19 @@ def cosine_topk_async(emb: torch.Tensor, emb16: torch.Tensor, valid: torch.Tenso
                       stats: torch.Tensor, queries: torch.Tensor, k: int, min_similarity: float, *,
                       n_rows: int | None = None, id_offset: int = 0, capacity: int = DEFAULT_CAPACITY,
                       status: torch.Tensor | None = None, workspace_owner=None,
-                      out: tuple[torch.Tensor, torch.Tensor] | None = None):
+                      out: tuple[torch.Tensor, torch.Tensor] | None = None,
+                      rescore_stream: torch.cuda.Stream | None = None):
     """One search attempt, enqueued without synchronising.
 
     Returns ``(ids, scores, status)``; ``status`` (device int32) must be read
     before the results are trusted: bit 0 = a query overflowed ``capacity``
     (retry larger), values >= 2 = a kernel wait timed out.
+
+    With ``rescore_stream``, the screening runs on the current stream and the
+    exact rescoring on ``rescore_stream`` after it (``sb_cosine_screen`` then
+    ``sb_cosine_rescore``): the results are ready on ``rescore_stream``, and the
+    workspace of ``workspace_owner`` stays in use until that stream has
+    finished the rescore, so the caller orders the next use of it.
     """
     for t, name in ((emb, "emb"), (emb16, "emb16"), (queries, "queries"), (stats, "stats")):
         _lib.require_cuda(t, name)
@@ -209,16 +216,37 @@ def cosine_topk_async(emb: torch.Tensor, emb16: torch.Tensor, valid: torch.Tenso
     cap = max(int(capacity), k)
     nbytes = lib.sb_cosine_topk_workspace_bytes(nq, n_rows, dim, dim_pad, cap)
     ws = _workspace(workspace_owner, nbytes, dev)
+    if rescore_stream is None:
+        _lib.check(
+            lib.sb_cosine_topk(
+                emb.data_ptr(), ld_e, emb16.data_ptr(), ld_b, _lib.dtype_code(emb16.dtype),
+                valid.data_ptr() if valid is not None else None, n_rows, dim, dim_pad, stats.data_ptr(),
+                queries.data_ptr(), ld_q, nq, k, float(min_similarity), int(id_offset),
+                ids.data_ptr(), scores.data_ptr(), cap, ws.data_ptr(), ws.numel(), status.data_ptr(),
+                _lib.stream_ptr(dev),
+            ),
+            "sb_cosine_topk",
+        )
+        return ids, scores, status
     _lib.check(
-        lib.sb_cosine_topk(
-            emb.data_ptr(), ld_e, emb16.data_ptr(), ld_b, _lib.dtype_code(emb16.dtype),
-            valid.data_ptr() if valid is not None else None, n_rows, dim, dim_pad, stats.data_ptr(),
-            queries.data_ptr(), ld_q, nq, k, float(min_similarity), int(id_offset),
-            ids.data_ptr(), scores.data_ptr(), cap, ws.data_ptr(), ws.numel(), status.data_ptr(),
-            _lib.stream_ptr(dev),
+        lib.sb_cosine_screen(
+            emb16.data_ptr(), ld_b, _lib.dtype_code(emb16.dtype), valid.data_ptr() if valid is not None else None,
+            n_rows, dim, dim_pad, stats.data_ptr(), queries.data_ptr(), ld_q, nq, k, float(min_similarity), cap,
+            ws.data_ptr(), ws.numel(), status.data_ptr(), _lib.stream_ptr(dev),
         ),
-        "sb_cosine_topk",
+        "sb_cosine_screen",
     )
+    rescore_stream.wait_stream(torch.cuda.current_stream(dev))
+    _lib.check(
+        lib.sb_cosine_rescore(
+            emb.data_ptr(), ld_e, n_rows, dim, dim_pad, nq, k, float(min_similarity), int(id_offset),
+            ids.data_ptr(), scores.data_ptr(), cap, ws.data_ptr(), ws.numel(), status.data_ptr(),
+            rescore_stream.cuda_stream,
+        ),
+        "sb_cosine_rescore",
+    )
+    for t in (ids, scores, status, ws):  # allocated on the current stream, used on the rescore stream
+        t.record_stream(rescore_stream)
     return ids, scores, status
 
 

@@ -22,6 +22,10 @@ from ._lib import NativeLibraryError
 from .search import DEFAULT_CAPACITY, DeviceDonorMatrix, cosine_topk_async, merge_topk
 
 
+class _Workspace:
+    """Holder of one pipeline slot's search workspace (``_ws``)."""
+
+
 def _exchange_group(group, cta_policy: int):
     """A new NCCL group over the ranks of ``group`` with the given CTA policy
     (collective: every rank of ``group`` calls it).  Falls back to ``group``
@@ -55,8 +59,11 @@ class ShardedDonorMatrix:
 
     def __init__(self, n_rows: int, dim: int, group=None, device=None, shadow_dtype=torch.float16,
                  local_search: Callable | None = None, merge: Callable | None = None,
-                 exchange_cta_policy: int | None = 1):
+                 exchange_cta_policy: int | None = 1, overlap_rescore: bool = True):
         self.group = group
+        # search_batches: batch i's exact rescoring runs on the exchange stream, beside batch
+        # i+1's screening (each slot has its own workspace); False keeps it on the current stream
+        self.overlap_rescore = bool(overlap_rescore)
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
         if (exchange_cta_policy is not None and self.world > 1 and local_search is None
@@ -147,6 +154,7 @@ class ShardedDonorMatrix:
             dev = self.local.device
             rec = self._record_bytes(nq, k)
             st = {"q": [torch.empty(nq, self.dim, dtype=torch.float32, device=dev) for _ in range(2)],
+                  "ws": [_Workspace() for _ in range(2)],
                   "send": [torch.empty(rec, dtype=torch.uint8, device=dev) for _ in range(2)],
                   "recv": [torch.empty(self.world * rec, dtype=torch.uint8, device=dev) for _ in range(2)],
                   "rec": rec}
@@ -159,19 +167,21 @@ class ShardedDonorMatrix:
                 send[12 * qk : 12 * qk + 4].view(torch.int32))
 
     def _shard_search(self, q: torch.Tensor, send: torch.Tensor, k: int, min_similarity: float,
-                      capacity: int) -> None:
-        """The shard's search of ``q`` into a send record."""
+                      capacity: int, rescore_stream=None, workspace_owner=None) -> None:
+        """The shard's search of ``q`` into a send record (the rescoring on
+        ``rescore_stream`` when given, with ``workspace_owner``'s workspace)."""
         m = self.local
         ids_v, sc_v, st_v = self._views(send, q.shape[0], k)
         cosine_topk_async(m.emb, m.emb16, m.valid, m.stats, q, k, min_similarity, n_rows=self.n_local,
-                          id_offset=self.row_begin, capacity=capacity, status=st_v, workspace_owner=m,
-                          out=(ids_v, sc_v))
+                          id_offset=self.row_begin, capacity=capacity, status=st_v,
+                          workspace_owner=workspace_owner if workspace_owner is not None else m,
+                          out=(ids_v, sc_v), rescore_stream=rescore_stream)
 
     def search_batches(self, batches, k: int, min_similarity: float, capacity: int = DEFAULT_CAPACITY,
                        on_result=None) -> list[tuple[torch.Tensor, torch.Tensor, torch.Tensor]]:
         """Search a sequence of query batches with two in flight, without a
-        host synchronisation: batch i's all-gather and merge run on a second
-        stream while batch i+1 is searched on the current one.  Returns
+        host synchronisation: batch i's exact rescoring, all-gather and merge
+        run on a second stream while batch i+1 is screened on the current one.  Returns
         ``(ids, scores, status [W])`` per batch, ready on the current stream.
         ``on_result(i, ids, scores)``, if given, is called on the exchange
         stream right after batch i is merged (e.g. to queue its copy to the
@@ -237,7 +247,13 @@ class ShardedDonorMatrix:
                 q = st["q"][slot]
             else:
                 q = q.to(device=dev, dtype=torch.float32).contiguous()
-            self._shard_search(q, st["send"][slot], kk, min_similarity, capacity)
+            if self.overlap_rescore:
+                # screening on the current stream, rescoring on the exchange stream in front of
+                # the all-gather, so batch i+1's screening starts as soon as batch i's ends
+                self._shard_search(q, st["send"][slot], kk, min_similarity, capacity, rescore_stream=xs,
+                                   workspace_owner=st["ws"][slot])
+            else:
+                self._shard_search(q, st["send"][slot], kk, min_similarity, capacity)
             if host:
                 consumed[slot].record(cur)
             ready[slot].record(cur)

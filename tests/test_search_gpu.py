@@ -497,3 +497,76 @@ def test_donor_store_reuse_on_device_matches_oracle():
     np.testing.assert_allclose([m.similarity for m in ms], [w[1] for w in want], atol=TOL)
     for m in ms:
         assert m.alignment.reuse_ratio >= 0.2
+
+
+def _split_search(m, Q, k, thr, rs, owner, out=None, n_rows=None, id_offset=0):
+    from semblend_b200.search import cosine_topk_async
+
+    return cosine_topk_async(m.emb, m.emb16, m.valid, m.stats, Q, k, thr, n_rows=n_rows, id_offset=id_offset,
+                             workspace_owner=owner, out=out, rescore_stream=rs)
+
+
+@pytest.mark.parametrize("k", [1, 8, 17, 32])
+def test_screen_then_rescore_on_another_stream_equals_one_call(k):
+    """sb_cosine_screen on the current stream + sb_cosine_rescore on a second
+    stream give the bits of one sb_cosine_topk call (ragged valid mask,
+    id offset, a row count below the matrix size)."""
+    from semblend_b200.search import cosine_topk_async
+
+    E, centers, rng = clustered(20011, 384, 32, seed=21)
+    valid = rng.random(E.shape[0]) > 0.1
+    m = build(E, valid)
+    Q = torch.from_numpy(queries_for(centers, rng, 333, 384)).to(DEV)
+    ids_f, s_f, st_f = cosine_topk_async(m.emb, m.emb16, m.valid, m.stats, Q, k, 0.55, n_rows=19000, id_offset=7)
+    rs = torch.cuda.Stream(DEV)
+
+    class Owner:
+        pass
+
+    ids_s, s_s, st_s = _split_search(m, Q, k, 0.55, rs, Owner(), n_rows=19000, id_offset=7)
+    torch.cuda.current_stream(DEV).wait_stream(rs)
+    assert int(st_f.item()) == 0 and int(st_s.item()) == 0
+    assert torch.equal(ids_s, ids_f) and torch.equal(s_s, s_f)
+    assert int(ids_s.max().item()) < 19000 + 7
+
+
+def test_split_search_with_no_rows_fills_empty():
+    m = DeviceDonorMatrix(64, 384, DEV)
+    rs = torch.cuda.Stream(DEV)
+    ids, sc, st = _split_search(m, torch.ones(5, 384, device=DEV), 4, 0.0, rs, None, n_rows=0)
+    torch.cuda.current_stream(DEV).wait_stream(rs)
+    assert torch.all(ids == -1) and torch.all(sc == -torch.inf) and int(st.item()) == 0
+
+
+def test_pipelined_split_search_with_two_workspaces():
+    """The sharded pipeline's pattern on one GPU: batch i is rescored on a
+    second stream while batch i+1 is screened, the two slots alternating their
+    workspaces and output buffers; every batch equals its own one-call search."""
+    from semblend_b200.search import cosine_topk_async
+
+    E, centers, rng = clustered(30000, 384, 32, seed=23)
+    m = build(E)
+    Qs = [torch.from_numpy(queries_for(centers, rng, 256, 384)).to(DEV) for _ in range(3)]
+    want = [cosine_topk_async(m.emb, m.emb16, m.valid, m.stats, q, 8, 0.6)[:2] for q in Qs]
+
+    class Owner:
+        pass
+
+    cur, rs = torch.cuda.current_stream(DEV), torch.cuda.Stream(DEV)
+    owners = [Owner(), Owner()]
+    outs = [(torch.empty(256, 8, dtype=torch.int64, device=DEV), torch.empty(256, 8, device=DEV)) for _ in range(2)]
+    done = [torch.cuda.Event() for _ in range(2)]
+    got = []
+    for i in range(7):
+        slot = i % 2
+        if i >= 2:
+            cur.wait_event(done[slot])
+        ids, sc, st = _split_search(m, Qs[i % 3], 8, 0.6, rs, owners[slot], out=outs[slot])
+        with torch.cuda.stream(rs):
+            got.append((ids.clone(), sc.clone(), st.clone()))
+            done[slot].record(rs)
+    cur.wait_stream(rs)
+    torch.cuda.synchronize(DEV)
+    for i, (ids, sc, st) in enumerate(got):
+        assert int(st.item()) == 0
+        assert torch.equal(ids, want[i % 3][0]) and torch.equal(sc, want[i % 3][1]), i
