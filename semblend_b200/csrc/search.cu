@@ -92,6 +92,22 @@ struct ScreenParams {
 constexpr int kSchedSlots = 64;
 __device__ unsigned g_screen_sched[kSchedSlots * 2];
 
+// Optional clock trace of CTA 0 (compiled out unless SB_SCREEN_TRACE): event
+// slot x index -> clock64().
+#ifndef SB_SCREEN_TRACE
+#define SB_SCREEN_TRACE 0
+#endif
+#if SB_SCREEN_TRACE
+constexpr int kTraceLen = 2048;
+__device__ long long g_screen_trace[12 * kTraceLen];
+#define SB_STRACE(slot, idx)                                                                        \
+  do {                                                                                              \
+    if (blockIdx.x == 0 && (idx) < kTraceLen) g_screen_trace[(slot) * kTraceLen + (idx)] = clock64(); \
+  } while (0)
+#else
+#define SB_STRACE(slot, idx) do { } while (0)
+#endif
+
 template <typename T> struct Half16;
 template <> struct Half16<__nv_bfloat16> {
   static __device__ __forceinline__ __nv_bfloat16 from(float x) { return __float2bfloat16_rn(x); }
@@ -238,6 +254,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = *tmem_holder;
   const tc::Abort ab{abort_flag, P.status};
   pdl_wait();  // query preparation (the previous kernel) has finished and is visible
+  if (threadIdx.x == 0) SB_STRACE(9, 0);
   // n-th unit of this CTA (-1: no more work).  A whole warp (epilogue) reads
   // the slot before lane 0 releases it; the single MMA thread releases it itself.
   auto pop_unit = [&](uint32_t n, bool whole_warp) -> int64_t {
@@ -274,6 +291,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int64_t t0 = (u / P.n_qtiles) * P.tiles_per_chunk;
         const int64_t t1 = min(t0 + P.tiles_per_chunk, P.n_ntiles);
         if (qi > 0 && !tc::mbar_wait(q_empty, (qi - 1) & 1, ab, 2, kWaitCycles)) break;
+        SB_STRACE(5, qi);
         tc::mbar_arrive_expect_tx(q_full, P.k_blocks * kQBlockBytes);
         for (int kb = 0; kb < P.k_blocks; ++kb)
           tc::tma_load_2d(sQ + kb * kQBlockBytes, &tmQ, q_full, kb * kBK, qt * kBM);
@@ -285,6 +303,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               ok = false;
               break;
             }
+            SB_STRACE(4, it);
             tc::mbar_arrive_expect_tx(&full[s], kEStageBytes);
             tc::tma_load_2d(sE + s * kEStageBytes, &tmE, &full[s], kb * kBK, (int)(t * kBN));
             ++it;
@@ -319,6 +338,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int64_t t0 = (u / P.n_qtiles) * P.tiles_per_chunk;
         const int64_t t1 = min(t0 + P.tiles_per_chunk, P.n_ntiles);
         if (!tc::mbar_wait(q_full, qi & 1, ab, 3, kWaitCycles)) break;
+        SB_STRACE(3, qi);
         tc::fence_after_sync();
         for (int64_t t = t0; t < t1 && ok; ++t) {
           const uint32_t b = ai & 1;
@@ -326,6 +346,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             ok = false;
             break;
           }
+          SB_STRACE(2, ai);
           tc::fence_after_sync();
           const uint32_t d_tmem = tmem + b * kBN;
           for (int kb = 0; kb < P.k_blocks; ++kb) {
@@ -334,6 +355,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               ok = false;
               break;
             }
+            SB_STRACE(0, it);
             tc::fence_after_sync();
 #pragma unroll
             for (int kk = 0; kk < kBK / 16; ++kk) {
@@ -342,6 +364,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               tc::mma_bf16_ss(d_tmem, da, db, idesc, (kb | kk) != 0);
             }
             tc::mma_commit(&empty[s]);
+            SB_STRACE(1, it);
             ++it;
           }
           if (!ok) break;
@@ -396,6 +419,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           ok = false;
           break;
         }
+        if (warp == 2 && lane == 0) SB_STRACE(6, ai);
         tc::fence_after_sync();
         const uint32_t base = tmem + ((uint32_t)(quarter * 32) << 16) + b * kBN + half * (kBN / 2);
         const float tk_before = tk[KT - 1];
@@ -472,6 +496,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc::fence_before_sync();
         __syncwarp();
         if (lane == 0) tc::mbar_arrive(&acc_empty[b]);
+        if (warp == 2 && lane == 0) SB_STRACE(7, ai);
+        if (warp == 9 && lane == 0) SB_STRACE(8, ai);
         ++ai;
         if (active) {
           if (nc) {
@@ -901,6 +927,17 @@ int launch_screen(const CUtensorMap &tq, const CUtensorMap &te, const ScreenPara
 
 }  // namespace
 }  // namespace sb
+
+#if SB_SCREEN_TRACE
+extern "C" SB_API int sb_screen_trace_read(long long *dst) {
+  return cudaMemcpyFromSymbol(dst, sb::g_screen_trace, sizeof(sb::g_screen_trace)) == cudaSuccess ? 0 : -3;
+}
+extern "C" SB_API int sb_screen_trace_reset() {
+  void *p = nullptr;
+  if (cudaGetSymbolAddress(&p, sb::g_screen_trace) != cudaSuccess) return -3;
+  return cudaMemset(p, 0, sizeof(sb::g_screen_trace)) == cudaSuccess ? 0 : -3;
+}
+#endif
 
 extern "C" SB_API int sb_search_prepare_rows(const float *emb, int64_t ld_emb, void *emb16, int64_t ld_16,
                                              int32_t dim, int32_t dim_pad, int32_t shadow_dtype, const int64_t *rows,

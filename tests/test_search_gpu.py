@@ -570,3 +570,15 @@ def test_pipelined_split_search_with_two_workspaces():
     for i, (ids, sc, st) in enumerate(got):
         assert int(st.item()) == 0
         assert torch.equal(ids, want[i % 3][0]) and torch.equal(sc, want[i % 3][1]), i
+
+
+@pytest.mark.parametrize("dim,nq", [(64, 260), (100, 383), (384, 4096), (512, 257)])
+def test_large_batches_vs_oracle(dim, nq):
+    """Batches of several query tiles (each donor chunk shared by concurrent
+    CTAs, each starting at its own tile of the chunk), a partial last tile, and
+    d = 512 (the largest query tile in shared memory)."""
+    E, centers, rng = clustered(9000, dim, 16, seed=dim + nq)
+    Q = queries_for(centers, rng, nq, dim)
+    m = build(E)
+    ids, s = m.search(Q, 8, 0.5)
+    assert_topk_equivalent(E, np.ones(E.shape[0], bool), Q, 0.5, ids.cpu().numpy(), s.cpu().numpy(), 8)
