@@ -277,10 +277,11 @@ SB_API int sb_cosine_topk(const float *emb, int64_t ld_emb, const void *emb16, i
  * sb_cosine_screen runs query preparation and the tensor-core screening into
  * the workspace; sb_cosine_rescore then rescores the workspace's candidates
  * exactly and writes out_ids / out_scores.  Both take the arguments of
- * sb_cosine_topk that they use, with the same meaning; the rescore must see
- * the screen's writes to the workspace and to *status (same stream, or an
- * event between the two streams), and the workspace must not be reused
- * before the rescore has finished.  Screen then rescore equals one
+ * sb_cosine_topk that they use, with the same meaning, except that
+ * sb_cosine_screen zeroes *status itself (on its stream, before its kernels).
+ * The rescore must see the screen's writes to the workspace and to *status
+ * (same stream, or an event between the two streams), and the workspace must
+ * not be reused before the rescore has finished.  Screen then rescore equals one
  * sb_cosine_topk call with the same arguments.  (No reference counterpart:
  * the reference searches one query at a time.) */
 SB_API int sb_cosine_screen(const void *emb16, int64_t ld_16, int32_t shadow_dtype,

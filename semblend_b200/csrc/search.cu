@@ -1086,14 +1086,25 @@ extern "C" SB_API int sb_cosine_screen(const void *emb16, int64_t ld_16, int32_t
   int s = check_topk_args(dim, n_rows, dim, dim_pad, n_queries, k, capacity, nullptr, nullptr, status);
   if (s != SB_OK) return s;
   if (shadow_dtype != SB_DTYPE_F16 && shadow_dtype != SB_DTYPE_BF16) return SB_ERR_UNSUPPORTED;
-  if (n_queries == 0 || n_rows == 0) return SB_OK;
+  if (n_queries == 0) return SB_OK;
+  if (n_rows == 0) {
+    const cudaError_t e = cudaMemsetAsync(status, 0, sizeof(int32_t), reinterpret_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) set_last_cuda_error(e);
+    return e == cudaSuccess ? SB_OK : SB_ERR_CUDA;
+  }
   if (queries == nullptr || stats == nullptr || emb16 == nullptr) return SB_ERR_INVALID_ARGUMENT;
   if (ld_q < dim || ld_16 < dim_pad) return SB_ERR_INVALID_ARGUMENT;
   if ((reinterpret_cast<uintptr_t>(emb16) % 16) || ((ld_16 * 2) % 16)) return SB_ERR_INVALID_ARGUMENT;
   const Workspace w = carve(workspace, n_queries, dim, dim_pad, capacity, n_rows);
   if (workspace == nullptr || workspace_bytes < w.bytes) return SB_ERR_WORKSPACE_TOO_SMALL;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const cudaError_t e = cudaMemsetAsync(status, 0, sizeof(int32_t), st);
+  if (e != cudaSuccess) {
+    set_last_cuda_error(e);
+    return SB_ERR_CUDA;
+  }
   return cosine_screen(emb16, ld_16, shadow_dtype, valid, n_rows, dim, dim_pad, stats, queries, ld_q, n_queries, k,
-                       min_similarity, capacity, w, status, reinterpret_cast<cudaStream_t>(stream));
+                       min_similarity, capacity, w, status, st);
 }
 
 extern "C" SB_API int sb_cosine_rescore(const float *emb, int64_t ld_emb, int64_t n_rows, int32_t dim,

@@ -210,8 +210,8 @@ def cosine_topk_async(emb: torch.Tensor, emb16: torch.Tensor, valid: torch.Tenso
         ids, scores = out
     if status is None:
         status = torch.zeros(1, dtype=torch.int32, device=dev)
-    else:
-        status.zero_()
+    elif rescore_stream is None:
+        status.zero_()  # (sb_cosine_screen zeroes it itself)
     lib = _lib.load()
     cap = max(int(capacity), k)
     nbytes = lib.sb_cosine_topk_workspace_bytes(nq, n_rows, dim, dim_pad, cap)
