@@ -170,4 +170,3 @@ def test_row_tile_pair_boundaries(count):
     mask[0, torch.randperm(S, generator=g)[:count]] = True
     out = tk.partial_prefill_attention(q.to(DEV), k.to(DEV), v.to(DEV), mask.to(DEV))
     _check_rows(out, q, k, v, mask, atol=2e-2)
-
