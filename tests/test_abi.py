@@ -93,3 +93,36 @@ def test_inject_params_flags_field():
 
     assert _lib.SbInjectParams.flags.offset == 28 and ctypes.sizeof(_lib.SbInjectParams) == 48
     assert _lib.SB_INJECT_BULK_STAGED == 1
+
+
+def test_search_entry_points_reject_bad_arguments_without_gpu():
+    """sb_cosine_topk, its two phases and sb_topk_merge check their arguments
+    before touching the device: rejected calls (and empty query batches) return
+    without a CUDA call, so this runs without a GPU."""
+    lib = _lib.load()
+    p = ctypes.c_void_p(16)  # never dereferenced: every call below returns before launching
+
+    def topk(nq=4, k=8, dim=384, dim_pad=384, cap=64, n_rows=1000, shadow=_lib.SB_DTYPE_F16, status=p):
+        return lib.sb_cosine_topk(p, dim, p, dim_pad, shadow, None, n_rows, dim, dim_pad, p, p, dim, nq, k, 0.5, 0,
+                                  p, p, cap, p, 1 << 20, status, None)
+
+    def screen(nq=4, k=8, dim=384, dim_pad=384, cap=64, n_rows=1000, shadow=_lib.SB_DTYPE_F16, status=p):
+        return lib.sb_cosine_screen(p, dim_pad, shadow, None, n_rows, dim, dim_pad, p, p, dim, nq, k, 0.5, cap, p,
+                                    1 << 20, status, None)
+
+    def rescore(nq=4, k=8, dim=384, dim_pad=384, cap=64, n_rows=1000, ids=p, scores=p, status=p):
+        return lib.sb_cosine_rescore(p, dim, n_rows, dim, dim_pad, nq, k, 0.5, 0, ids, scores, cap, p, 1 << 20,
+                                     status, None)
+
+    inv, uns, big = _lib.SB_ERR_INVALID_ARGUMENT, _lib.SB_ERR_UNSUPPORTED, _lib.SB_ERR_TOO_LARGE
+    for fn in (topk, screen, rescore):
+        assert fn(k=0) == inv and fn(k=33) == inv
+        assert fn(cap=4) == inv and fn(cap=16385) == inv  # capacity below k, above the maximum
+        assert fn(dim_pad=400) == uns and fn(dim_pad=576) == uns  # not a multiple of 64, above 512
+        assert fn(n_rows=1 << 31) == big
+        assert fn(status=None) == inv
+        assert fn(nq=0) == _lib.SB_OK  # nothing to do
+    assert topk(shadow=_lib.SB_DTYPE_F32) == uns and screen(shadow=_lib.SB_DTYPE_F32) == uns
+    assert rescore(ids=None) == inv  # one output without the other
+    assert lib.sb_topk_merge(p, 32, p, 32, 17, 4, 8, p, p, None) == inv  # more than 16 lists
+    assert lib.sb_topk_merge(p, 31, p, 32, 2, 4, 8, p, p, None) == inv  # list stride below Q * k
